@@ -1,0 +1,123 @@
+/*
+ * libswattn_b200 -- C ABI of the B200 (sm_100a) Switch Attention GQA prefill path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t; NULL = legacy default stream), enqueues its
+ * work on that stream and returns 0 on success or a negative SWA_E* code.  No
+ * entry point allocates memory or synchronises the stream.  On error,
+ * swa_last_error_string() describes the failure (thread-local).
+ *
+ * Layouts (all row-major, contiguous):
+ *   q    bf16 [B, Sq, Hq, 128]        k, v  bf16 [B, Skv, Hkv, 128]
+ *   out  bf16 [B, Sq, Hq, 128]        lse   fp32 [B, Sq, Hq]  (log2 domain)
+ *   index lists int32 [B, stride]: routed positions, strictly increasing.
+ *
+ * Reference interfaces replaced (YushengZhao/SwitchAttentionKernels):
+ *   swa_compact_mask      <- build_switch_query_indices   swiattn_gqa_prefill_varlen.py:306-322
+ *   swa_prepare_indices   <- _prepare_indices             swiattn_gqa_prefill_varlen.py:271-304
+ *   swa_check_cover       <- coverage check               swiattn_gqa_prefill_varlen.py:390-393
+ *   swa_build_metadata    <- build_switch_attention_metadata (imported at
+ *                            swiattn_gqa_prefill_varlen.py:27, used at :353-359)
+ *   swa_prefill_forward   <- both _switch_gqa_prefill_branch launches of
+ *                            switch_gqa_prefill_forward     swiattn_gqa_prefill_varlen.py:395-446
+ *                            (kernels swiattn_gqa_prefill.py:8-214,
+ *                             swiattn_gqa_prefill_varlen.py:33-249)
+ */
+#ifndef SWATTN_B200_H_
+#define SWATTN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SWA_OK 0
+#define SWA_E_INVALID (-1)     /* bad argument (shape, pointer, alignment)      */
+#define SWA_E_CUDA (-2)        /* a CUDA runtime call failed                    */
+#define SWA_E_UNSUPPORTED (-3) /* e.g. head_dim != 128, not an sm_100 device    */
+#define SWA_E_TMA (-4)         /* tensor-map encoding failed                    */
+
+/* Status-word bits written by the validation kernels and the prefill kernel. */
+#define SWA_STATUS_FULL_RANGE (1 << 0)
+#define SWA_STATUS_FULL_ORDER (1 << 1)
+#define SWA_STATUS_LOCAL_RANGE (1 << 2)
+#define SWA_STATUS_LOCAL_ORDER (1 << 3)
+#define SWA_STATUS_FULL_PAD (1 << 4)
+#define SWA_STATUS_LOCAL_PAD (1 << 5)
+#define SWA_STATUS_COVER (1 << 6)
+#define SWA_STATUS_TIMEOUT (1 << 16)
+
+/* ABI version of this header (1). */
+int swa_abi_version(void);
+
+/* Description of the last error on the calling thread ("" if none). */
+const char* swa_last_error_string(void);
+
+/* Number of SMs of `device` (the persistent grid size), or a negative code. */
+int swa_num_sms(int device);
+
+/* Compact a routing mask (uint8/bool [B, S], non-zero = full attention) into
+ * the increasing full / local position lists full[B, S], local[B, S]; entries
+ * past each row's count are -1.  counts[2*b] = n_full, counts[2*b+1] = n_local.
+ * Replaces build_switch_query_indices (swiattn_gqa_prefill_varlen.py:306-322),
+ * which handles B = 1 only. */
+int swa_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local, int32_t* counts,
+                     void* stream);
+
+/* Capacity-bucket preparation and validation of one index list per batch row
+ * (replaces _prepare_indices, swiattn_gqa_prefill_varlen.py:271-304).
+ *   idx [B, N]; trailing_pad = 0: all N entries are routed rows (the reference
+ *   form, count = N); trailing_pad = 1: -1 entries are trailing padding.
+ *   padded [B, cap] (nullable) receives the list with -1 fill; count [B].
+ *   Violations OR range_bit / order_bit / pad_bit into *status. */
+int swa_prepare_indices(const int32_t* idx, int B, int N, int seq_len, int trailing_pad, int cap,
+                        int32_t* padded, int32_t* count, int32_t* status, int range_bit, int order_bit,
+                        int pad_bit, void* stream);
+
+/* counts [2, B] (full row then local row): ORs SWA_STATUS_COVER into *status
+ * when count_full[b] + count_local[b] != seq_len for some b
+ * (swiattn_gqa_prefill_varlen.py:390-393). */
+int swa_check_cover(const int32_t* counts, int B, int seq_len, int32_t* status, void* stream);
+
+/* Per-row key bounds for packed varlen prefill.  cu_seqlens int32 [nseg + 1]
+ * (nullable: one sequence).  Writes the seven SwitchAttentionMetadata vectors
+ * of lengths (q_len, kv_len, q_len, kv_len, q_len, q_len, q_len). */
+int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_len, int window,
+                       int32_t* q_positions, int32_t* kv_positions, int32_t* q_segment_ids,
+                       int32_t* kv_segment_ids, int32_t* full_starts, int32_t* local_starts,
+                       int32_t* causal_ends, void* stream);
+
+/* Both Switch Attention branches of causal GQA prefill in one persistent launch.
+ *   full_idx / local_idx : int32 [B, *_stride]; row b holds the first counts
+ *                          of routed positions (B == 1 with counts == NULL:
+ *                          count_full / count_local are used).
+ *   full_cap / local_cap : number of readable slots per row (<= stride).
+ *   counts               : int32 [2, B] device counts (nullable when B == 1).
+ *   full_starts, local_starts, causal_ends : int32 [Sq] varlen bounds
+ *                          (all NULL: fixed-length masks key <= t and
+ *                          t - window + 1 <= key <= t).
+ *   bg_list / n_bg       : (b * Hkv + g) work units to compute (NULL: all B*Hkv),
+ *                          used by the multi-GPU driver to shard units.
+ *   gate                 : nullable device int32; non-zero makes the launch a no-op
+ *                          (set by the validation kernels).
+ *   workspace            : >= 16 bytes of device memory; workspace[0] is the work
+ *                          counter (zeroed by this call on `stream`),
+ *                          workspace[1] receives SWA_STATUS_TIMEOUT on a device-side
+ *                          wait timeout.  Launches that overlap on the GPU need
+ *                          distinct workspaces.
+ * Requires head_dim == 128, Hq % Hkv == 0, window > 0, 16-byte aligned q/k/v. */
+int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                        const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                        const int32_t* counts, int count_full, int count_local, const int32_t* full_starts,
+                        const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
+                        void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
+                        float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWATTN_B200_H_ */

@@ -1,0 +1,193 @@
+"""Switch Attention GQA prefill, restated on the CPU in FP32 torch (test oracle only).
+
+Reference semantics (YushengZhao/SwitchAttentionKernels):
+
+* scale: ``scale_log2 = (sm_scale or 1/sqrt(D)) * log2(e)``
+  (``swiattn_gqa_prefill.py:43-46``, ``swiattn_gqa_prefill_varlen.py:73-76``);
+* GQA head map: query head ``h`` reads KV head ``h // (Hq / Hkv)``
+  (``swiattn_gqa_prefill.py:88``, ``swiattn_gqa_prefill_varlen.py:124``);
+* legality of key ``j`` for a row at position ``t`` (``swiattn_gqa_prefill.py:145-158``):
+  full ``0 <= j <= t``, local ``max(t - W + 1, 0) <= j <= t``, and ``j < Skv``;
+  with metadata (``swiattn_gqa_prefill_varlen.py:134-137,186-196``):
+  ``start[t] <= j < causal_ends[t]`` and ``j < Skv`` where ``start`` is
+  ``full_starts`` or ``local_starts``;
+* output: ``O = softmax_2(scale_log2 * q k^T) v`` and the log2-domain
+  ``LSE = log2(sum_j 2^(scale_log2 * s_j))`` (``swiattn_gqa_prefill_varlen.py:207-241``);
+  a row with no legal key yields ``O = 0/0`` (NaN) and ``LSE = -inf`` exactly as the
+  kernel's ``acc_o / row_sum`` and ``log2(row_sum)`` do;
+* rows are written at their original positions (``:243-249``).
+
+``prefill_dense`` computes the exact FP32 result (the accuracy reference).
+``prefill_tiled`` replays the kernel loop tile by tile -- union key range of a
+query tile (``swiattn_gqa_prefill.py:95-105``, varlen ``:142-154``), running max
+initialised to ``-2**30`` (``:132``), ``exp2`` rescaling, P rounded to BF16 before
+``P @ V`` (``:187``, varlen ``:225``), final division and log2 (``:201-206``) -- to
+show how far the reference's own rounding sits from the exact result.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+LOG2E = 1.4426950408889634
+
+
+def scale_log2_of(sm_scale, dim: int) -> float:
+    return (sm_scale if sm_scale is not None else (1.0 / dim) ** 0.5) * LOG2E
+
+
+def row_bounds(pos: np.ndarray, is_local: bool, window: int, skv: int, metadata=None) -> tuple[np.ndarray, np.ndarray]:
+    """Half-open legal key range ``[lo, hi)`` of each row (before clipping to ``[0, Skv)``)."""
+    pos = np.asarray(pos, dtype=np.int64)
+    if metadata is None:
+        hi = pos + 1
+        lo = np.maximum(pos - window + 1, 0) if is_local else np.zeros_like(pos)
+    else:
+        starts = np.asarray(metadata["local_starts" if is_local else "full_starts"], dtype=np.int64)
+        ends = np.asarray(metadata["causal_ends"], dtype=np.int64)
+        lo = starts[pos]
+        hi = ends[pos]
+    lo = np.maximum(lo, 0)
+    hi = np.minimum(hi, skv)
+    return lo, hi
+
+
+def legal_key_counts(full_lists, local_lists, *, window: int, skv: int, metadata=None) -> int:
+    """Total number of legal (row, key) pairs for one query head, summed over batches."""
+    total = 0
+    for fl, ll in zip(full_lists, local_lists):
+        for is_local, lst in ((False, fl), (True, ll)):
+            lo, hi = row_bounds(lst, is_local, window, skv, metadata)
+            total += int(np.maximum(hi - lo, 0).sum())
+    return total
+
+
+def prefill_dense(q, k, v, full_lists, local_lists, *, window: int, sm_scale=None, metadata=None,
+                  subset=None, budget_bytes: int = 1 << 28):
+    """Exact FP32 result.  ``q``: ``[B,Sq,Hq,D]``, ``k``/``v``: ``[B,Skv,Hkv,D]`` (any float dtype, CPU).
+
+    ``full_lists`` / ``local_lists``: per batch, 1-D int arrays of positions.
+    ``subset``: optional per batch array of positions to compute (others stay NaN).
+    Returns ``(O, LSE)`` as FP32 tensors ``[B,Sq,Hq,D]`` / ``[B,Sq,Hq]``.
+    """
+    B, Sq, Hq, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    r = Hq // Hkv
+    sl2 = scale_log2_of(sm_scale, D)
+    O = torch.full((B, Sq, Hq, D), float("nan"), dtype=torch.float32)
+    LSE = torch.full((B, Sq, Hq), float("nan"), dtype=torch.float32)
+    for b in range(B):
+        for is_local, lst in ((False, full_lists[b]), (True, local_lists[b])):
+            pos = np.asarray(lst, dtype=np.int64)
+            if subset is not None:
+                pos = pos[np.isin(pos, np.asarray(subset[b]))]
+            if pos.size == 0:
+                continue
+            lo, hi = row_bounds(pos, is_local, window, Skv, metadata)
+            c = 0
+            while c < pos.size:
+                # rows per chunk bounded by the score-matrix budget
+                span_guess = int(hi[min(c + 63, pos.size - 1)] - lo[c]) + 1
+                n = max(1, min(64, budget_bytes // max(1, 4 * Hq * max(span_guess, 1))))
+                p = pos[c:c + n]
+                l, h = lo[c:c + n], hi[c:c + n]
+                c += n
+                L0, L1 = int(l.min()), int(h.max())
+                qc = q[b, torch.from_numpy(p)].float().view(len(p), Hkv, r, D)
+                if L1 <= L0:
+                    O[b, torch.from_numpy(p)] = float("nan")
+                    LSE[b, torch.from_numpy(p)] = float("-inf")
+                    continue
+                kc = k[b, L0:L1].float()
+                vc = v[b, L0:L1].float()
+                s = torch.einsum("ngrd,lgd->ngrl", qc, kc) * sl2
+                keys = torch.arange(L0, L1)
+                legal = (keys[None, :] >= torch.from_numpy(l)[:, None]) & (keys[None, :] < torch.from_numpy(h)[:, None])
+                s = s.masked_fill(~legal[:, None, None, :], float("-inf"))
+                m = s.amax(dim=-1, keepdim=True)
+                m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+                pe = torch.exp2(s - m_safe)
+                den = pe.sum(dim=-1, keepdim=True)
+                num = torch.einsum("ngrl,lgd->ngrd", pe, vc)
+                o = num / den
+                lse = (m_safe + torch.log2(den)).squeeze(-1)
+                O[b, torch.from_numpy(p)] = o.reshape(len(p), Hq, D)
+                LSE[b, torch.from_numpy(p)] = lse.reshape(len(p), Hq)
+    return O, LSE
+
+
+def prefill_tiled(q, k, v, full_list, local_list, *, window: int, sm_scale=None, metadata=None,
+                  block_m: int = 64, block_k: int = 64):
+    """Tile-by-tile replay of the reference branch kernel for ``B = 1`` (small cases only).
+
+    Follows ``swiattn_gqa_prefill.py:86-214`` (fixed) and, when ``metadata`` is
+    given, ``swiattn_gqa_prefill_varlen.py:122-249``; all query heads of a tile are
+    processed together (the kernel's grid z axis).
+    """
+    B, Sq, Hq, D = q.shape
+    assert B == 1
+    Skv, Hkv = k.shape[1], k.shape[2]
+    r = Hq // Hkv
+    sl2 = scale_log2_of(sm_scale, D)
+    O = torch.full((Sq, Hq, D), float("nan"), dtype=torch.float32)
+    LSE = torch.full((Sq, Hq), float("nan"), dtype=torch.float32)
+    kv_head = torch.arange(Hq) // r
+    for is_local, lst in ((False, full_list), (True, local_list)):
+        idx = np.asarray(lst, dtype=np.int64)
+        count = idx.size
+        if count == 0:
+            continue
+        cap = -(-count // block_m) * block_m
+        for q0 in range(0, cap, block_m):
+            slots = np.arange(q0, q0 + block_m)
+            valid = slots < count
+            qpos = np.where(valid, idx[np.minimum(slots, count - 1)], 0)
+            first_slot = min(q0, max(count - 1, 0))
+            last_slot = min(q0 + block_m - 1, max(count - 1, 0))
+            first_q = max(int(idx[first_slot]), 0)
+            last_q = max(int(idx[last_slot]), 0)
+            if metadata is None:
+                first_key = max(first_q - window + 1, 0) if is_local else 0
+                last_key = min(last_q + 1, Skv)
+                lo = np.maximum(qpos - window + 1, 0) if is_local else np.zeros_like(qpos)
+                hi = qpos + 1
+            else:
+                starts = np.asarray(metadata["local_starts" if is_local else "full_starts"], dtype=np.int64)
+                ends = np.asarray(metadata["causal_ends"], dtype=np.int64)
+                first_key = int(starts[first_q]) if q0 < count else Skv
+                last_key = min(int(ends[last_q]), Skv) if q0 < count else 0
+                lo, hi = starts[qpos], ends[qpos]
+            first_block = first_key // block_k
+            last_block = -(-last_key // block_k)
+            nblocks = max(last_block - first_block, 0)
+            qt = q[0, torch.from_numpy(np.clip(qpos, 0, Sq - 1))].float()            # [BM, Hq, D]
+            acc_o = torch.zeros(block_m, Hq, D)
+            row_sum = torch.zeros(block_m, Hq)
+            row_max = torch.full((block_m, Hq), -(2.0 ** 30))
+            lo_t = torch.from_numpy(lo)[:, None]
+            hi_t = torch.from_numpy(hi)[:, None]
+            valid_t = torch.from_numpy(valid)[:, None]
+            for jb in range(nblocks):
+                key0 = (first_block + jb) * block_k
+                keys = torch.arange(key0, key0 + block_k)
+                safe = keys.clamp(0, Skv - 1)
+                kt = k[0, safe].float()[:, kv_head]                                    # [BK, Hq, D]
+                vt = v[0, safe].float()[:, kv_head]
+                legal = valid_t & (keys[None, :] < Skv) & (keys[None, :] >= lo_t) & (keys[None, :] < hi_t)
+                acc_s = torch.einsum("mhd,nhd->mhn", qt, kt)
+                acc_s = torch.where(legal[:, None, :], acc_s, torch.tensor(float("-inf")))
+                prev = row_max
+                row_max = torch.maximum(prev, acc_s.amax(dim=-1))
+                alpha = torch.exp2((prev - row_max) * sl2)
+                pe = torch.exp2(acc_s * sl2 - (row_max * sl2)[..., None])
+                row_sum = row_sum * alpha + pe.sum(dim=-1)
+                acc_o = acc_o * alpha[..., None]
+                acc_o = acc_o + torch.einsum("mhn,nhd->mhd", pe.to(torch.bfloat16).float(), vt)
+            out = acc_o / row_sum[..., None]
+            lse = torch.log2(row_sum) + row_max * sl2
+            sel = torch.from_numpy(qpos[valid])
+            O[sel] = out[torch.from_numpy(valid)]
+            LSE[sel] = lse[torch.from_numpy(valid)]
+    return O[None], LSE[None]

@@ -1,0 +1,24 @@
+"""B200-native (sm_100a) Switch Attention GQA prefill.
+
+Public API (drop-in for YushengZhao/SwitchAttentionKernels):
+
+* ``build_switch_query_indices(full_mask)``
+* ``switch_gqa_prefill_forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, ...)``
+* ``SwitchAttentionMetadata``, ``build_switch_attention_metadata``
+
+Extensions: ``build_switch_query_indices_batched`` (B > 1 routing masks) and
+``sharded_switch_gqa_prefill_forward`` (one process per GPU, (batch, KV group)
+units sharded across ranks, optional NCCL all-gather of O/LSE).
+"""
+from ._core import build_switch_query_indices_batched
+from .metadata import SwitchAttentionMetadata, build_switch_attention_metadata, cu_seqlens_from_lengths
+from .swiattn_gqa_prefill_varlen import build_switch_query_indices, switch_gqa_prefill_forward
+
+__all__ = [
+    "SwitchAttentionMetadata",
+    "build_switch_attention_metadata",
+    "build_switch_query_indices",
+    "build_switch_query_indices_batched",
+    "cu_seqlens_from_lengths",
+    "switch_gqa_prefill_forward",
+]

@@ -1,0 +1,283 @@
+"""Host side of the Switch Attention prefill path: validation, index lists,
+capacity buckets and the launch of the sm_100a kernels through the C ABI.
+
+Error types and messages are the reference's
+(``swiattn_gqa_prefill_varlen.py:251-304,313-320,345-393``).  Deliberate
+supersets of the reference's accepted inputs:
+
+* any ``Hq % Hkv == 0`` (the reference wrapper only accepts Hq=32, Hkv=8,
+  ``:266-267``, although its kernels support any group size);
+* ``B >= 1`` (the reference wrapper only accepts B=1, ``:346-347``; its
+  fixed-length kernel already takes ``QueryIndices[batch, cap]``,
+  ``swiattn_gqa_prefill.py:64-65``).  For ``B > 1`` the index lists are
+  ``[B, N]`` int32 tensors whose rows end in ``-1`` padding, as produced by
+  ``build_switch_query_indices_batched``.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from . import _native
+from .metadata import SwitchAttentionMetadata
+
+LOG2E = 1.4426950408889634
+
+ERR_RANGE = "query index is outside [0, sequence_length)"
+ERR_ORDER = "query indices must be strictly increasing"
+ERR_COVER = "full and local query lists must cover the sequence"
+ERR_PAD = "query index padding (-1) must be trailing"
+ERR_META = "invalid Switch Attention position metadata"
+
+# When set (environment variable SWA_CHECK_STATUS=1), every forward call reads
+# back the kernel's status word and raises if a device-side wait timed out.
+CHECK_DEVICE_STATUS = os.environ.get("SWA_CHECK_STATUS", "0") == "1"
+
+
+# --------------------------------------------------------------------------- validation
+def validate_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """``_validate_qkv`` (reference ``swiattn_gqa_prefill_varlen.py:251-269``) minus the Hq=32/Hkv=8 pin."""
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise TypeError("Switch Attention prefill requires BF16 Q/K/V")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("Q/K/V must be tensors on a supported accelerator device")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("Q/K/V must be contiguous")
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("Q/K/V must use [B,S,H,D] layout")
+    if k.shape != v.shape:
+        raise ValueError("K and V must have identical shapes")
+    if q.shape[0] != k.shape[0]:
+        raise ValueError("Q and KV batch sizes must match")
+    if q.shape[3] != 128 or k.shape[3] != 128:
+        raise ValueError("the first kernel is specialized for head_dim=128")
+    if q.shape[2] % k.shape[2]:
+        raise ValueError("query heads must be divisible by KV heads")
+    if not (q.device == k.device == v.device):
+        raise ValueError("Q/K/V must be on the same device")
+
+
+def bucket_capacity(count: int, block_m: int) -> int:
+    """Capacity bucket (reference ``swiattn_gqa_prefill_varlen.py:287-292``)."""
+    if count == 0:
+        return 0
+    padded = block_m << max(0, math.ceil(count / block_m).bit_length() - 1)
+    if padded < count:
+        padded <<= 1
+    return padded
+
+
+def _raise_status(status: int) -> None:
+    order = [
+        (_native.STATUS_FULL_RANGE, ERR_RANGE),
+        (_native.STATUS_FULL_PAD, ERR_PAD),
+        (_native.STATUS_FULL_ORDER, ERR_ORDER),
+        (_native.STATUS_LOCAL_RANGE, ERR_RANGE),
+        (_native.STATUS_LOCAL_PAD, ERR_PAD),
+        (_native.STATUS_LOCAL_ORDER, ERR_ORDER),
+        (_native.STATUS_COVER, ERR_COVER),
+    ]
+    for bit, msg in order:
+        if status & bit:
+            raise ValueError(msg)
+    if status & _native.STATUS_TIMEOUT:
+        raise RuntimeError("Switch Attention kernel: a device-side wait timed out")
+
+
+# --------------------------------------------------------------------------- index lists
+def build_switch_query_indices(full_mask: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Compact a B=1 hard route mask into sorted full and local query positions.
+
+    Same contract as the reference (``swiattn_gqa_prefill_varlen.py:306-322``):
+    ``True`` routes a position to full causal attention, ``False`` to the sliding
+    window; both outputs are int32 and strictly increasing.  Computed by one
+    ballot/scan CUDA kernel; one device-to-host read sizes the outputs (the
+    reference's ``positions[mask]`` performs the same synchronisation).
+    """
+    if full_mask.ndim == 2:
+        if full_mask.shape[0] != 1:
+            raise ValueError("the first kernel supports B=1 routing")
+        full_mask = full_mask[0]
+    if full_mask.ndim != 1 or full_mask.dtype != torch.bool or not full_mask.is_cuda:
+        raise TypeError("full_mask must be a device-resident bool tensor with shape [S] or [1,S]")
+    full, local, counts = build_switch_query_indices_batched(full_mask.unsqueeze(0))
+    n_full, n_local = (int(x) for x in counts[0].tolist())
+    return full[0, :n_full], local[0, :n_local]
+
+
+def build_switch_query_indices_batched(full_mask: torch.Tensor):
+    """``[B, S]`` bool mask -> ``(full [B,S], local [B,S], counts [B,2])`` on the device, no host sync.
+
+    Row ``b`` of ``full`` / ``local`` holds the routed positions in increasing
+    order followed by ``-1``; ``counts[b] = (n_full, n_local)``.
+    """
+    if full_mask.ndim != 2 or full_mask.dtype != torch.bool or not full_mask.is_cuda:
+        raise TypeError("full_mask must be a device-resident bool tensor with shape [B,S]")
+    mask = full_mask.contiguous()
+    B, S = mask.shape
+    dev = mask.device
+    full = torch.empty((B, S), dtype=torch.int32, device=dev)
+    local = torch.empty((B, S), dtype=torch.int32, device=dev)
+    counts = torch.zeros((B, 2), dtype=torch.int32, device=dev)
+    if B == 0 or S == 0:
+        return full, local, counts
+    lib = _native.load()
+    with torch.cuda.device(dev):
+        rc = lib.swa_compact_mask(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
+                                  _native.ptr(counts), _native.stream_ptr(dev))
+    _native.check(rc, "build_switch_query_indices")
+    return full, local, counts
+
+
+def prepare_indices(indices: torch.Tensor, *, seq_len: int, block_m: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """``_prepare_indices`` (reference ``swiattn_gqa_prefill_varlen.py:271-304``).
+
+    Returns ``(padded [1, cap], count [1])`` with ``cap`` the power-of-two
+    capacity bucket and ``-1`` fill; raises the reference's ``ValueError`` for an
+    out-of-range or non-increasing list (one device-to-host read, as in the
+    reference).
+    """
+    if indices.ndim == 1:
+        indices = indices.unsqueeze(0)
+    if indices.ndim != 2 or indices.shape[0] != 1:
+        raise ValueError("the first kernel accepts one batch of query indices")
+    if indices.device.type != "cuda":
+        raise ValueError("query indices must be on a supported accelerator device")
+    indices = indices.to(dtype=torch.int32).contiguous()
+    count = int(indices.shape[1])
+    dev = indices.device
+    if count == 0:
+        return indices, torch.zeros((1,), dtype=torch.int32, device=dev)
+    cap = bucket_capacity(count, block_m)
+    padded = torch.empty((1, cap), dtype=torch.int32, device=dev)
+    count_t = torch.empty((1,), dtype=torch.int32, device=dev)
+    status = torch.zeros((1,), dtype=torch.int32, device=dev)
+    lib = _native.load()
+    with torch.cuda.device(dev):
+        rc = lib.swa_prepare_indices(_native.ptr(indices), 1, count, int(seq_len), 0, cap, _native.ptr(padded),
+                                     _native.ptr(count_t), _native.ptr(status), _native.STATUS_FULL_RANGE,
+                                     _native.STATUS_FULL_ORDER, 0, _native.stream_ptr(dev))
+    _native.check(rc, "_prepare_indices")
+    st = int(status.item())
+    if st & _native.STATUS_FULL_RANGE:
+        raise ValueError(ERR_RANGE)
+    if st & _native.STATUS_FULL_ORDER:
+        raise ValueError(ERR_ORDER)
+    return padded, count_t
+
+
+# --------------------------------------------------------------------------- forward
+def _check_metadata(metadata: SwitchAttentionMetadata, q: torch.Tensor, q_len: int, kv_len: int) -> None:
+    """Metadata validation of the reference wrapper (``swiattn_gqa_prefill_varlen.py:360-383``)."""
+    tensors = (metadata.q_positions, metadata.kv_positions, metadata.q_segment_ids, metadata.kv_segment_ids,
+               metadata.full_starts, metadata.local_starts, metadata.causal_ends)
+    expected = (q_len, kv_len, q_len, kv_len, q_len, q_len, q_len)
+    for t, n in zip(tensors, expected):
+        if (t.device != q.device or t.dtype != torch.int32 or t.ndim != 1 or t.numel() != n
+                or not t.is_contiguous()):
+            raise ValueError(ERR_META)
+
+
+def _index_rows(indices: torch.Tensor, B: int, device: torch.device, name: str) -> torch.Tensor:
+    if not isinstance(indices, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if indices.device.type != "cuda":
+        raise ValueError("query indices must be on a supported accelerator device")
+    if indices.device != device:
+        raise ValueError("query indices must be on the same device as Q")
+    if B == 1:
+        if indices.ndim == 1:
+            indices = indices.unsqueeze(0)
+        if indices.ndim != 2 or indices.shape[0] != 1:
+            raise ValueError("the first kernel accepts one batch of query indices")
+    elif indices.ndim != 2 or indices.shape[0] != B:
+        raise ValueError(f"{name} must have shape [B, N] (rows padded with -1) when B > 1")
+    return indices.to(dtype=torch.int32).contiguous()
+
+
+def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, window_size=1024, sm_scale=None,
+            validate=True, bg_list=None, out=None, lse=None):
+    """Both branches of Switch Attention GQA prefill (see ``switch_gqa_prefill_forward``).
+
+    ``bg_list`` (int32 device tensor of ``b * Hkv + g``) restricts the launch to
+    those (batch, KV group) units; ``out`` / ``lse`` may be given to write into
+    existing buffers (rows outside the computed units are left untouched).
+    """
+    validate_qkv(q, k, v)
+    if window_size <= 0:
+        raise ValueError("window_size must be positive")
+    B, q_len, Hq, D = q.shape
+    kv_len, Hkv = k.shape[1], k.shape[2]
+    dev = q.device
+    if metadata is not None:
+        _check_metadata(metadata, q, q_len, kv_len)
+    full = _index_rows(full_query_indices, B, dev, "full_query_indices")
+    local = _index_rows(local_query_indices, B, dev, "local_query_indices")
+    scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * LOG2E
+    if not scale > 0:
+        raise ValueError("sm_scale must be positive")
+
+    lib = _native.load()
+    stream = _native.stream_ptr(dev)
+    n_full, n_local = int(full.shape[1]), int(local.shape[1])
+    ws = torch.zeros(4 + 2 * B, dtype=torch.int32, device=dev)
+    status = ws[2:3]
+    counts = ws[4:]
+    gate = None
+    with torch.cuda.device(dev):
+        if B == 1:
+            if validate:
+                for t, n, rb, ob in ((full, n_full, _native.STATUS_FULL_RANGE, _native.STATUS_FULL_ORDER),
+                                     (local, n_local, _native.STATUS_LOCAL_RANGE, _native.STATUS_LOCAL_ORDER)):
+                    if n:
+                        _native.check(lib.swa_prepare_indices(_native.ptr(t), 1, n, q_len, 0, 0, None,
+                                                              _native.ptr(counts), _native.ptr(status), rb, ob, 0,
+                                                              stream), "index validation")
+                st = int(status.item())
+                _raise_status(st)
+            if n_full + n_local != q_len:
+                raise ValueError(ERR_COVER)
+            counts_arg = None
+        else:
+            for t, n, row, rb, ob, pb in (
+                    (full, n_full, 0, _native.STATUS_FULL_RANGE, _native.STATUS_FULL_ORDER, _native.STATUS_FULL_PAD),
+                    (local, n_local, 1, _native.STATUS_LOCAL_RANGE, _native.STATUS_LOCAL_ORDER,
+                     _native.STATUS_LOCAL_PAD)):
+                _native.check(lib.swa_prepare_indices(_native.ptr(t) if n else None, B, n, q_len, 1, 0, None,
+                                                      _native.ptr(counts[row * B:(row + 1) * B]),
+                                                      _native.ptr(status), rb, ob, pb, stream), "index validation")
+            _native.check(lib.swa_check_cover(_native.ptr(counts), B, q_len, _native.ptr(status), stream),
+                          "coverage check")
+            if validate:
+                _raise_status(int(status.item()))
+            else:
+                gate = status
+            counts_arg = counts
+        if out is None:
+            out = torch.empty_like(q)
+        if lse is None:
+            lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+        if metadata is not None:
+            fs, ls, ce = metadata.full_starts, metadata.local_starts, metadata.causal_ends
+        else:
+            fs = ls = ce = None
+        n_bg = 0
+        if bg_list is not None:
+            bg_list = bg_list.to(device=dev, dtype=torch.int32).contiguous()
+            n_bg = int(bg_list.numel())
+        rc = lib.swa_prefill_forward(
+            _native.ptr(q), _native.ptr(k), _native.ptr(v),
+            _native.ptr(full) if n_full else None, _native.ptr(local) if n_local else None,
+            n_full, n_local, n_full, n_local,
+            _native.ptr(counts_arg), n_full, n_local,
+            _native.ptr(fs), _native.ptr(ls), _native.ptr(ce),
+            _native.ptr(bg_list), n_bg,
+            _native.ptr(out), _native.ptr(lse),
+            B, q_len, kv_len, Hq, Hkv, D, int(window_size), float(scale),
+            _native.ptr(gate), _native.ptr(ws), ws.numel() * 4, stream)
+        _native.check(rc, "switch_gqa_prefill_forward")
+        if CHECK_DEVICE_STATUS:
+            _raise_status(int(ws[1].item()))
+    return out, lse

@@ -1,0 +1,107 @@
+"""ctypes binding of libswattn_b200.so (C ABI: include/swattn_b200.h).
+
+The library is loaded on first use.  There is no fallback: when the shared
+object is missing or the device is not an sm_100 GPU the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libswattn_b200.so")
+
+SWA_OK = 0
+STATUS_FULL_RANGE = 1 << 0
+STATUS_FULL_ORDER = 1 << 1
+STATUS_LOCAL_RANGE = 1 << 2
+STATUS_LOCAL_ORDER = 1 << 3
+STATUS_FULL_PAD = 1 << 4
+STATUS_LOCAL_PAD = 1 << 5
+STATUS_COVER = 1 << 6
+STATUS_TIMEOUT = 1 << 16
+
+EXPORTED = (
+    "swa_abi_version",
+    "swa_last_error_string",
+    "swa_num_sms",
+    "swa_compact_mask",
+    "swa_prepare_indices",
+    "swa_check_cover",
+    "swa_build_metadata",
+    "swa_prefill_forward",
+)
+
+_lock = threading.Lock()
+_lib = None
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+_f = ctypes.c_float
+
+
+def _declare(lib) -> None:
+    lib.swa_abi_version.restype = _i
+    lib.swa_abi_version.argtypes = []
+    lib.swa_last_error_string.restype = ctypes.c_char_p
+    lib.swa_last_error_string.argtypes = []
+    lib.swa_num_sms.restype = _i
+    lib.swa_num_sms.argtypes = [_i]
+    lib.swa_compact_mask.restype = _i
+    lib.swa_compact_mask.argtypes = [_p, _i, _i, _p, _p, _p, _p]
+    lib.swa_prepare_indices.restype = _i
+    lib.swa_prepare_indices.argtypes = [_p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _i, _i, _p]
+    lib.swa_check_cover.restype = _i
+    lib.swa_check_cover.argtypes = [_p, _i, _i, _p, _p]
+    lib.swa_build_metadata.restype = _i
+    lib.swa_build_metadata.argtypes = [_p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p]
+    lib.swa_prefill_forward.restype = _i
+    lib.swa_prefill_forward.argtypes = [
+        _p, _p, _p,            # q, k, v
+        _p, _p,                # full_idx, local_idx
+        _i, _i, _i, _i,        # strides, caps
+        _p, _i, _i,            # counts, count_full, count_local
+        _p, _p, _p,            # full_starts, local_starts, causal_ends
+        _p, _i,                # bg_list, n_bg
+        _p, _p,                # out, lse
+        _i, _i, _i, _i, _i, _i,  # B, Sq, Skv, Hq, Hkv, head_dim
+        _i, _f,                # window, scale_log2
+        _p, _p, _sz,           # gate, workspace, workspace_bytes
+        _p,                    # stream
+    ]
+
+
+def load():
+    """Load (once) and return the native library; raise if it is not built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python -m switchattentionkernels_b200.build`")
+                lib = ctypes.CDLL(LIB_PATH)
+                _declare(lib)
+                if lib.swa_abi_version() != 1:
+                    raise RuntimeError("libswattn_b200 ABI version mismatch")
+                _lib = lib
+    return _lib
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def check(rc: int, what: str) -> None:
+    if rc != SWA_OK:
+        msg = load().swa_last_error_string().decode(errors="replace")
+        if rc == -1:
+            raise ValueError(f"{what}: {msg}")
+        raise RuntimeError(f"{what} failed ({rc}): {msg}")

@@ -1,0 +1,188 @@
+// C ABI of libswattn_b200 (declared in include/swattn_b200.h).
+#include <cstdio>
+#include <string>
+
+#include "../../include/swattn_b200.h"
+#include "swattn_internal.h"
+#include "tma_host.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SWA_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int swa_abi_version(void) { return 1; }
+
+const char* swa_last_error_string(void) { return g_last_error.c_str(); }
+
+int swa_num_sms(int device) {
+  int n = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  return n;
+}
+
+int swa_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local, int32_t* counts,
+                     void* stream) {
+  if (B < 0 || S < 0) return fail(SWA_E_INVALID, "negative shape");
+  if (B == 0) return SWA_OK;
+  if (mask == nullptr || full == nullptr || local == nullptr || counts == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  cudaError_t e = swa::launch_compact_mask(mask, B, S, full, local, counts, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "compact_mask launch");
+  return SWA_OK;
+}
+
+int swa_prepare_indices(const int32_t* idx, int B, int N, int seq_len, int trailing_pad, int cap,
+                        int32_t* padded, int32_t* count, int32_t* status, int range_bit, int order_bit,
+                        int pad_bit, void* stream) {
+  if (B < 0 || N < 0 || cap < 0) return fail(SWA_E_INVALID, "negative shape");
+  if (B == 0) return SWA_OK;
+  if ((N > 0 && idx == nullptr) || count == nullptr || status == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  if (padded != nullptr && cap < N) return fail(SWA_E_INVALID, "capacity below list length");
+  if (trailing_pad && pad_bit == 0) return fail(SWA_E_INVALID, "trailing padding needs a pad status bit");
+  cudaError_t e = swa::launch_prepare_indices(idx, B, N, seq_len, B, padded ? cap : 0, padded, count, status,
+                                              range_bit, order_bit, trailing_pad ? pad_bit : 0,
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prepare_indices launch");
+  return SWA_OK;
+}
+
+int swa_check_cover(const int32_t* counts, int B, int seq_len, int32_t* status, void* stream) {
+  if (B <= 0) return SWA_OK;
+  if (counts == nullptr || status == nullptr) return fail(SWA_E_INVALID, "null pointer");
+  cudaError_t e = swa::launch_check_cover(counts, B, seq_len, status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "check_cover launch");
+  return SWA_OK;
+}
+
+int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_len, int window,
+                       int32_t* q_positions, int32_t* kv_positions, int32_t* q_segment_ids,
+                       int32_t* kv_segment_ids, int32_t* full_starts, int32_t* local_starts,
+                       int32_t* causal_ends, void* stream) {
+  if (q_len < 0 || kv_len < 0 || window <= 0) return fail(SWA_E_INVALID, "bad metadata shape");
+  if (cu_seqlens != nullptr && (nseg <= 0 || kv_len != q_len))
+    return fail(SWA_E_INVALID, "packed metadata needs nseg > 0 and kv_len == q_len");
+  if (q_len == 0 && kv_len == 0) return SWA_OK;
+  cudaError_t e = swa::launch_build_metadata(cu_seqlens, nseg, q_len, kv_len, window, q_positions, kv_positions,
+                                             q_segment_ids, kv_segment_ids, full_starts, local_starts, causal_ends,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "build_metadata launch");
+  return SWA_OK;
+}
+
+int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                        const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                        const int32_t* counts, int count_full, int count_local, const int32_t* full_starts,
+                        const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
+                        void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
+                        float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
+  if (B <= 0 || Sq <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
+  if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
+  if (window <= 0) return fail(SWA_E_INVALID, "window_size must be positive");
+  if (!(scale_log2 > 0.0f)) return fail(SWA_E_INVALID, "softmax scale must be positive");
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || lse == nullptr)
+    return fail(SWA_E_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(SWA_E_INVALID, "q/k/v/out must be 16-byte aligned");
+  if (workspace == nullptr || workspace_bytes < 16) return fail(SWA_E_INVALID, "workspace must hold 16 bytes");
+  if (counts == nullptr && B != 1) return fail(SWA_E_INVALID, "device counts are required when B > 1");
+  if (full_cap < 0 || local_cap < 0 || (full_cap > 0 && full_idx == nullptr) ||
+      (local_cap > 0 && local_idx == nullptr))
+    return fail(SWA_E_INVALID, "bad index lists");
+  if (full_cap > full_stride && B > 1) return fail(SWA_E_INVALID, "full_cap exceeds full_stride");
+  if (local_cap > local_stride && B > 1) return fail(SWA_E_INVALID, "local_cap exceeds local_stride");
+  const bool has_meta = causal_ends != nullptr;
+  if (has_meta && (full_starts == nullptr || local_starts == nullptr))
+    return fail(SWA_E_INVALID, "metadata needs full_starts, local_starts and causal_ends");
+  if (bg_list != nullptr && n_bg <= 0) return fail(SWA_E_INVALID, "empty unit list");
+  if (static_cast<int64_t>(B) * Sq * Hq >= (int64_t(1) << 31) || static_cast<int64_t>(B) * Skv * Hkv >= (int64_t(1) << 31))
+    return fail(SWA_E_UNSUPPORTED, "tensor too large for 32-bit row indices");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, nsm = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (major != 10) return fail(SWA_E_UNSUPPORTED, "this library targets sm_100 (B200) devices");
+
+  const int r = Hq / Hkv;
+  int rp = r & (-r);  // largest power of two dividing the group size
+  if (rp > 256) rp = 256;
+
+  swa::PrefillParams p{};
+  {
+    const uint64_t qd[2] = {128, static_cast<uint64_t>(B) * Sq * Hq};
+    const uint64_t qs[1] = {256};
+    const uint32_t qb[2] = {64, static_cast<uint32_t>(rp < 128 ? rp : 128)};
+    if (!swa::make_bf16_map_sw128(&p.q_map, q, 2, qd, qs, qb)) return fail(SWA_E_TMA, "q tensor map");
+    const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Skv), static_cast<uint64_t>(B)};
+    const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Skv) * Hkv * 256};
+    const uint32_t kb[4] = {64, 1, 128, 1};
+    if (!swa::make_bf16_map_sw128(&p.k_map, k, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+    if (!swa::make_bf16_map_sw128(&p.v_map, v, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  }
+  p.idx[0] = full_idx;
+  p.idx[1] = local_idx;
+  p.idx_stride[0] = full_stride;
+  p.idx_stride[1] = local_stride;
+  p.idx_cap[0] = full_idx ? full_cap : 0;
+  p.idx_cap[1] = local_idx ? local_cap : 0;
+  p.counts = counts;
+  p.count_scalar[0] = count_full;
+  p.count_scalar[1] = count_local;
+  p.starts[0] = full_starts;
+  p.starts[1] = local_starts;
+  p.ends = causal_ends;
+  p.bg_list = bg_list;
+  p.n_bg = bg_list ? n_bg : B * Hkv;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.counter = workspace;
+  p.status = workspace + 1;
+  p.gate = gate;
+  p.B = B;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.window = window;
+  p.scale_log2 = scale_log2;
+  p.rp = rp;
+  p.pc = 256 / rp;
+  p.nhb = r / rp;
+  p.boxh = rp < 128 ? rp : 128;
+
+  const int64_t per_level = static_cast<int64_t>(p.n_bg) * p.nhb;
+  const int64_t items =
+      (static_cast<int64_t>(p.idx_cap[0] + p.pc - 1) / p.pc + (p.idx_cap[1] + p.pc - 1) / p.pc) * per_level;
+  if (items == 0) return SWA_OK;
+  const int ctas = static_cast<int>(items < nsm ? items : nsm);
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace reset");
+  e = swa::launch_prefill(p, ctas, s);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return SWA_OK;
+}
+
+}  // extern "C"

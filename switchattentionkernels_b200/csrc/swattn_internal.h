@@ -1,0 +1,67 @@
+// Internal declarations shared by the CUDA translation units of libswattn_b200.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace swa {
+
+// Bits of the device status word (int32).  The index-validation kernels set the
+// first group; the prefill kernel sets kStatusTimeout when a bounded wait gave up.
+enum : int32_t {
+  kStatusFullRange = 1 << 0,   // full list: index outside [0, seq_len)
+  kStatusFullOrder = 1 << 1,   // full list: not strictly increasing
+  kStatusLocalRange = 1 << 2,  // local list: index outside [0, seq_len)
+  kStatusLocalOrder = 1 << 3,  // local list: not strictly increasing
+  kStatusFullPad = 1 << 4,     // full list ([B, N] form): -1 padding not trailing
+  kStatusLocalPad = 1 << 5,    // local list ([B, N] form): -1 padding not trailing
+  kStatusCover = 1 << 6,       // per-batch counts do not add up to the sequence length
+  kStatusTimeout = 1 << 16,    // a device-side wait exceeded its limit
+};
+
+struct __align__(64) PrefillParams {
+  CUtensorMap q_map;  // 2-D {128, B*Sq*Hq}, box {64, boxh}, 128B swizzle
+  CUtensorMap k_map;  // 4-D {128, Hkv, Skv, B}, box {64, 1, 128, 1}, 128B swizzle
+  CUtensorMap v_map;
+  const int32_t* idx[2];       // routed positions per branch: [B, idx_stride]
+  int idx_stride[2];
+  int idx_cap[2];              // valid slots per row are < min(count, idx_cap)
+  const int32_t* counts;       // [2, B] device counts (nullable)
+  int count_scalar[2];         // counts for B == 1 when `counts` is null
+  const int32_t* starts[2];    // metadata: full_starts, local_starts (nullable)
+  const int32_t* ends;         // metadata: causal_ends (nullable: fixed-length masks)
+  const int32_t* bg_list;      // (b * Hkv + g) units handled by this launch (nullable: all)
+  int n_bg;
+  __nv_bfloat16* out;          // [B, Sq, Hq, 128]
+  float* lse;                  // [B, Sq, Hq]
+  int* counter;                // work counter, zero at launch
+  int* status;                 // status word (kStatus* bits)
+  const int* gate;             // nullable; non-zero => the launch does nothing
+  int B, Sq, Skv, Hq, Hkv, window;
+  float scale_log2;
+  int rp;    // query heads per position in a unit (power of two dividing Hq/Hkv)
+  int pc;    // positions per unit = 256 / rp
+  int nhb;   // head blocks per KV group = (Hq/Hkv) / rp
+  int boxh;  // rows per Q TMA box = min(rp, 128)
+};
+
+cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);
+uint32_t prefill_smem_bytes();
+
+cudaError_t launch_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local,
+                                int32_t* counts, cudaStream_t stream);
+
+cudaError_t launch_prepare_indices(const int32_t* idx, int B, int N, int seq_len, int padded_rows, int cap,
+                                   int32_t* padded, int32_t* count, int32_t* status, int range_bit, int order_bit,
+                                   int pad_bit, cudaStream_t stream);
+
+cudaError_t launch_check_cover(const int32_t* counts, int B, int seq_len, int32_t* status, cudaStream_t stream);
+
+cudaError_t launch_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_len, int window,
+                                  int32_t* q_positions, int32_t* kv_positions, int32_t* q_segment_ids,
+                                  int32_t* kv_segment_ids, int32_t* full_starts, int32_t* local_starts,
+                                  int32_t* causal_ends, cudaStream_t stream);
+
+}  // namespace swa

@@ -1,0 +1,66 @@
+"""Shared helpers of the parity tests: run the CUDA path, run the CPU oracle on
+the same inputs, compare with the stated tolerances."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import attention as oracle_attn
+from oracle import indices as oracle_idx
+
+# Tolerances against the FP32 oracle (BF16 output, P rounded to BF16 before P V).
+O_MAX_ABS = 2e-2
+O_MEAN_ABS = 2e-3
+LSE_MAX_ABS = 1e-3
+
+
+def lists_from_mask(mask: torch.Tensor):
+    m = mask.cpu().numpy().astype(bool)
+    full, local = [], []
+    for b in range(m.shape[0]):
+        f, l = oracle_idx.compact_mask(m[b])
+        full.append(f)
+        local.append(l)
+    return full, local
+
+
+def device_lists(full, local, device, B):
+    """Index tensors in the forward's input format (1-D for B=1, -1 padded [B, N] otherwise)."""
+    if B == 1:
+        return (torch.from_numpy(full[0]).to(device), torch.from_numpy(local[0]).to(device))
+    nf = max(1, max(len(x) for x in full))
+    nl = max(1, max(len(x) for x in local))
+    F = torch.full((B, nf), -1, dtype=torch.int32)
+    L = torch.full((B, nl), -1, dtype=torch.int32)
+    for b in range(B):
+        F[b, :len(full[b])] = torch.from_numpy(full[b])
+        L[b, :len(local[b])] = torch.from_numpy(local[b])
+    return F.to(device), L.to(device)
+
+
+def compare(O, LSE, O_ref, LSE_ref, rows=None, label=""):
+    """Compare on the rows where the oracle is defined (finite LSE)."""
+    O = O.float().cpu()
+    LSE = LSE.float().cpu()
+    sel = torch.isfinite(LSE_ref) if rows is None else rows
+    assert sel.any(), f"{label}: nothing to compare"
+    o_err = (O[sel] - O_ref[sel]).abs()
+    l_err = (LSE[sel] - LSE_ref[sel]).abs()
+    o_max, o_mean, l_max = o_err.max().item(), o_err.mean().item(), l_err.max().item()
+    assert torch.isfinite(O[sel]).all(), f"{label}: non-finite output rows"
+    assert o_max <= O_MAX_ABS, f"{label}: O max-abs {o_max:.3e} > {O_MAX_ABS}"
+    assert o_mean <= O_MEAN_ABS, f"{label}: O mean-abs {o_mean:.3e} > {O_MEAN_ABS}"
+    assert l_max <= LSE_MAX_ABS, f"{label}: LSE max-abs {l_max:.3e} > {LSE_MAX_ABS}"
+    return o_max, o_mean, l_max
+
+
+def oracle_subset(q, k, v, full, local, window, subset=None, metadata=None, sm_scale=None):
+    return oracle_attn.prefill_dense(q.cpu(), k.cpu(), v.cpu(), full, local, window=window, subset=subset,
+                                     metadata=metadata, sm_scale=sm_scale)
+
+
+def sample_positions(S: int, n: int, seed: int, must=()):
+    rng = np.random.default_rng(seed)
+    pick = set(rng.choice(S, size=min(n, S), replace=False).tolist())
+    pick.update(p for p in must if 0 <= p < S)
+    return np.array(sorted(pick), dtype=np.int64)
