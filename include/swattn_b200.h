@@ -94,7 +94,10 @@ int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_le
  *                          of routed positions (B == 1 with counts == NULL:
  *                          count_full / count_local are used).
  *   full_cap / local_cap : number of readable slots per row (<= stride).
- *   counts               : int32 [2, B] device counts (nullable when B == 1).
+ *   counts               : int32 device counts (nullable when B == 1): [2, B]
+ *                          (full row, then local row) or, with
+ *                          counts_batch_major = 1, [B, 2] as written by
+ *                          swa_compact_mask.
  *   full_starts, local_starts, causal_ends : int32 [Sq] varlen bounds
  *                          (all NULL: fixed-length masks key <= t and
  *                          t - window + 1 <= key <= t).
@@ -110,7 +113,8 @@ int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_le
  * Requires head_dim == 128, Hq % Hkv == 0, window > 0, 16-byte aligned q/k/v. */
 int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
                         const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
-                        const int32_t* counts, int count_full, int count_local, const int32_t* full_starts,
+                        const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                        const int32_t* full_starts,
                         const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
                         void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,

@@ -64,6 +64,53 @@ def legal_key_counts(full_lists, local_lists, *, window: int, skv: int, metadata
     return total
 
 
+def prefill_rows(q, k, v, b: int, positions, is_local: bool, *, window: int, sm_scale=None, metadata=None,
+                 budget_bytes: int = 1 << 28):
+    """Exact FP32 rows of one branch: ``(O [n, Hq, D], LSE [n, Hq])`` for ``positions`` of batch ``b``.
+
+    ``positions`` must be increasing (chunks take the union key range of
+    consecutive rows, like the kernel's query tiles).
+    """
+    B, Sq, Hq, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    r = Hq // Hkv
+    sl2 = scale_log2_of(sm_scale, D)
+    pos = np.asarray(positions, dtype=np.int64)
+    O = torch.empty((pos.size, Hq, D), dtype=torch.float32)
+    LSE = torch.empty((pos.size, Hq), dtype=torch.float32)
+    if pos.size == 0:
+        return O, LSE
+    lo, hi = row_bounds(pos, is_local, window, Skv, metadata)
+    c = 0
+    while c < pos.size:
+        span_guess = int(hi[min(c + 63, pos.size - 1)] - lo[c]) + 1
+        n = max(1, min(64, budget_bytes // max(1, 4 * Hq * max(span_guess, 1))))
+        sl = slice(c, c + n)
+        p, l, h = pos[sl], lo[sl], hi[sl]
+        n = p.size
+        c += n
+        L0, L1 = int(l.min()), int(h.max())
+        if L1 <= L0:
+            O[sl] = float("nan")
+            LSE[sl] = float("-inf")
+            continue
+        qc = q[b, torch.from_numpy(p)].float().view(n, Hkv, r, D)
+        kc = k[b, L0:L1].float()
+        vc = v[b, L0:L1].float()
+        s = torch.einsum("ngrd,lgd->ngrl", qc, kc) * sl2
+        keys = torch.arange(L0, L1)
+        legal = (keys[None, :] >= torch.from_numpy(l)[:, None]) & (keys[None, :] < torch.from_numpy(h)[:, None])
+        s = s.masked_fill(~legal[:, None, None, :], float("-inf"))
+        m = s.amax(dim=-1, keepdim=True)
+        m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+        pe = torch.exp2(s - m_safe)
+        den = pe.sum(dim=-1, keepdim=True)
+        num = torch.einsum("ngrl,lgd->ngrd", pe, vc)
+        O[sl] = (num / den).reshape(n, Hq, D)
+        LSE[sl] = (m_safe + torch.log2(den)).squeeze(-1).reshape(n, Hq)
+    return O, LSE
+
+
 def prefill_dense(q, k, v, full_lists, local_lists, *, window: int, sm_scale=None, metadata=None,
                   subset=None, budget_bytes: int = 1 << 28):
     """Exact FP32 result.  ``q``: ``[B,Sq,Hq,D]``, ``k``/``v``: ``[B,Skv,Hkv,D]`` (any float dtype, CPU).
@@ -73,9 +120,6 @@ def prefill_dense(q, k, v, full_lists, local_lists, *, window: int, sm_scale=Non
     Returns ``(O, LSE)`` as FP32 tensors ``[B,Sq,Hq,D]`` / ``[B,Sq,Hq]``.
     """
     B, Sq, Hq, D = q.shape
-    Skv, Hkv = k.shape[1], k.shape[2]
-    r = Hq // Hkv
-    sl2 = scale_log2_of(sm_scale, D)
     O = torch.full((B, Sq, Hq, D), float("nan"), dtype=torch.float32)
     LSE = torch.full((B, Sq, Hq), float("nan"), dtype=torch.float32)
     for b in range(B):
@@ -85,36 +129,10 @@ def prefill_dense(q, k, v, full_lists, local_lists, *, window: int, sm_scale=Non
                 pos = pos[np.isin(pos, np.asarray(subset[b]))]
             if pos.size == 0:
                 continue
-            lo, hi = row_bounds(pos, is_local, window, Skv, metadata)
-            c = 0
-            while c < pos.size:
-                # rows per chunk bounded by the score-matrix budget
-                span_guess = int(hi[min(c + 63, pos.size - 1)] - lo[c]) + 1
-                n = max(1, min(64, budget_bytes // max(1, 4 * Hq * max(span_guess, 1))))
-                p = pos[c:c + n]
-                l, h = lo[c:c + n], hi[c:c + n]
-                c += n
-                L0, L1 = int(l.min()), int(h.max())
-                qc = q[b, torch.from_numpy(p)].float().view(len(p), Hkv, r, D)
-                if L1 <= L0:
-                    O[b, torch.from_numpy(p)] = float("nan")
-                    LSE[b, torch.from_numpy(p)] = float("-inf")
-                    continue
-                kc = k[b, L0:L1].float()
-                vc = v[b, L0:L1].float()
-                s = torch.einsum("ngrd,lgd->ngrl", qc, kc) * sl2
-                keys = torch.arange(L0, L1)
-                legal = (keys[None, :] >= torch.from_numpy(l)[:, None]) & (keys[None, :] < torch.from_numpy(h)[:, None])
-                s = s.masked_fill(~legal[:, None, None, :], float("-inf"))
-                m = s.amax(dim=-1, keepdim=True)
-                m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
-                pe = torch.exp2(s - m_safe)
-                den = pe.sum(dim=-1, keepdim=True)
-                num = torch.einsum("ngrl,lgd->ngrd", pe, vc)
-                o = num / den
-                lse = (m_safe + torch.log2(den)).squeeze(-1)
-                O[b, torch.from_numpy(p)] = o.reshape(len(p), Hq, D)
-                LSE[b, torch.from_numpy(p)] = lse.reshape(len(p), Hq)
+            o, lse = prefill_rows(q, k, v, b, pos, is_local, window=window, sm_scale=sm_scale, metadata=metadata,
+                                  budget_bytes=budget_bytes)
+            O[b, torch.from_numpy(pos)] = o
+            LSE[b, torch.from_numpy(pos)] = lse
     return O, LSE
 
 

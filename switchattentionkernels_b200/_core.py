@@ -198,12 +198,18 @@ def _index_rows(indices: torch.Tensor, B: int, device: torch.device, name: str) 
 
 
 def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, window_size=1024, sm_scale=None,
-            validate=True, bg_list=None, out=None, lse=None):
+            validate=True, query_counts=None, bg_list=None, out=None, lse=None, prefill_events=None):
     """Both branches of Switch Attention GQA prefill (see ``switch_gqa_prefill_forward``).
 
-    ``bg_list`` (int32 device tensor of ``b * Hkv + g``) restricts the launch to
-    those (batch, KV group) units; ``out`` / ``lse`` may be given to write into
-    existing buffers (rows outside the computed units are left untouched).
+    ``query_counts``: optional int32 ``[B, 2]`` device tensor of per-row
+    ``(n_full, n_local)`` as returned by ``build_switch_query_indices_batched``;
+    the lists are then read as ``-1`` padded rows for any ``B`` and, with
+    ``validate=False``, no validation kernel runs.
+    ``bg_list`` (``b * Hkv + g`` ids) restricts the launch to those (batch, KV
+    group) units; ``out`` / ``lse`` may be given to write into existing buffers
+    (rows outside the computed units are left untouched).
+    ``prefill_events``: optional pair of CUDA events recorded on the current
+    stream right before and after the prefill kernel launch (kernel timing).
     """
     validate_qkv(q, k, v)
     if window_size <= 0:
@@ -213,21 +219,36 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     dev = q.device
     if metadata is not None:
         _check_metadata(metadata, q, q_len, kv_len)
+    padded = B > 1 or query_counts is not None
     full = _index_rows(full_query_indices, B, dev, "full_query_indices")
     local = _index_rows(local_query_indices, B, dev, "local_query_indices")
     scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * LOG2E
     if not scale > 0:
         raise ValueError("sm_scale must be positive")
+    if query_counts is not None:
+        if (query_counts.device != dev or query_counts.dtype != torch.int32 or tuple(query_counts.shape) != (B, 2)
+                or not query_counts.is_contiguous()):
+            raise ValueError("query_counts must be a contiguous int32 [B, 2] tensor on the device of Q")
 
+    n_full, n_local = int(full.shape[1]), int(local.shape[1])
+    if not padded and not validate and n_full + n_local != q_len:
+        raise ValueError(ERR_COVER)
+    if bg_list is not None:
+        bg_list = torch.as_tensor(bg_list, dtype=torch.int32)
+        if bg_list.ndim != 1 or bg_list.numel() == 0:
+            raise ValueError("bg_list must be a non-empty 1-D list of b * Hkv + g unit ids")
+        if bool(((bg_list < 0) | (bg_list >= B * Hkv)).any()):
+            raise ValueError("bg_list entries must lie in [0, B * Hkv)")
     lib = _native.load()
     stream = _native.stream_ptr(dev)
-    n_full, n_local = int(full.shape[1]), int(local.shape[1])
     ws = torch.zeros(4 + 2 * B, dtype=torch.int32, device=dev)
     status = ws[2:3]
     counts = ws[4:]
     gate = None
+    counts_arg, batch_major = None, 0
     with torch.cuda.device(dev):
-        if B == 1:
+        if not padded:
+            # the reference's form: B == 1, every entry of each list is a routed row
             if validate:
                 for t, n, rb, ob in ((full, n_full, _native.STATUS_FULL_RANGE, _native.STATUS_FULL_ORDER),
                                      (local, n_local, _native.STATUS_LOCAL_RANGE, _native.STATUS_LOCAL_ORDER)):
@@ -235,12 +256,10 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
                         _native.check(lib.swa_prepare_indices(_native.ptr(t), 1, n, q_len, 0, 0, None,
                                                               _native.ptr(counts), _native.ptr(status), rb, ob, 0,
                                                               stream), "index validation")
-                st = int(status.item())
-                _raise_status(st)
+                _raise_status(int(status.item()))
             if n_full + n_local != q_len:
                 raise ValueError(ERR_COVER)
-            counts_arg = None
-        else:
+        elif validate or query_counts is None:
             for t, n, row, rb, ob, pb in (
                     (full, n_full, 0, _native.STATUS_FULL_RANGE, _native.STATUS_FULL_ORDER, _native.STATUS_FULL_PAD),
                     (local, n_local, 1, _native.STATUS_LOCAL_RANGE, _native.STATUS_LOCAL_ORDER,
@@ -255,6 +274,8 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
             else:
                 gate = status
             counts_arg = counts
+        else:
+            counts_arg, batch_major = query_counts, 1
         if out is None:
             out = torch.empty_like(q)
         if lse is None:
@@ -265,19 +286,23 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
             fs = ls = ce = None
         n_bg = 0
         if bg_list is not None:
-            bg_list = bg_list.to(device=dev, dtype=torch.int32).contiguous()
+            bg_list = bg_list.to(device=dev).contiguous()
             n_bg = int(bg_list.numel())
+        if prefill_events is not None:
+            prefill_events[0].record()
         rc = lib.swa_prefill_forward(
             _native.ptr(q), _native.ptr(k), _native.ptr(v),
             _native.ptr(full) if n_full else None, _native.ptr(local) if n_local else None,
             n_full, n_local, n_full, n_local,
-            _native.ptr(counts_arg), n_full, n_local,
+            _native.ptr(counts_arg), batch_major, n_full, n_local,
             _native.ptr(fs), _native.ptr(ls), _native.ptr(ce),
             _native.ptr(bg_list), n_bg,
             _native.ptr(out), _native.ptr(lse),
             B, q_len, kv_len, Hq, Hkv, D, int(window_size), float(scale),
             _native.ptr(gate), _native.ptr(ws), ws.numel() * 4, stream)
         _native.check(rc, "switch_gqa_prefill_forward")
+        if prefill_events is not None:
+            prefill_events[1].record()
         if CHECK_DEVICE_STATUS:
             _raise_status(int(ws[1].item()))
     return out, lse

@@ -63,7 +63,7 @@ def _declare(lib) -> None:
         _p, _p, _p,            # q, k, v
         _p, _p,                # full_idx, local_idx
         _i, _i, _i, _i,        # strides, caps
-        _p, _i, _i,            # counts, count_full, count_local
+        _p, _i, _i, _i,        # counts, counts_batch_major, count_full, count_local
         _p, _p, _p,            # full_starts, local_starts, causal_ends
         _p, _i,                # bg_list, n_bg
         _p, _p,                # out, lse

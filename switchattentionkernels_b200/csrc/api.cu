@@ -88,7 +88,8 @@ int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_le
 
 int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
                         const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
-                        const int32_t* counts, int count_full, int count_local, const int32_t* full_starts,
+                        const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                        const int32_t* full_starts,
                         const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
                         void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
@@ -147,6 +148,8 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
   p.idx_cap[0] = full_idx ? full_cap : 0;
   p.idx_cap[1] = local_idx ? local_cap : 0;
   p.counts = counts;
+  p.cs_branch = counts_batch_major ? 1 : B;
+  p.cs_batch = counts_batch_major ? 2 : 1;
   p.count_scalar[0] = count_full;
   p.count_scalar[1] = count_local;
   p.starts[0] = full_starts;

@@ -11,25 +11,34 @@
 // tile once per group instead of once per query head and narrows the position
 // span of a tile, so the union key range wastes fewer masked entries.
 //
-// Roles (384 threads, one CTA per SM, persistent over a dynamic work counter):
-//   warp 0      producer : TMA Q gather (one box per routed position) and the
-//                          K/V tile ring (4 stages of 128 keys x 128 dims)
+// Roles (320 threads, one CTA per SM, persistent over a dynamic work counter):
+//   warp 0      producer : takes work units from the global counter (one unit
+//                          ahead) and publishes them through a shared-memory ring;
+//                          TMA Q gather (one box per routed position, the next
+//                          unit's boxes prefetched into L2 one unit ahead) and the
+//                          K/V tile ring (5 stages of 128 keys x 128 dims)
 //   warp 1      MMA      : one thread issues tcgen05.mma
 //                          S_i = Q_i K^T (SS, K-major) and O_i += P_i V (TS: P in TMEM,
-//                          V MN-major), commits to mbarriers
-//   warp 2      scheduler: fetches work units (atomic counter), publishes them
-//                          through a shared-memory ring
-//   warps 4-7   softmax 0: rows 0..127   (TMEM lane = row)
-//   warps 8-11  softmax 1: rows 128..255
+//                          V MN-major), commits to mbarriers.  Its issue order is one
+//                          continuous stream over key steps; at a unit boundary the
+//                          next unit's first S MMAs follow the last P V MMAs exactly
+//                          like the next key step inside a unit, so the tensor pipe
+//                          does not drain between units.
+//   warps 2-5   softmax 0: rows 0..127   (TMEM lane = row), then the O/LSE epilogue
+//   warps 6-9   softmax 1: rows 128..255
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs)
-// overwrites the first 64 columns of S_i and is consumed by the next PV MMA.
+// overwrites the first 64 columns of S_i and is consumed by the next PV MMA.  P is
+// published in two halves of 64 keys so the PV MMAs of the first half start while
+// the second half is still being exponentiated.
 //
 // Numerics follow the reference: FP32 scores, log2-domain online softmax with
 // scale_log2 = sm_scale * log2(e), running max initialised to -2^30 (scaled),
 // P rounded to BF16 before P V, the row sum accumulated from the unrounded FP32
 // P, O = acc / l and LSE = log2(l) + m.  The running max is only raised (and O
 // rescaled) when it grows by more than 8 (a factor 256), which leaves the final
-// O and LSE mathematically unchanged while removing most O rescales.
+// O and LSE mathematically unchanged while removing most O rescales.  Every other
+// pair of exponentials is evaluated on the FMA pipe (exp2_poly_pair) instead of the
+// MUFU unit, which otherwise bounds the softmax rate.
 #include "sm100.cuh"
 #include "swattn_internal.h"
 
@@ -37,7 +46,7 @@ namespace swa {
 
 namespace {
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 576;
 constexpr int kBK = 128;            // keys per K/V tile
 constexpr int kStages = 4;          // K/V ring depth (each stage: one K or one V tile)
 constexpr int kSchedSlots = 4;      // work-unit ring depth
@@ -68,14 +77,18 @@ struct SmemLayout {
   static constexpr int b_kv_full = b_q_empty + 2;
   static constexpr int b_kv_empty = b_kv_full + kStages;
   static constexpr int b_s_full = b_kv_empty + kStages;
-  static constexpr int b_p_full = b_s_full + 2;
-  static constexpr int b_o_full = b_p_full + 2;
+  static constexpr int b_p_half = b_s_full + 2;    // [tile][half]
+  static constexpr int b_o_full = b_p_half + 4;
   static constexpr int b_o_empty = b_o_full + 2;
   static constexpr int b_drain = b_o_empty + 2;
   static constexpr int n_bars = b_drain + 1;
   static constexpr uint32_t units = bars + ((n_bars * 8 + 63) / 64) * 64;
   static constexpr uint32_t misc = units + kSchedSlots * sizeof(Unit);
-  static constexpr uint32_t total = misc + 64;
+  // row-max exchange [2 parity][2 tile][2 half][128] floats (4 KB), then the row-sum
+  // exchange [2 tile][2 half][128] floats (2 KB)
+  static constexpr uint32_t xchg = misc + 64;
+  static constexpr uint32_t orows = xchg + 4096 + 2048;  // output row offsets [2 tile][128] int64 (2 KB)
+  static constexpr uint32_t total = orows + 2048;
 };
 
 constexpr uint32_t kSmemBytes = SmemLayout::total + 1024;  // + alignment slack
@@ -83,6 +96,35 @@ constexpr uint32_t kSmemBytes = SmemLayout::total + 1024;  // + alignment slack
 struct RowBounds {
   int lo, hi;
 };
+
+// Optional cycle-level event trace of CTA 0 (compiled only with -DSWA_TRACE): each
+// recorder (MMA issuer, softmax warpgroup 0, softmax warpgroup 1) appends
+// (event id, key step, clock64) records to its own region of g_swa_trace.
+#ifdef SWA_TRACE
+__device__ unsigned long long* g_swa_trace = nullptr;
+constexpr int kTraceCap = 8192;
+struct Tracer {
+  unsigned long long* buf;
+  int n;
+  __device__ explicit Tracer(int recorder)
+      : buf(blockIdx.x == 0 && recorder >= 0 && g_swa_trace != nullptr
+                ? g_swa_trace + static_cast<size_t>(recorder) * 2 * kTraceCap
+                : nullptr),
+        n(0) {}
+  __device__ __forceinline__ void ev(int id, int step) {
+    if (buf != nullptr && n < kTraceCap) {
+      buf[2 * n] = (static_cast<unsigned long long>(id) << 32) | static_cast<unsigned>(step);
+      buf[2 * n + 1] = clock64();
+      ++n;
+    }
+  }
+};
+#else
+struct Tracer {
+  __device__ explicit Tracer(int) {}
+  __device__ __forceinline__ void ev(int, int) {}
+};
+#endif
 
 __device__ __forceinline__ RowBounds row_bounds(const PrefillParams& p, int branch, int qpos) {
   RowBounds r;
@@ -97,7 +139,7 @@ __device__ __forceinline__ RowBounds row_bounds(const PrefillParams& p, int bran
 }
 
 __device__ __forceinline__ int branch_count(const PrefillParams& p, int branch, int b) {
-  return p.counts != nullptr ? p.counts[branch * p.B + b] : p.count_scalar[branch];
+  return p.counts != nullptr ? p.counts[branch * p.cs_branch + b * p.cs_batch] : p.count_scalar[branch];
 }
 
 __device__ __forceinline__ int load_pos(const PrefillParams& p, int branch, int b, int slot) {
@@ -163,6 +205,63 @@ __device__ __forceinline__ void read_unit(const volatile Unit* src, Unit& u) {
   u.n = src->n;
 }
 
+// 2^x for a pair of arguments on the FMA pipe.  Cody-Waite style range
+// reduction x = j + f with j = round(x) (the 1.5 * 2^23 shifter), f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted for minimum maximal relative
+// error on that interval (max relative error 7.5e-5, below the BF16 rounding that
+// P receives); 2^j is added to the exponent field.  Arguments are clamped at
+// -125 so the result stays a normal number (masked entries, -inf, give 2^-125).
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& p0, float& p1) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t shifter = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t neg_shifter = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t minus_one = f2_pack(-1.0f, -1.0f);
+  const uint64_t t = f2_add(xc, shifter);          // 1.5 * 2^23 + round(x)
+  const uint64_t jf = f2_add(t, neg_shifter);      // round(x)
+  const uint64_t f = f2_fma(jf, minus_one, xc);    // x - round(x)
+  uint64_t p = f2_fma(f2_pack(0.05517097935080528f, 0.05517097935080528f), f,
+                      f2_pack(0.24260970950126648f, 0.24260970950126648f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999281764030457f, 0.9999281764030457f));
+  float t0, t1, q0, q1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, q0, q1);
+  // bits(t) = bits(shifter) + j and bits(shifter) * 2^23 vanishes mod 2^32
+  p0 = __int_as_float(__float_as_int(t0) * (1 << 23) + __float_as_int(q0));
+  p1 = __int_as_float(__float_as_int(t1) * (1 << 23) + __float_as_int(q1));
+}
+
+__device__ __forceinline__ float row_max64(const float* s) {
+  float t[22];
+#pragma unroll
+  for (int i = 0; i < 21; ++i) t[i] = fmax3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+  t[21] = s[63];
+  float u[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) u[i] = fmax3(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+  u[7] = t[21];
+  return fmax3(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[5]), fmaxf(u[6], u[7]));
+}
+
+__device__ __forceinline__ float row_max128(const float* s) {
+  float t[43];
+#pragma unroll
+  for (int i = 0; i < 42; ++i) t[i] = fmax3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+  t[42] = fmaxf(s[126], s[127]);
+  float u[15];
+#pragma unroll
+  for (int i = 0; i < 14; ++i) u[i] = fmax3(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+  u[14] = t[42];
+  float w[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) w[i] = fmax3(u[3 * i], u[3 * i + 1], u[3 * i + 2]);
+  return fmax3(fmax3(w[0], w[1], w[2]), w[3], w[4]);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __grid_constant__ PrefillParams p) {
   if (p.gate != nullptr && *p.gate != 0) return;  // index validation failed: write nothing
 
@@ -181,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   uint64_t* kv_full = bars + SmemLayout::b_kv_full;
   uint64_t* kv_empty = bars + SmemLayout::b_kv_empty;
   uint64_t* s_full = bars + SmemLayout::b_s_full;
-  uint64_t* p_full = bars + SmemLayout::b_p_full;
+  uint64_t* p_half = bars + SmemLayout::b_p_half;
   uint64_t* o_full = bars + SmemLayout::b_o_full;
   uint64_t* o_empty = bars + SmemLayout::b_o_empty;
   uint64_t* drain = bars + SmemLayout::b_drain;
@@ -192,15 +291,16 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSchedSlots; ++s) {
       mbar_init(&sched_full[s], 1);
-      mbar_init(&sched_empty[s], 1 + 1 + 256);  // producer lane 0, MMA lane 0, 256 softmax threads
+      mbar_init(&sched_empty[s], 1 + 512);  // MMA lane 0 and the 512 softmax threads
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 256);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_half[2 * i], 128);
+      mbar_init(&p_half[2 * i + 1], 128);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&o_empty[i], 256);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -224,27 +324,42 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 2) {
-    // ------------------------------------------------------------------ scheduler
-    if (lane == 0) {
-      int maxnpb0 = 0, maxnpb1 = 0;
-      for (int b = 0; b < p.B; ++b) {
-        maxnpb0 = max(maxnpb0, (min(branch_count(p, 0, b), p.idx_cap[0]) + p.pc - 1) / p.pc);
-        maxnpb1 = max(maxnpb1, (min(branch_count(p, 1, b), p.idx_cap[1]) + p.pc - 1) / p.pc);
+  if (warp == 0) {
+    // ------------------------------------------------------------------ scheduler + producer
+    // Lane 0 takes work items from the global counter (one unit ahead), every lane
+    // decodes the same item, the unit is published through the ring for the MMA and
+    // softmax warps, and the warp then issues the unit's TMA loads.
+    int maxnpb0 = 0, maxnpb1 = 0;
+    for (int b = 0; b < p.B; ++b) {
+      maxnpb0 = max(maxnpb0, (min(branch_count(p, 0, b), p.idx_cap[0]) + p.pc - 1) / p.pc);
+      maxnpb1 = max(maxnpb1, (min(branch_count(p, 1, b), p.idx_cap[1]) + p.pc - 1) / p.pc);
+    }
+    const int per_level = p.n_bg * p.nhb;
+    const int nf = maxnpb0 * per_level;
+    const int total = nf + maxnpb1 * per_level;
+    auto fetch = [&](Unit& u) {
+      u.valid = 0;
+      while (true) {
+        int it = 0;
+        if (lane == 0) it = atomicAdd(p.counter, 1);
+        it = __shfl_sync(0xffffffffu, it, 0);
+        if (it >= total) break;
+        if (decode_item(p, it, nf, maxnpb0, maxnpb1, u)) break;
       }
-      const int per_level = p.n_bg * p.nhb;
-      const int nf = maxnpb0 * per_level;
-      const int total = nf + maxnpb1 * per_level;
-      for (int k = 0;; ++k) {
-        const int slot = k % kSchedSlots;
-        if (!mbar_wait(&sched_empty[slot], ((k / kSchedSlots) & 1) ^ 1, abort_flag)) break;
-        Unit u;
-        u.valid = 0;
-        while (true) {
-          const int it = atomicAdd(p.counter, 1);
-          if (it >= total) break;
-          if (decode_item(p, it, nf, maxnpb0, maxnpb1, u)) break;
-        }
+    };
+    uint32_t kv_it = 0;
+    uint32_t q_use[2] = {0, 0};
+    const int r = p.Hq / p.Hkv;
+    const int boxes = 128 / p.boxh;  // boxes per tile per 64-column half
+    Unit u;
+    fetch(u);
+    for (int k = 0;; ++k) {
+      Unit un;
+      un.valid = 0;
+      if (u.valid) fetch(un);
+      const int slot = k % kSchedSlots;
+      if (!mbar_wait(&sched_empty[slot], ((k / kSchedSlots) & 1) ^ 1, abort_flag)) break;
+      if (lane == 0) {
         volatile Unit* dst = &units[slot];
         dst->valid = u.valid;
         dst->branch = u.branch;
@@ -256,61 +371,65 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         dst->j0 = u.j0;
         dst->n = u.n;
         mbar_arrive(&sched_full[slot]);
-        if (!u.valid) break;
       }
-    }
-  } else if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    uint32_t kv_it = 0;
-    uint32_t q_use[2] = {0, 0};
-    const int r = p.Hq / p.Hkv;
-    const int boxes = 128 / p.boxh;  // boxes per tile per 64-column half
-    for (int k = 0;; ++k) {
-      const int slot = k % kSchedSlots;
-      if (!mbar_wait(&sched_full[slot], (k / kSchedSlots) & 1, abort_flag)) break;
-      Unit u;
-      read_unit(&units[slot], u);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sched_empty[slot]);
       if (!u.valid) break;
-      if (u.n == 0) continue;
-      bool ok = true;
-      for (int i = 0; i < 2 && ok; ++i) {
-        if (!mbar_wait(&q_empty[i], (q_use[i] & 1) ^ 1, abort_flag)) { ok = false; break; }
-        ++q_use[i];
-        if (lane == 0) mbar_arrive_expect_tx(&q_full[i], kTileBytes);
-        __syncwarp();
-        uint8_t* qdst = smem + (i == 0 ? SmemLayout::q0 : SmemLayout::q1);
-        for (int t = lane; t < 2 * boxes; t += 32) {
+      if (un.valid && un.n > 0) {
+        // Prefetch the next unit's Q boxes into L2 so its gather (issued only once
+        // this unit's last S MMA has freed the Q buffers) hits L2.
+        for (int t = lane; t < 2 * 2 * boxes; t += 32) {
           const int half = t & 1;
-          const int bx = t >> 1;
-          const int row0 = 128 * i + bx * p.boxh;          // first unit row of this box
-          const int slot_in_unit = row0 / p.rp;
-          const int hoff = row0 % p.rp;
-          const int slot_abs = min(u.pb * p.pc + slot_in_unit, u.count - 1);
-          const int pos = min(max(load_pos(p, u.branch, u.b, slot_abs), 0), p.Sq - 1);
-          const int row = (u.b * p.Sq + pos) * p.Hq + u.g * r + u.hb * p.rp + hoff;
-          tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, &q_full[i], half * 64, row);
+          const int row0 = (t >> 1) * p.boxh;  // over both tiles
+          const int slot_abs = min(un.pb * p.pc + row0 / p.rp, un.count - 1);
+          const int pos = min(max(load_pos(p, un.branch, un.b, slot_abs), 0), p.Sq - 1);
+          const int row = (un.b * p.Sq + pos) * p.Hq + un.g * r + un.hb * p.rp + row0 % p.rp;
+          tma_prefetch_l2_2d(&p.q_map, half * 64, row);
         }
       }
-      if (!ok) break;
-      for (int j = 0; j < u.n && ok; ++j) {
-        const int key0 = (u.j0 + j) * kBK;
-        for (int kv = 0; kv < 2; ++kv) {
+      bool ok = true;
+      if (u.n > 0) {
+        auto load_kv = [&](int j, int kv) -> bool {
           const uint32_t s = kv_it % kStages;
-          if (!mbar_wait(&kv_empty[s], ((kv_it / kStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
-            uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes;
+          if (!mbar_wait(&kv_empty[s], ((kv_it / kStages) & 1) ^ 1, abort_flag)) return false;
+          // lanes 0 and 1 each issue one 64-column half; lane 0 arms the barrier first
+          if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+          __syncwarp();
+          if (lane < 2) {
+            uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes + lane * kHalfBytes;
             const CUtensorMap* map = kv == 0 ? &p.k_map : &p.v_map;
-            tma_load_4d(dst, map, &kv_full[s], 0, u.g, key0, u.b);
-            tma_load_4d(dst + kHalfBytes, map, &kv_full[s], 64, u.g, key0, u.b);
+            tma_load_4d(dst, map, &kv_full[s], lane * 64, u.g, (u.j0 + j) * kBK, u.b);
           }
           __syncwarp();
           ++kv_it;
-        }
+          return true;
+        };
+        auto load_q = [&](int i) -> bool {
+          // Q_i is free once the previous unit's epilogue has stored its output from it
+          if (!mbar_wait(&q_empty[i], (q_use[i] & 1) ^ 1, abort_flag)) return false;
+          ++q_use[i];
+          if (lane == 0) mbar_arrive_expect_tx(&q_full[i], kTileBytes);
+          __syncwarp();
+          uint8_t* qdst = smem + (i == 0 ? SmemLayout::q0 : SmemLayout::q1);
+          for (int t = lane; t < 2 * boxes; t += 32) {
+            const int half = t & 1;
+            const int bx = t >> 1;
+            const int row0 = 128 * i + bx * p.boxh;          // first unit row of this box
+            const int slot_in_unit = row0 / p.rp;
+            const int hoff = row0 % p.rp;
+            const int slot_abs = min(u.pb * p.pc + slot_in_unit, u.count - 1);
+            const int pos = min(max(load_pos(p, u.branch, u.b, slot_abs), 0), p.Sq - 1);
+            const int row = (u.b * p.Sq + pos) * p.Hq + u.g * r + u.hb * p.rp + hoff;
+            tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, &q_full[i], half * 64, row);
+          }
+          return true;
+        };
+        // ring order K_0, V_0, K_1, V_1, ...; the Q tiles go between K_0 and V_0 so
+        // that K_0 streams in while the previous unit's epilogues still hold Q
+        ok = load_kv(0, 0) && load_q(0) && load_q(1) && load_kv(0, 1);
+        for (int j = 1; j < u.n && ok; ++j) ok = load_kv(j, 0) && load_kv(j, 1);
       }
       if (!ok) break;
+      u = un;
     }
     if (*abort_flag) {
       // Let every load already issued land before the CTA releases its memory.
@@ -328,129 +447,181 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // The whole warp runs this loop (waits, descriptors); one elected lane issues
+    // each tcgen05 instruction.
     constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
     constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
     const uint32_t q_addr[2] = {smem_u32(smem + SmemLayout::q0), smem_u32(smem + SmemLayout::q1)};
     const uint32_t kv_addr = smem_u32(smem + SmemLayout::kv);
     const uint32_t tm_s[2] = {tmem + 0, tmem + 128};
     const uint32_t tm_o[2] = {tmem + 256, tmem + 384};
-    uint32_t kv_it = 0, q_use[2] = {0, 0}, p_use[2] = {0, 0}, o_use = 0;
+    uint32_t kv_it = 0, q_use[2] = {0, 0}, p_use[2] = {0, 0}, o_use[2] = {0, 0};
+    int k_sched = 0;
     bool ok = true;
+    Tracer tr(lane == 0 ? 0 : -1);
+    int step = 0;
+
+    // Next unit with key tiles from the ring (units without any are consumed and skipped).
+    auto next_unit = [&](Unit& u) -> bool {
+      while (true) {
+        const int slot = k_sched % kSchedSlots;
+        if (!mbar_wait(&sched_full[slot], (k_sched / kSchedSlots) & 1, abort_flag)) { ok = false; return false; }
+        read_unit(&units[slot], u);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sched_empty[slot]);
+        ++k_sched;
+        if (!u.valid) return false;
+        if (u.n > 0) return true;
+      }
+    };
     auto issue_s = [&](int i, uint32_t kstage) {
       const uint32_t kb = kv_addr + kstage * kTileBytes;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-        umma_ss(tm_s[i], make_smem_desc_sw128(q_addr[i] + off, 16, 1024), make_smem_desc_sw128(kb + off, 16, 1024),
-                idesc_s, kk > 0 ? 1u : 0u);
+        umma_ss_warp(tm_s[i], make_smem_desc_sw128(q_addr[i] + off, 16, 1024),
+                     make_smem_desc_sw128(kb + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
       }
     };
-    auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) {
+    // P V for one tile, in two halves of 64 keys gated by the softmax's half barriers.
+    auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) -> bool {
       const uint32_t vb = kv_addr + vstage * kTileBytes;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        umma_ts(tm_o[i], tm_s[i] + kk * 8, make_smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), idesc_o,
-                (accumulate || kk > 0) ? 1u : 0u);
+      for (int h = 0; h < 2; ++h) {
+        if (!mbar_wait(&p_half[2 * i + h], p_use[i] & 1, abort_flag)) { ok = false; return false; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
+          umma_ts_warp(tm_o[i], tm_s[i] + kk * 8, make_smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), idesc_o,
+                       (accumulate || kk > 0) ? 1u : 0u);
+        }
       }
+      ++p_use[i];
+      return true;
     };
-    for (int k = 0; ok; ++k) {
-      const int slot = k % kSchedSlots;
-      if (!mbar_wait(&sched_full[slot], (k / kSchedSlots) & 1, abort_flag)) break;
-      Unit u;
-      read_unit(&units[slot], u);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sched_empty[slot]);
-      if (!u.valid) break;
-      if (u.n == 0) continue;
-      if (lane == 0) {
-        // prologue: S_0(0), S_1(0)
-        uint32_t ks = kv_it % kStages;
-        ok = ok && mbar_wait(&q_full[0], q_use[0] & 1, abort_flag);
-        ok = ok && mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag);
-        if (ok) {
-          ++q_use[0];
-          tc_fence_after();
-          issue_s(0, ks);
-          tc_commit(&s_full[0]);
-        }
-        ok = ok && mbar_wait(&q_full[1], q_use[1] & 1, abort_flag);
-        if (ok) {
-          ++q_use[1];
-          tc_fence_after();
-          issue_s(1, ks);
-          tc_commit(&s_full[1]);
-          if (u.n == 1) {
-            tc_commit(&q_empty[0]);
-            tc_commit(&q_empty[1]);
-          }
-          tc_commit(&kv_empty[ks]);
-          ++kv_it;
-        }
-        for (int j = 0; j < u.n && ok; ++j) {
-          const uint32_t vs = kv_it % kStages;
-          ok = ok && mbar_wait(&kv_full[vs], (kv_it / kStages) & 1, abort_flag);
-          ++kv_it;
-          ok = ok && mbar_wait(&p_full[0], p_use[0] & 1, abort_flag);
-          ++p_use[0];
-          if (j == 0) ok = ok && mbar_wait(&o_empty[0], (o_use & 1) ^ 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(0, vs, j > 0);
-          uint32_t ks_next = 0;
-          const bool more = j + 1 < u.n;
-          if (more) {
-            ks_next = kv_it % kStages;
-            ok = ok && mbar_wait(&kv_full[ks_next], (kv_it / kStages) & 1, abort_flag);
-            ++kv_it;
-            if (!ok) break;
-            issue_s(0, ks_next);
-            tc_commit(&s_full[0]);
-            if (j + 2 == u.n) tc_commit(&q_empty[0]);
-          } else {
-            tc_commit(&o_full[0]);
-          }
-          ok = ok && mbar_wait(&p_full[1], p_use[1] & 1, abort_flag);
-          ++p_use[1];
-          if (j == 0) ok = ok && mbar_wait(&o_empty[1], (o_use & 1) ^ 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(1, vs, j > 0);
-          tc_commit(&kv_empty[vs]);
-          if (more) {
-            issue_s(1, ks_next);
-            tc_commit(&s_full[1]);
-            if (j + 2 == u.n) tc_commit(&q_empty[1]);
-            tc_commit(&kv_empty[ks_next]);
-          } else {
-            tc_commit(&o_full[1]);
-          }
-        }
-        ++o_use;
+    // S MMAs of one key step for tile i.  (Q_i is released by the epilogue, which
+    // stages the tile's output rows in the Q_i buffer once the last S MMA is done.)
+    auto issue_s_step = [&](int i, uint32_t kstage) {
+      issue_s(i, kstage);
+      tc_commit_warp(&s_full[i]);
+    };
+
+    Unit cur;
+    bool have = next_unit(cur);
+    if (have) {
+      const uint32_t ks = kv_it % kStages;
+      ok = ok && mbar_wait(&q_full[0], q_use[0] & 1, abort_flag);
+      ok = ok && mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag);
+      if (ok) {
+        ++q_use[0];
+        tc_fence_after();
+        issue_s_step(0, ks);
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      ok = ok && mbar_wait(&q_full[1], q_use[1] & 1, abort_flag);
+      if (ok) {
+        ++q_use[1];
+        tc_fence_after();
+        issue_s_step(1, ks);
+        tc_commit_warp(&kv_empty[ks]);
+        ++kv_it;
+      }
     }
-    if (lane == 0) {
-      // drain: wait until every MMA issued by this thread has completed
-      tc_commit(drain);
-      volatile int dummy = 0;
-      mbar_wait(drain, 0, &dummy);
+    int j = 0;
+    while (have && ok) {
+      // invariant: S_0(j), S_1(j) of `cur` are issued.  Inside a unit the order is
+      // PV_0(j), S_0(j+1), PV_1(j), S_1(j+1); at a unit's last step both P V MMAs go
+      // first, then the next unit's S MMAs (their Q tiles arrive only after this
+      // unit's epilogue has stored its output through the Q buffers).
+      const bool last = j == cur.n - 1;
+      const uint32_t vs = kv_it % kStages;
+      tr.ev(1, step);
+      if (!mbar_wait(&kv_full[vs], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
+      ++kv_it;
+      tr.ev(2, step);
+      if (j == 0) {
+        if (!mbar_wait(&o_empty[0], (o_use[0] & 1) ^ 1, abort_flag)) { ok = false; break; }
+        ++o_use[0];
+      }
+      if (!issue_pv(0, vs, j > 0)) break;
+      tr.ev(3, step);
+      uint32_t ks = 0;
+      if (last) {
+        tc_commit_warp(&o_full[0]);
+      } else {
+        ks = kv_it % kStages;
+        if (!mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
+        ++kv_it;
+        tc_fence_after();
+        tr.ev(4, step);
+        issue_s_step(0, ks);
+      }
+      if (j == 0) {
+        if (!mbar_wait(&o_empty[1], (o_use[1] & 1) ^ 1, abort_flag)) { ok = false; break; }
+        ++o_use[1];
+      }
+      if (!issue_pv(1, vs, j > 0)) break;
+      tr.ev(5, step);
+      tc_commit_warp(&kv_empty[vs]);
+      if (!last) {
+        issue_s_step(1, ks);
+        tc_commit_warp(&kv_empty[ks]);
+        ++j;
+      } else {
+        tc_commit_warp(&o_full[1]);
+        have = next_unit(cur);
+        if (!ok || !have) break;
+        j = 0;
+        const uint32_t k0s = kv_it % kStages;
+        if (!mbar_wait(&q_full[0], q_use[0] & 1, abort_flag)) { ok = false; break; }
+        ++q_use[0];
+        if (!mbar_wait(&kv_full[k0s], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
+        ++kv_it;
+        tc_fence_after();
+        issue_s_step(0, k0s);
+        if (!mbar_wait(&q_full[1], q_use[1] & 1, abort_flag)) { ok = false; break; }
+        ++q_use[1];
+        tc_fence_after();
+        issue_s_step(1, k0s);
+        tc_commit_warp(&kv_empty[k0s]);
+      }
+      tr.ev(6, step);
+      ++step;
     }
+    // drain: wait until every MMA issued by this warp has completed
+    tc_commit_warp(drain);
+    volatile int dummy = 0;
+    mbar_wait(drain, 0, &dummy);
     __syncwarp();
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    const int tile = (warp - 4) >> 2;            // 0 or 1
-    const int t = threadIdx.x - 128 * (1 + tile);  // row within the tile = TMEM lane
+    // Four warpgroups: tile = (warp - 2) / 8, column half = ((warp - 2) / 4) % 2.
+    // Thread (tile, half, t) owns keys [64 * half, 64 * half + 64) of row t of its
+    // tile.  A warp may only access the TMEM lane quarter (warp % 4), so each group
+    // of four consecutive warps covers lanes 0..127.  The two threads of a row
+    // exchange their partial row maxima through shared memory every key step (named
+    // barrier 1 + tile over the tile's 256 threads) and their partial row sums once
+    // per unit, at the epilogue.
+    const int grp = (warp - 2) >> 2;             // 0..3
+    const int tile = grp >> 1;
+    const int half = grp & 1;
     const int lane_base = (warp & 3) * 32;
+    const int t = lane_base + lane;              // row within the tile = TMEM lane
     const uint32_t tm_s = tmem + 128 * tile + (static_cast<uint32_t>(lane_base) << 16);
-    const uint32_t tm_o = tmem + 256 + 128 * tile + (static_cast<uint32_t>(lane_base) << 16);
+    const uint32_t tm_o = tmem + 256 + 128 * tile + 64 * half + (static_cast<uint32_t>(lane_base) << 16);
     const int R = 128 * tile + t;                  // row within the unit
     const int slot_in_unit = R / p.rp;
     const int head_in_group_off = R % p.rp;
     const int r = p.Hq / p.Hkv;
     const float sl2 = p.scale_log2;
     const float m_init = -1073741824.0f * sl2;     // reference initial row max (-2^30), scaled
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
+    float* xmax = reinterpret_cast<float*>(smem + SmemLayout::xchg);          // [2 parity][2 tile][2 half][128]
+    float* xsum = reinterpret_cast<float*>(smem + SmemLayout::xchg + 4096);   // [2 tile][2 half][128]
+    static_assert(SmemLayout::orows - SmemLayout::xchg == 4096 + 2048, "exchange buffer sizes");
+    const int bar_id = 1 + tile;
     uint32_t s_use = 0, o_use = 0;
     bool ok = true;
+    Tracer tr(t == 0 && half == 0 ? 1 + tile : -1);
     for (int k = 0; ok; ++k) {
       const int slot = k % kSchedSlots;
       if (!mbar_wait(&sched_full[slot], (k / kSchedSlots) & 1, abort_flag)) break;
@@ -469,45 +640,46 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       if (u.n == 0) {
         if (valid_row) {
           const uint32_t nan_pair = 0x7FC07FC0u;
-          uint4* dst = reinterpret_cast<uint4*>(p.out + orow * 128);
+          uint4* dst = reinterpret_cast<uint4*>(p.out + orow * 128 + 64 * half);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) dst[c] = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
-          p.lse[orow] = -INFINITY;
+          for (int c = 0; c < 8; ++c) dst[c] = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
+          if (half == 0) p.lse[orow] = -INFINITY;
         }
         continue;
       }
       float m = m_init;
-      float l = 0.0f;
+      float l = 0.0f;   // partial row sum over this thread's key half
       for (int j = 0; j < u.n; ++j) {
+        tr.ev(10, s_use + 1);
         if (!mbar_wait(&s_full[tile], s_use & 1, abort_flag)) { ok = false; break; }
-        ++s_use;
+        tr.ev(11, s_use + 1);
         tc_fence_after();
-        uint32_t sr[128];
-        tmem_ld_x32(tm_s + 0, sr + 0);
-        tmem_ld_x32(tm_s + 32, sr + 32);
-        tmem_ld_x32(tm_s + 64, sr + 64);
-        tmem_ld_x32(tm_s + 96, sr + 96);
+        uint32_t sr[64];
+        tmem_ld_x32(tm_s + 64 * half, sr + 0);
+        tmem_ld_x32(tm_s + 64 * half + 32, sr + 32);
         tmem_ld_wait();
         reg_fence32(sr + 0);
         reg_fence32(sr + 32);
-        reg_fence32(sr + 64);
-        reg_fence32(sr + 96);
         float* s = reinterpret_cast<float*>(sr);
-        const int k0 = (u.j0 + j) * kBK;
-        if (!(rb.lo <= k0 && k0 + kBK <= rb.hi)) {
+        const int k0 = (u.j0 + j) * kBK + 64 * half;
+        if (!(rb.lo <= k0 && k0 + 64 <= rb.hi)) {
 #pragma unroll
-          for (int e = 0; e < 128; ++e) {
+          for (int e = 0; e < 64; ++e) {
             const int key = k0 + e;
             if (key < rb.lo || key >= rb.hi) s[e] = -INFINITY;
           }
         }
-        float mx = s[0];
-#pragma unroll
-        for (int e = 1; e < 128; ++e) mx = fmaxf(mx, s[e]);
-        const float m_tile = mx * sl2;
+        tr.ev(12, s_use + 1);
+        // partial max, exchanged with the partner thread of the same row
+        const float pmax = row_max64(s);
+        float* xm = xmax + (s_use & 1) * 512 + tile * 256;
+        xm[half * 128 + t] = pmax;
+        named_bar_sync(bar_id, 256);
+        const float m_tile = fmaxf(pmax, xm[(half ^ 1) * 128 + t]) * sl2;
+        ++s_use;
         bool rescale = false;
         float alpha = 1.0f;
-        if (l == 0.0f) {
+        if (m == m_init) {
           m = fmaxf(m, m_tile);
         } else if (m_tile > m + kRescaleThreshold) {
           alpha = ex2_approx(m - m_tile);
@@ -515,45 +687,65 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           m = m_tile;
           rescale = true;
         }
-        const float neg_m = -m;
-        float sum = 0.0f;
-        uint32_t pk[64];
-#pragma unroll
-        for (int e = 0; e < 128; e += 2) {
-          const float p0 = ex2_approx(fmaf(s[e], sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(s[e + 1], sl2, neg_m));
-          sum += p0 + p1;
-          pk[e >> 1] = pack_bf16x2(p0, p1);
-        }
-        l += sum;
-        tmem_st_x32(tm_s + 0, pk);
-        tmem_st_x32(tm_s + 32, pk + 32);
         if (__any_sync(0xffffffffu, rescale)) {
-          // O_tile (PV of earlier key tiles, all complete) *= alpha for this row
+          // this thread's half of the O row (P V of earlier key tiles, all complete)
+          // *= alpha, before any P of this key step is published
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
-            uint32_t orr[32];
-            tmem_ld_x32(tm_o + 32 * c, orr);
+            uint32_t orr[16];
+            tmem_ld_x16(tm_o + 16 * c, orr);
             tmem_ld_wait();
-            reg_fence32(orr);
+            reg_fence16(orr);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st_x32(tm_o + 32 * c, orr);
+            for (int e = 0; e < 16; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+            tmem_st_x16(tm_o + 16 * c, orr);
           }
         }
+        const uint64_t negm2 = f2_pack(-m, -m);
+        uint64_t acc[4] = {0, 0, 0, 0};
+        uint32_t pk[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const uint64_t x2 = f2_fma(f2_pack(s[2 * q], s[2 * q + 1]), sl2x2, negm2);
+          float p0, p1;
+          if ((q & 3) == 3) {
+            exp2_poly_pair(x2, p0, p1);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
+          pk[q] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_x32(tm_s + 32 * half, pk);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_full[tile]);
+        mbar_arrive(&p_half[2 * tile + half]);
+        tr.ev(13, s_use);
+        float a0, a1, b0, b1, c0, c1, d0, d1;
+        f2_unpack(acc[0], a0, a1);
+        f2_unpack(acc[1], b0, b1);
+        f2_unpack(acc[2], c0, c1);
+        f2_unpack(acc[3], d0, d1);
+        l += ((a0 + a1) + (b0 + b1)) + ((c0 + c1) + (d0 + d1));
       }
       if (!ok) break;
-      // epilogue: O / l -> BF16 at the row's original position, LSE in log2 units
+      // epilogue: O / l -> BF16 staged in this tile's Q buffer (free since the
+      // unit's last S MMA), then copied out with coalesced stores; LSE in log2 units.
+      tr.ev(20, s_use);
+      xsum[tile * 256 + half * 128 + t] = l;
       if (!mbar_wait(&o_full[tile], o_use & 1, abort_flag)) { ok = false; break; }
       ++o_use;
+      tr.ev(21, s_use);
+      named_bar_sync(bar_id, 256);
+      l += xsum[tile * 256 + (half ^ 1) * 128 + t];
       tc_fence_after();
       const float inv_l = 1.0f / l;
-      uint4 packed[16];
+      uint8_t* stage = smem + (tile == 0 ? SmemLayout::q0 : SmemLayout::q1) + half * kHalfBytes + t * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t orr[32];
         tmem_ld_x32(tm_o + 32 * c, orr);
         tmem_ld_wait();
@@ -561,21 +753,42 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(orr[q4 * 8 + 0]) * inv_l, __uint_as_float(orr[q4 * 8 + 1]) * inv_l);
-          w.y = pack_bf16x2(__uint_as_float(orr[q4 * 8 + 2]) * inv_l, __uint_as_float(orr[q4 * 8 + 3]) * inv_l);
-          w.z = pack_bf16x2(__uint_as_float(orr[q4 * 8 + 4]) * inv_l, __uint_as_float(orr[q4 * 8 + 5]) * inv_l);
-          w.w = pack_bf16x2(__uint_as_float(orr[q4 * 8 + 6]) * inv_l, __uint_as_float(orr[q4 * 8 + 7]) * inv_l);
-          packed[c * 4 + q4] = w;
+          w.x = pack_bf16x2(__uint_as_float(orr[8 * q4 + 0]) * inv_l, __uint_as_float(orr[8 * q4 + 1]) * inv_l);
+          w.y = pack_bf16x2(__uint_as_float(orr[8 * q4 + 2]) * inv_l, __uint_as_float(orr[8 * q4 + 3]) * inv_l);
+          w.z = pack_bf16x2(__uint_as_float(orr[8 * q4 + 4]) * inv_l, __uint_as_float(orr[8 * q4 + 5]) * inv_l);
+          w.w = pack_bf16x2(__uint_as_float(orr[8 * q4 + 6]) * inv_l, __uint_as_float(orr[8 * q4 + 7]) * inv_l);
+          const int chunk = 4 * c + q4;  // 16-byte chunk of this thread's 128-byte row half
+          *reinterpret_cast<uint4*>(stage + ((chunk ^ (t & 7)) << 4)) = w;
         }
       }
       tc_fence_before();
       mbar_arrive(&o_empty[tile]);
-      if (valid_row) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + orow * 128);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) dst[c] = packed[c];
-        p.lse[orow] = lg2_approx(l) + m;
+      int64_t* orow_tab = reinterpret_cast<int64_t*>(smem + SmemLayout::orows) + tile * 128;
+      if (half == 0) {
+        if (valid_row) p.lse[orow] = lg2_approx(l) + m;
+        orow_tab[t] = valid_row ? orow : -1;
       }
+      named_bar_sync(bar_id, 256);
+      tr.ev(23, s_use);
+      {
+        // Copy the staged tile out with coalesced 16-byte stores: warp wi of the tile
+        // writes tile rows 2m and 2m+1 (m = wi + 8k), lane L the 16-byte chunk
+        // L & 15 of row 2m + (L >> 4); a row's 256 bytes are contiguous in `out`.
+        const int wi = (grp & 1) * 4 + (warp & 3);
+        const uint8_t* tile_base = smem + (tile == 0 ? SmemLayout::q0 : SmemLayout::q1);
+        const int cidx = lane & 15;
+        const int hh = cidx >> 3;
+        const int ch = cidx & 7;
+#pragma unroll
+        for (int k2 = 0; k2 < 8; ++k2) {
+          const int row = 2 * (wi + 8 * k2) + (lane >> 4);
+          const uint4 w = *reinterpret_cast<const uint4*>(tile_base + hh * kHalfBytes + row * 128 + ((ch ^ (row & 7)) << 4));
+          const int64_t grow = orow_tab[row];
+          if (grow >= 0) *reinterpret_cast<uint4*>(p.out + grow * 128 + cidx * 8) = w;
+        }
+      }
+      mbar_arrive(&q_empty[tile]);  // all 256 threads: the producer may now refill Q_i
+      tr.ev(22, s_use);
     }
   }
 

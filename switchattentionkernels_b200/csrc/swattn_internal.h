@@ -28,7 +28,8 @@ struct __align__(64) PrefillParams {
   const int32_t* idx[2];       // routed positions per branch: [B, idx_stride]
   int idx_stride[2];
   int idx_cap[2];              // valid slots per row are < min(count, idx_cap)
-  const int32_t* counts;       // [2, B] device counts (nullable)
+  const int32_t* counts;       // device counts (nullable): counts[branch * cs_branch + b * cs_batch]
+  int cs_branch, cs_batch;
   int count_scalar[2];         // counts for B == 1 when `counts` is null
   const int32_t* starts[2];    // metadata: full_starts, local_starts (nullable)
   const int32_t* ends;         // metadata: causal_ends (nullable: fixed-length masks)

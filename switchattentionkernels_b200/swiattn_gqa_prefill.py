@@ -39,9 +39,10 @@ def switch_gqa_prefill_forward(
     num_stages: int = 2,
     threads: int = 128,
     validate: bool = True,
+    query_counts: torch.Tensor | None = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """BF16 output ``[B, Sq, Hq, 128]`` and FP32 log2-LSE ``[B, Sq, Hq]``."""
     assert block_m in (64, 128), "qualified query tiles are BM64/BM128"
     assert block_k in (64, 128), "qualified key tiles are BK64/BK128"
     return _core.forward(q, k, v, full_query_indices, local_query_indices, window_size=window_size,
-                         sm_scale=sm_scale, validate=validate)
+                         sm_scale=sm_scale, validate=validate, query_counts=query_counts)

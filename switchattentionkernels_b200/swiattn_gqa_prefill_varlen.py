@@ -61,6 +61,7 @@ def switch_gqa_prefill_forward(
     num_stages: int = 1,
     threads: int = 128,
     validate: bool = True,
+    query_counts: torch.Tensor | None = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """Run Switch Attention prefill forward.
 
@@ -69,11 +70,13 @@ def switch_gqa_prefill_forward(
     position exactly once.  Without ``metadata`` the rows use the single-sequence
     bounds (full: keys ``0..t``; local: keys ``t-W+1..t``), which is what the
     reference's default metadata encodes.  ``validate=False`` skips the index
-    range / order checks and their device-to-host read.
+    range / order checks and their device-to-host read.  ``query_counts``
+    (extension): int32 ``[B, 2]`` per-row list lengths from
+    ``build_switch_query_indices_batched``; the lists are then ``-1`` padded rows.
     """
     assert block_m == 64, "the qualified schedule is BM64"
     assert block_k == 64, "the qualified schedule is BK64"
     assert num_stages == 1, "the qualified schedule uses one stage"
     assert threads == 128, "the qualified schedule uses 128 threads"
     return _core.forward(q, k, v, full_query_indices, local_query_indices, metadata=metadata,
-                         window_size=window_size, sm_scale=sm_scale, validate=validate)
+                         window_size=window_size, sm_scale=sm_scale, validate=validate, query_counts=query_counts)

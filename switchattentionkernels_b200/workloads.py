@@ -81,13 +81,17 @@ def varlen_lengths(cfg: Config) -> np.ndarray:
 
 
 def make_inputs(cfg_id: int, *, device="cpu", p_full: float | None = None, on_device: bool = False,
-                batch_override: int | None = None):
+                batch_override: int | None = None, seed_offset: int = 0):
     """q, k, v (BF16), mask (bool [B, S]) and, for config 4, ``cu_seqlens``.
 
     ``batch_override`` draws a batch of a different size with the same recipe
-    (used for weak-scaling runs, where each GPU gets its own copy of the batch).
+    (used for weak-scaling runs, where each GPU gets its own copy of the batch);
+    ``seed_offset`` shifts the seed (one independent draw per GPU).
     """
     cfg = CONFIGS[cfg_id]
+    if seed_offset:
+        from dataclasses import replace
+        cfg = replace(cfg, seed=cfg.seed + seed_offset)
     p = cfg.p_full if p_full is None else p_full
     gen_dev = torch.device(device) if on_device else torch.device("cpu")
     g = torch.Generator(device=gen_dev).manual_seed(cfg.seed)
