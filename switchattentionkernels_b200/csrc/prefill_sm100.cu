@@ -247,21 +247,6 @@ __device__ __forceinline__ float row_max64(const float* s) {
   return fmax3(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[5]), fmaxf(u[6], u[7]));
 }
 
-__device__ __forceinline__ float row_max128(const float* s) {
-  float t[43];
-#pragma unroll
-  for (int i = 0; i < 42; ++i) t[i] = fmax3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
-  t[42] = fmaxf(s[126], s[127]);
-  float u[15];
-#pragma unroll
-  for (int i = 0; i < 14; ++i) u[i] = fmax3(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
-  u[14] = t[42];
-  float w[5];
-#pragma unroll
-  for (int i = 0; i < 5; ++i) w[i] = fmax3(u[3 * i], u[3 * i + 1], u[3 * i + 2]);
-  return fmax3(fmax3(w[0], w[1], w[2]), w[3], w[4]);
-}
-
 __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __grid_constant__ PrefillParams p) {
   if (p.gate != nullptr && *p.gate != 0) return;  // index validation failed: write nothing
 
@@ -672,9 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         tr.ev(12, s_use + 1);
         // partial max, exchanged with the partner thread of the same row
         const float pmax = row_max64(s);
+        tr.ev(14, s_use + 1);
         float* xm = xmax + (s_use & 1) * 512 + tile * 256;
         xm[half * 128 + t] = pmax;
         named_bar_sync(bar_id, 256);
+        tr.ev(15, s_use + 1);
         const float m_tile = fmaxf(pmax, xm[(half ^ 1) * 128 + t]) * sl2;
         ++s_use;
         bool rescale = false;
@@ -719,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
           pk[q] = pack_bf16x2(p0, p1);
         }
+        tr.ev(16, s_use);
         tmem_st_x32(tm_s + 32 * half, pk);
         tmem_st_wait();
         tc_fence_before();
