@@ -120,6 +120,32 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Allocation-free batched prefill.  No counterpart in the reference: it exists
+ * for callers that must not allocate device memory when they run attention --
+ * e.g. a plugin whose host framework owns all device memory and passes only
+ * input and output buffers, or a serving loop held to a fixed memory budget in
+ * which cudaMalloc (and the device synchronisation it can cause) is not allowed.
+ * Same computation as swa_prefill_forward on -1 padded [B, *_stride] index
+ * lists, including index validation, with all scratch (work counter, status
+ * words, per-row counts) kept in a 16 KB array inside the library on each GPU
+ * that loads it (held until the process exits).  Limits and behaviour:
+ *   - 1 <= B <= swa_noalloc_max_batch() (2046); larger batches get SWA_E_INVALID;
+ *   - nothing is allocated; the scratch is cleared on `stream` by every call;
+ *   - every call on a device shares that one array, so calls that can overlap on
+ *     the GPU (different streams, or a second call before the first finished on
+ *     another stream) race -- serialise them on one stream;
+ *   - the first call on a device resolves the array's device address (with that
+ *     device current); make that first call before any stream capture;
+ *   - status_out (nullable, device int32[2]) receives the validation bits
+ *     (SWA_STATUS_FULL_* / LOCAL_* / COVER; a non-zero value means nothing was
+ *     computed) and the kernel status bits (SWA_STATUS_TIMEOUT). */
+int swa_noalloc_max_batch(void);
+int swa_prefill_forward_noalloc(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                                const int32_t* local_idx, int full_stride, int local_stride,
+                                const int32_t* full_starts, const int32_t* local_starts, const int32_t* causal_ends,
+                                void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim,
+                                int window, float scale_log2, int32_t* status_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

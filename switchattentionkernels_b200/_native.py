@@ -32,6 +32,8 @@ EXPORTED = (
     "swa_check_cover",
     "swa_build_metadata",
     "swa_prefill_forward",
+    "swa_noalloc_max_batch",
+    "swa_prefill_forward_noalloc",
 )
 
 _lock = threading.Lock()
@@ -71,6 +73,18 @@ def _declare(lib) -> None:
         _i, _f,                # window, scale_log2
         _p, _p, _sz,           # gate, workspace, workspace_bytes
         _p,                    # stream
+    ]
+    lib.swa_noalloc_max_batch.restype = _i
+    lib.swa_noalloc_max_batch.argtypes = []
+    lib.swa_prefill_forward_noalloc.restype = _i
+    lib.swa_prefill_forward_noalloc.argtypes = [
+        _p, _p, _p,            # q, k, v
+        _p, _p, _i, _i,        # full_idx, local_idx, full_stride, local_stride
+        _p, _p, _p,            # full_starts, local_starts, causal_ends
+        _p, _p,                # out, lse
+        _i, _i, _i, _i, _i, _i,  # B, Sq, Skv, Hq, Hkv, head_dim
+        _i, _f,                # window, scale_log2
+        _p, _p,                # status_out, stream
     ]
 
 

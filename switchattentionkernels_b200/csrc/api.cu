@@ -23,6 +23,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace swa {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace swa
+
 extern "C" {
 
 int swa_abi_version(void) { return 1; }

@@ -49,6 +49,9 @@ struct __align__(64) PrefillParams {
 };
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);
+
+// Record the message returned by swa_last_error_string() on this thread.
+void set_last_error(const char* msg);
 uint32_t prefill_smem_bytes();
 
 cudaError_t launch_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local,
