@@ -11,34 +11,38 @@
 // tile once per group instead of once per query head and narrows the position
 // span of a tile, so the union key range wastes fewer masked entries.
 //
-// Roles (320 threads, one CTA per SM, persistent over a dynamic work counter):
+// Roles (576 threads, one CTA per SM, persistent over a dynamic work counter):
 //   warp 0      producer : takes work units from the global counter (one unit
 //                          ahead) and publishes them through a shared-memory ring;
 //                          TMA Q gather (one box per routed position, the next
 //                          unit's boxes prefetched into L2 one unit ahead) and the
-//                          K/V tile ring (5 stages of 128 keys x 128 dims)
-//   warp 1      MMA      : one thread issues tcgen05.mma
+//                          K/V tile ring (4 entries of 128 keys x 128 dims, K and V
+//                          tiles alternating)
+//   warp 1      MMA      : one elected lane issues tcgen05.mma in groups of eight
+//                          (S) or four (P V) instructions:
 //                          S_i = Q_i K^T (SS, K-major) and O_i += P_i V (TS: P in TMEM,
 //                          V MN-major), commits to mbarriers.  Its issue order is one
-//                          continuous stream over key steps; at a unit boundary the
-//                          next unit's first S MMAs follow the last P V MMAs exactly
-//                          like the next key step inside a unit, so the tensor pipe
-//                          does not drain between units.
-//   warps 2-5   softmax 0: rows 0..127   (TMEM lane = row), then the O/LSE epilogue
-//   warps 6-9   softmax 1: rows 128..255
+//                          continuous stream over key steps: PV_0(j), S_0(j+1),
+//                          PV_1(j), S_1(j+1); at a unit's last step both P V groups
+//                          go first, then the next unit's S MMAs.
+//   warps 2-17  softmax  : four warpgroups; tile = (warp - 2) / 8 (rows 0..127 or
+//                          128..255 of the unit, TMEM lane = row), key half =
+//                          ((warp - 2) / 4) % 2 (keys [64 h, 64 h + 64) of each key
+//                          tile and O columns [64 h, 64 h + 64)); then the O/LSE
+//                          epilogue of the tile.
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs)
 // overwrites the first 64 columns of S_i and is consumed by the next PV MMA.  P is
-// published in two halves of 64 keys so the PV MMAs of the first half start while
-// the second half is still being exponentiated.
+// published in two halves of 64 keys (one per key-half warpgroup).
+// Key tiles of a unit start at the 64-aligned key at or below its first legal key.
 //
 // Numerics follow the reference: FP32 scores, log2-domain online softmax with
 // scale_log2 = sm_scale * log2(e), running max initialised to -2^30 (scaled),
 // P rounded to BF16 before P V, the row sum accumulated from the unrounded FP32
 // P, O = acc / l and LSE = log2(l) + m.  The running max is only raised (and O
 // rescaled) when it grows by more than 8 (a factor 256), which leaves the final
-// O and LSE mathematically unchanged while removing most O rescales.  Every other
-// pair of exponentials is evaluated on the FMA pipe (exp2_poly_pair) instead of the
-// MUFU unit, which otherwise bounds the softmax rate.
+// O and LSE mathematically unchanged while removing most O rescales.  One pair of
+// exponentials in four is evaluated on the FMA pipe (exp2_poly_pair) instead of
+// the MUFU unit, which otherwise bounds the softmax rate.
 #include "sm100.cuh"
 #include "swattn_internal.h"
 
@@ -59,7 +63,7 @@ struct Unit {
   int branch;   // 0 = full, 1 = local
   int b, g, hb, pb;
   int count;    // routed rows of this (branch, b)
-  int j0, n;    // first key tile and number of key tiles
+  int j0, n;    // first key (a multiple of 64) / 64, and number of 128-key tiles from there
   int pad[7];
 };
 
@@ -179,8 +183,10 @@ __device__ bool decode_item(const PrefillParams& p, int it, int nf, int maxnpb0,
     lo = branch ? max(fpos - p.window + 1, 0) : 0;
     hi = min(lpos + 1, p.Skv);
   }
-  const int j0 = lo / kBK;
-  const int j1 = (hi + kBK - 1) / kBK;
+  // key tiles start at the 64-aligned key at or below lo (a 128-key grid would
+  // waste up to 64 more masked keys per row)
+  const int j0 = lo / 64;
+  const int j1 = j0 + (hi - j0 * 64 + kBK - 1) / kBK;
   u.valid = 1;
   u.branch = branch;
   u.b = b;
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           if (lane < 2) {
             uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes + lane * kHalfBytes;
             const CUtensorMap* map = kv == 0 ? &p.k_map : &p.v_map;
-            tma_load_4d(dst, map, &kv_full[s], lane * 64, u.g, (u.j0 + j) * kBK, u.b);
+            tma_load_4d(dst, map, &kv_full[s], lane * 64, u.g, u.j0 * 64 + j * kBK, u.b);
           }
           __syncwarp();
           ++kv_it;
@@ -459,27 +465,23 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (u.n > 0) return true;
       }
     };
+    // Descriptors are built once; a ring entry's descriptor is the base plus the
+    // entry offset in the 14-bit start-address field (bytes >> 4).
+    const uint64_t q_desc[2] = {make_smem_desc_sw128(q_addr[0], 16, 1024), make_smem_desc_sw128(q_addr[1], 16, 1024)};
+    const uint64_t k_desc0 = make_smem_desc_sw128(kv_addr, 16, 1024);
+    const uint64_t v_desc0 = make_smem_desc_sw128(kv_addr, kHalfBytes, 1024);
     auto issue_s = [&](int i, uint32_t kstage) {
-      const uint32_t kb = kv_addr + kstage * kTileBytes;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-        umma_ss_warp(tm_s[i], make_smem_desc_sw128(q_addr[i] + off, 16, 1024),
-                     make_smem_desc_sw128(kb + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-      }
+      umma_ss_k128_warp(tm_s[i], q_desc[i], k_desc0 + kstage * (kTileBytes >> 4), idesc_s);
     };
     // P V for one tile, in two halves of 64 keys gated by the softmax's half barriers.
     auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) -> bool {
-      const uint32_t vb = kv_addr + vstage * kTileBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         if (!mbar_wait(&p_half[2 * i + h], p_use[i] & 1, abort_flag)) { ok = false; return false; }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-          umma_ts_warp(tm_o[i], tm_s[i] + kk * 8, make_smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), idesc_o,
-                       (accumulate || kk > 0) ? 1u : 0u);
-        }
+        // keys [64 h, 64 h + 64): P columns [32 h, +32), V rows at byte offset 8192 h
+        umma_ts_k64_warp(tm_o[i], tm_s[i] + 32 * h, v_desc0 + vstage * (kTileBytes >> 4) + h * (8192 >> 4), idesc_o,
+                         (accumulate || h > 0) ? 1u : 0u);
       }
       ++p_use[i];
       return true;
@@ -646,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         reg_fence32(sr + 0);
         reg_fence32(sr + 32);
         float* s = reinterpret_cast<float*>(sr);
-        const int k0 = (u.j0 + j) * kBK + 64 * half;
+        const int k0 = u.j0 * 64 + j * kBK + 64 * half;
         if (!(rb.lo <= k0 && k0 + 64 <= rb.hi)) {
 #pragma unroll
           for (int e = 0; e < 64; ++e) {

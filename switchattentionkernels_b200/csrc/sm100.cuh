@@ -218,6 +218,52 @@ __device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
       : "memory");
 }
 
+// Eight back-to-back SS MMAs over K = 128 (two 64-column swizzled halves, four
+// 16-element steps each) with a single elected issuing lane.  a_desc / b_desc are
+// the descriptors of the first step; step kk adds ((kk / 4) * 16384 + (kk % 4) * 32)
+// bytes to both start addresses (start-address field = bytes >> 4, no carry out of
+// its 14 bits for shared-memory addresses).  The first step overwrites D.
+__device__ __forceinline__ void umma_ss_k128_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, p1;\n\t.reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n\t"
+      "setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\tadd.s64 a4, %1, 1024;\n\t"
+      "add.s64 a5, %1, 1026;\n\tadd.s64 a6, %1, 1028;\n\tadd.s64 a7, %1, 1030;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\tadd.s64 b4, %2, 1024;\n\t"
+      "add.s64 b5, %2, 1026;\n\tadd.s64 b6, %2, 1028;\n\tadd.s64 b7, %2, 1030;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+
+// Four back-to-back TS MMAs over 64 keys: A = P from TMEM (8 columns per 16 keys),
+// B = V MN-major (2048 bytes per 16 keys).  `accumulate_first` = 0 makes the first
+// step overwrite D.
+__device__ __forceinline__ void umma_ts_k64_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate_first) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, p1;\n\t.reg .b64 b1, b2, b3;\n\t.reg .b32 t1, t2, t3;\n\t"
+      "setp.ne.b32 pf, %4, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "add.s64 b1, %2, 128;\n\tadd.s64 b2, %2, 256;\n\tadd.s64 b3, %2, 384;\n\t"
+      "add.u32 t1, %1, 8;\n\tadd.u32 t2, %1, 16;\n\tadd.u32 t3, %1, 24;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, p1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate_first)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm100 version field = 1.
 //   K-major operand : lbo ignored (pass 16), sbo = byte stride between 8-row groups.
 //   MN-major operand: lbo = byte stride between 64-element MN blocks,
