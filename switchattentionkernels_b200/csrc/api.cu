@@ -139,6 +139,17 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
     const uint64_t qs[1] = {256};
     const uint32_t qb[2] = {64, static_cast<uint32_t>(rp < 128 ? rp : 128)};
     if (!swa::make_bf16_map_sw128(&p.q_map, q, 2, qd, qs, qb)) return fail(SWA_E_TMA, "q tensor map");
+    // runs of consecutive routed positions: one box covers 2^(L+1) positions x rp heads
+    p.n_q3 = 0;
+    if (rp <= 64) {
+      const uint64_t q3d[3] = {128, static_cast<uint64_t>(Hq), static_cast<uint64_t>(B) * Sq};
+      const uint64_t q3s[2] = {256, static_cast<uint64_t>(Hq) * 256};
+      for (int npos = 2; npos * rp <= 128 && p.n_q3 < swa::kMaxQRunMaps; npos *= 2) {
+        const uint32_t q3b[3] = {64, static_cast<uint32_t>(rp), static_cast<uint32_t>(npos)};
+        if (!swa::make_bf16_map_sw128(&p.q_runs[p.n_q3], q, 3, q3d, q3s, q3b)) return fail(SWA_E_TMA, "q run tensor map");
+        ++p.n_q3;
+      }
+    }
     const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Skv), static_cast<uint64_t>(B)};
     const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Skv) * Hkv * 256};
     const uint32_t kb[4] = {64, 1, 128, 1};

@@ -84,7 +84,8 @@ struct SmemLayout {
   static constexpr int b_p_half = b_s_full + 2;    // [tile][half]
   static constexpr int b_o_full = b_p_half + 4;
   static constexpr int b_o_empty = b_o_full + 2;
-  static constexpr int b_drain = b_o_empty + 2;
+  static constexpr int b_stage_free = b_o_empty + 2;  // [tile]: the staging slot is this tile's turn
+  static constexpr int b_drain = b_stage_free + 2;
   static constexpr int n_bars = b_drain + 1;
   static constexpr uint32_t units = bars + ((n_bars * 8 + 63) / 64) * 64;
   static constexpr uint32_t misc = units + kSchedSlots * sizeof(Unit);
@@ -92,7 +93,10 @@ struct SmemLayout {
   // exchange [2 tile][2 half][128] floats (2 KB)
   static constexpr uint32_t xchg = misc + 64;
   static constexpr uint32_t orows = xchg + 4096 + 2048;  // output row offsets [2 tile][128] int64 (2 KB)
-  static constexpr uint32_t total = orows + 2048;
+  // epilogue staging slot: 128 rows x 64 output columns (BF16), shared by the two
+  // tiles in turn, so that the Q buffers are free as soon as a unit's last S MMA is
+  static constexpr uint32_t stage = ((orows + 2048 + 1023) / 1024) * 1024;
+  static constexpr uint32_t total = stage + kHalfBytes;
 };
 
 constexpr uint32_t kSmemBytes = SmemLayout::total + 1024;  // + alignment slack
@@ -128,6 +132,12 @@ struct Tracer {
   __device__ explicit Tracer(int) {}
   __device__ __forceinline__ void ev(int, int) {}
 };
+#endif
+
+// Optional per-CTA duration in SM clock cycles (compiled only with -DSWA_CYCLES),
+// for comparing kernel variants independently of the clock frequency.
+#ifdef SWA_CYCLES
+__device__ unsigned long long g_swa_cycles[1024];
 #endif
 
 __device__ __forceinline__ RowBounds row_bounds(const PrefillParams& p, int branch, int qpos) {
@@ -211,6 +221,74 @@ __device__ __forceinline__ void read_unit(const volatile Unit* src, Unit& u) {
   u.n = src->n;
 }
 
+// TMA boxes of Q tile i (rows 128 i .. 128 i + 127) of unit u, issued by the
+// producer warp's lanes: loads into `qdst` (completing on `bar`) or, with
+// qdst == nullptr, L2 prefetches.  With rp <= 64 a tile holds spt = 128 / rp
+// routed positions (slots); each slot s is covered by the largest aligned
+// power-of-two block of slots containing it whose positions are consecutive, and
+// such a block of 2^L slots is one box of 2^L positions x rp heads (3-D map
+// q_runs[L - 1]), or of rp rows (2-D map) for a single slot.  Blocks of
+// consecutive positions contain sub-blocks of consecutive positions, so these
+// maximal blocks partition the slots and every row is loaded exactly once.
+__device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit& u, int i, int lane, uint8_t* qdst,
+                                             uint64_t* bar) {
+  const int head0 = u.g * (p.Hq / p.Hkv) + u.hb * p.rp;
+  if (p.rp > 64) {
+    // at most one position per tile: boxes of boxh rows (rp = 128: one box per half;
+    // rp = 256: tile i holds heads [128 i, 128 i + 128) of the unit's position)
+    const int boxes = 128 / p.boxh;
+    for (int t = lane; t < 2 * boxes; t += 32) {
+      const int half = t & 1;
+      const int bx = t >> 1;
+      const int row0 = 128 * i + bx * p.boxh;
+      const int slot_abs = min(u.pb * p.pc + row0 / p.rp, u.count - 1);
+      const int pos = min(max(load_pos(p, u.branch, u.b, slot_abs), 0), p.Sq - 1);
+      const int row = (u.b * p.Sq + pos) * p.Hq + head0 + row0 % p.rp;
+      if (qdst != nullptr) {
+        tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, bar, half * 64, row);
+      } else {
+        tma_prefetch_l2_2d(&p.q_map, half * 64, row);
+      }
+    }
+    return;
+  }
+  const int spt = 128 / p.rp;
+  const int base = u.pb * p.pc + i * spt;  // absolute slot of the tile's first row
+  auto pos_of = [&](int s) {
+    return min(max(load_pos(p, u.branch, u.b, min(base + s, u.count - 1)), 0), p.Sq - 1);
+  };
+  for (int s = lane; s < spt; s += 32) {
+    int lev = 0;
+    for (int L = p.n_q3; L >= 1; --L) {
+      const int b0 = s & ~((1 << L) - 1);
+      const int b1 = b0 + (1 << L) - 1;
+      // all slots of the block routed (no clamped repeats) and positions consecutive
+      if (base + b1 < u.count && pos_of(b1) - pos_of(b0) == (1 << L) - 1) {
+        lev = L;
+        break;
+      }
+    }
+    if ((s & ((1 << lev) - 1)) != 0) continue;  // not the first slot of its block
+    const int pos = pos_of(s);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      if (lev == 0) {
+        const int row = (u.b * p.Sq + pos) * p.Hq + head0;
+        if (qdst != nullptr) {
+          tma_load_2d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_map, bar, half * 64, row);
+        } else {
+          tma_prefetch_l2_2d(&p.q_map, half * 64, row);
+        }
+      } else if (qdst != nullptr) {
+        tma_load_3d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_runs[lev - 1], bar, half * 64, head0,
+                    u.b * p.Sq + pos);
+      } else {
+        tma_prefetch_l2_3d(&p.q_runs[lev - 1], half * 64, head0, u.b * p.Sq + pos);
+      }
+    }
+  }
+}
+
 // 2^x for a pair of arguments on the FMA pipe.  Cody-Waite style range
 // reduction x = j + f with j = round(x) (the 1.5 * 2^23 shifter), f in
 // [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted for minimum maximal relative
@@ -255,6 +333,9 @@ __device__ __forceinline__ float row_max64(const float* s) {
 
 __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __grid_constant__ PrefillParams p) {
   if (p.gate != nullptr && *p.gate != 0) return;  // index validation failed: write nothing
+#ifdef SWA_CYCLES
+  const unsigned long long cycles_start = clock64();
+#endif
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
@@ -274,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   uint64_t* p_half = bars + SmemLayout::b_p_half;
   uint64_t* o_full = bars + SmemLayout::b_o_full;
   uint64_t* o_empty = bars + SmemLayout::b_o_empty;
+  uint64_t* stage_free = bars + SmemLayout::b_stage_free;
   uint64_t* drain = bars + SmemLayout::b_drain;
 
   const int warp = threadIdx.x >> 5;
@@ -286,12 +368,13 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 256);
+      mbar_init(&q_empty[i], 1);  // committed after the unit's last S MMA of tile i
       mbar_init(&s_full[i], 1);
       mbar_init(&p_half[2 * i], 128);
       mbar_init(&p_half[2 * i + 1], 128);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 256);
+      mbar_init(&stage_free[i], 256);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -340,8 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     };
     uint32_t kv_it = 0;
     uint32_t q_use[2] = {0, 0};
-    const int r = p.Hq / p.Hkv;
-    const int boxes = 128 / p.boxh;  // boxes per tile per 64-column half
     Unit u;
     fetch(u);
     for (int k = 0;; ++k) {
@@ -366,16 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       __syncwarp();
       if (!u.valid) break;
       if (un.valid && un.n > 0) {
-        // Prefetch the next unit's Q boxes into L2 so its gather (issued only once
-        // this unit's last S MMA has freed the Q buffers) hits L2.
-        for (int t = lane; t < 2 * 2 * boxes; t += 32) {
-          const int half = t & 1;
-          const int row0 = (t >> 1) * p.boxh;  // over both tiles
-          const int slot_abs = min(un.pb * p.pc + row0 / p.rp, un.count - 1);
-          const int pos = min(max(load_pos(p, un.branch, un.b, slot_abs), 0), p.Sq - 1);
-          const int row = (un.b * p.Sq + pos) * p.Hq + un.g * r + un.hb * p.rp + row0 % p.rp;
-          tma_prefetch_l2_2d(&p.q_map, half * 64, row);
-        }
+        // Prefetch the next unit's Q boxes into L2 so its gather (issued once this
+        // unit's last S MMAs have freed the Q buffers) hits L2.
+        q_tile_boxes(p, un, 0, lane, nullptr, nullptr);
+        q_tile_boxes(p, un, 1, lane, nullptr, nullptr);
       }
       bool ok = true;
       if (u.n > 0) {
@@ -395,23 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           return true;
         };
         auto load_q = [&](int i) -> bool {
-          // Q_i is free once the previous unit's epilogue has stored its output from it
+          // Q_i is free once the previous unit's last S MMA of tile i has completed
           if (!mbar_wait(&q_empty[i], (q_use[i] & 1) ^ 1, abort_flag)) return false;
           ++q_use[i];
           if (lane == 0) mbar_arrive_expect_tx(&q_full[i], kTileBytes);
           __syncwarp();
-          uint8_t* qdst = smem + (i == 0 ? SmemLayout::q0 : SmemLayout::q1);
-          for (int t = lane; t < 2 * boxes; t += 32) {
-            const int half = t & 1;
-            const int bx = t >> 1;
-            const int row0 = 128 * i + bx * p.boxh;          // first unit row of this box
-            const int slot_in_unit = row0 / p.rp;
-            const int hoff = row0 % p.rp;
-            const int slot_abs = min(u.pb * p.pc + slot_in_unit, u.count - 1);
-            const int pos = min(max(load_pos(p, u.branch, u.b, slot_abs), 0), p.Sq - 1);
-            const int row = (u.b * p.Sq + pos) * p.Hq + u.g * r + u.hb * p.rp + hoff;
-            tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, &q_full[i], half * 64, row);
-          }
+          q_tile_boxes(p, u, i, lane, smem + (i == 0 ? SmemLayout::q0 : SmemLayout::q1), &q_full[i]);
           return true;
         };
         // ring order K_0, V_0, K_1, V_1, ...; the Q tiles go between K_0 and V_0 so
@@ -486,11 +550,12 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       ++p_use[i];
       return true;
     };
-    // S MMAs of one key step for tile i.  (Q_i is released by the epilogue, which
-    // stages the tile's output rows in the Q_i buffer once the last S MMA is done.)
-    auto issue_s_step = [&](int i, uint32_t kstage) {
+    // S MMAs of one key step for tile i; after the unit's last one, Q_i is released
+    // to the producer (the commit arrives once these MMAs have read it).
+    auto issue_s_step = [&](int i, uint32_t kstage, bool last_of_unit) {
       issue_s(i, kstage);
       tc_commit_warp(&s_full[i]);
+      if (last_of_unit) tc_commit_warp(&q_empty[i]);
     };
 
     Unit cur;
@@ -502,13 +567,13 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       if (ok) {
         ++q_use[0];
         tc_fence_after();
-        issue_s_step(0, ks);
+        issue_s_step(0, ks, cur.n == 1);
       }
       ok = ok && mbar_wait(&q_full[1], q_use[1] & 1, abort_flag);
       if (ok) {
         ++q_use[1];
         tc_fence_after();
-        issue_s_step(1, ks);
+        issue_s_step(1, ks, cur.n == 1);
         tc_commit_warp(&kv_empty[ks]);
         ++kv_it;
       }
@@ -517,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     while (have && ok) {
       // invariant: S_0(j), S_1(j) of `cur` are issued.  Inside a unit the order is
       // PV_0(j), S_0(j+1), PV_1(j), S_1(j+1); at a unit's last step both P V MMAs go
-      // first, then the next unit's S MMAs (their Q tiles arrive only after this
-      // unit's epilogue has stored its output through the Q buffers).
+      // first, then the next unit's S MMAs (S_i(0) overwrites the columns that hold
+      // P_i of this step).
       const bool last = j == cur.n - 1;
       const uint32_t vs = kv_it % kStages;
       tr.ev(1, step);
@@ -540,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         ++kv_it;
         tc_fence_after();
         tr.ev(4, step);
-        issue_s_step(0, ks);
+        issue_s_step(0, ks, j + 1 == cur.n - 1);
       }
       if (j == 0) {
         if (!mbar_wait(&o_empty[1], (o_use[1] & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -550,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       tr.ev(5, step);
       tc_commit_warp(&kv_empty[vs]);
       if (!last) {
-        issue_s_step(1, ks);
+        issue_s_step(1, ks, j + 1 == cur.n - 1);
         tc_commit_warp(&kv_empty[ks]);
         ++j;
       } else {
@@ -564,11 +629,11 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (!mbar_wait(&kv_full[k0s], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
         ++kv_it;
         tc_fence_after();
-        issue_s_step(0, k0s);
+        issue_s_step(0, k0s, cur.n == 1);
         if (!mbar_wait(&q_full[1], q_use[1] & 1, abort_flag)) { ok = false; break; }
         ++q_use[1];
         tc_fence_after();
-        issue_s_step(1, k0s);
+        issue_s_step(1, k0s, cur.n == 1);
         tc_commit_warp(&kv_empty[k0s]);
       }
       tr.ev(6, step);
@@ -722,62 +787,69 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         l += ((a0 + a1) + (b0 + b1)) + ((c0 + c1) + (d0 + d1));
       }
       if (!ok) break;
-      // epilogue: O / l -> BF16 staged in this tile's Q buffer (free since the
-      // unit's last S MMA), then copied out with coalesced stores; LSE in log2 units.
+      // epilogue: O / l -> BF16 through the shared staging slot, 64 columns per
+      // round (round h: the key-half-h warpgroup stages its columns, then the
+      // tile's eight warps copy them out with coalesced stores); LSE in log2 units.
       tr.ev(20, s_use);
       xsum[tile * 256 + half * 128 + t] = l;
       if (!mbar_wait(&o_full[tile], o_use & 1, abort_flag)) { ok = false; break; }
-      ++o_use;
       tr.ev(21, s_use);
       named_bar_sync(bar_id, 256);
       l += xsum[tile * 256 + (half ^ 1) * 128 + t];
-      tc_fence_after();
       const float inv_l = 1.0f / l;
-      uint8_t* stage = smem + (tile == 0 ? SmemLayout::q0 : SmemLayout::q1) + half * kHalfBytes + t * 128;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t orr[32];
-        tmem_ld_x32(tm_o + 32 * c, orr);
-        tmem_ld_wait();
-        reg_fence32(orr);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(orr[8 * q4 + 0]) * inv_l, __uint_as_float(orr[8 * q4 + 1]) * inv_l);
-          w.y = pack_bf16x2(__uint_as_float(orr[8 * q4 + 2]) * inv_l, __uint_as_float(orr[8 * q4 + 3]) * inv_l);
-          w.z = pack_bf16x2(__uint_as_float(orr[8 * q4 + 4]) * inv_l, __uint_as_float(orr[8 * q4 + 5]) * inv_l);
-          w.w = pack_bf16x2(__uint_as_float(orr[8 * q4 + 6]) * inv_l, __uint_as_float(orr[8 * q4 + 7]) * inv_l);
-          const int chunk = 4 * c + q4;  // 16-byte chunk of this thread's 128-byte row half
-          *reinterpret_cast<uint4*>(stage + ((chunk ^ (t & 7)) << 4)) = w;
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&o_empty[tile]);
       int64_t* orow_tab = reinterpret_cast<int64_t*>(smem + SmemLayout::orows) + tile * 128;
       if (half == 0) {
         if (valid_row) p.lse[orow] = lg2_approx(l) + m;
         orow_tab[t] = valid_row ? orow : -1;
       }
-      named_bar_sync(bar_id, 256);
-      tr.ev(23, s_use);
-      {
-        // Copy the staged tile out with coalesced 16-byte stores: warp wi of the tile
-        // writes tile rows 2m and 2m+1 (m = wi + 8k), lane L the 16-byte chunk
-        // L & 15 of row 2m + (L >> 4); a row's 256 bytes are contiguous in `out`.
-        const int wi = (grp & 1) * 4 + (warp & 3);
-        const uint8_t* tile_base = smem + (tile == 0 ? SmemLayout::q0 : SmemLayout::q1);
-        const int cidx = lane & 15;
-        const int hh = cidx >> 3;
-        const int ch = cidx & 7;
+      // the slot alternates tile 0, tile 1, tile 0, ... (one turn per unit each)
+      if (!mbar_wait(&stage_free[tile], (o_use & 1) ^ (tile == 0 ? 1u : 0u), abort_flag)) { ok = false; break; }
+      ++o_use;
+      uint8_t* stg = smem + SmemLayout::stage;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        if (half == h) {
+          tc_fence_after();
+          uint8_t* srow = stg + t * 128;
 #pragma unroll
-        for (int k2 = 0; k2 < 8; ++k2) {
-          const int row = 2 * (wi + 8 * k2) + (lane >> 4);
-          const uint4 w = *reinterpret_cast<const uint4*>(tile_base + hh * kHalfBytes + row * 128 + ((ch ^ (row & 7)) << 4));
-          const int64_t grow = orow_tab[row];
-          if (grow >= 0) *reinterpret_cast<uint4*>(p.out + grow * 128 + cidx * 8) = w;
+          for (int c = 0; c < 2; ++c) {
+            uint32_t orr[32];
+            tmem_ld_x32(tm_o + 32 * c, orr);
+            tmem_ld_wait();
+            reg_fence32(orr);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(orr[8 * q4 + 0]) * inv_l, __uint_as_float(orr[8 * q4 + 1]) * inv_l);
+              w.y = pack_bf16x2(__uint_as_float(orr[8 * q4 + 2]) * inv_l, __uint_as_float(orr[8 * q4 + 3]) * inv_l);
+              w.z = pack_bf16x2(__uint_as_float(orr[8 * q4 + 4]) * inv_l, __uint_as_float(orr[8 * q4 + 5]) * inv_l);
+              w.w = pack_bf16x2(__uint_as_float(orr[8 * q4 + 6]) * inv_l, __uint_as_float(orr[8 * q4 + 7]) * inv_l);
+              const int chunk = 4 * c + q4;  // 16-byte chunk of this thread's 128-byte row half
+              *reinterpret_cast<uint4*>(srow + ((chunk ^ (t & 7)) << 4)) = w;
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&o_empty[tile]);
         }
+        named_bar_sync(bar_id, 256);
+        tr.ev(23, s_use);
+        {
+          // 1024 16-byte chunks (128 rows x 8): warp wi of the tile copies chunks
+          // [32 (wi + 8 k), +32) = rows 4 (wi + 8 k) .. +3, lane L chunk L & 7 of
+          // row 4 (wi + 8 k) + (L >> 3); each row half is 128 contiguous bytes of `out`.
+          const int wi = (grp & 1) * 4 + (warp & 3);
+          const int ch = lane & 7;
+#pragma unroll
+          for (int k2 = 0; k2 < 4; ++k2) {
+            const int row = 4 * (wi + 8 * k2) + (lane >> 3);
+            const uint4 w = *reinterpret_cast<const uint4*>(stg + row * 128 + ((ch ^ (row & 7)) << 4));
+            const int64_t grow = orow_tab[row];
+            if (grow >= 0) *reinterpret_cast<uint4*>(p.out + grow * 128 + 64 * h + ch * 8) = w;
+          }
+        }
+        if (h == 0) named_bar_sync(bar_id, 256);  // slot read before round 1 refills it
       }
-      mbar_arrive(&q_empty[tile]);  // all 256 threads: the producer may now refill Q_i
+      mbar_arrive(&stage_free[tile ^ 1]);  // all 256 threads: the other tile's turn
       tr.ev(22, s_use);
     }
   }
@@ -790,6 +862,9 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(p.status, kStatusTimeout);
+#ifdef SWA_CYCLES
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_swa_cycles[blockIdx.x] = clock64() - cycles_start;
+#endif
 }
 
 }  // namespace
@@ -809,5 +884,12 @@ cudaError_t launch_prefill(const PrefillParams& params, int num_sms, cudaStream_
 }
 
 uint32_t prefill_smem_bytes() { return kSmemBytes; }
+
+#ifdef SWA_CYCLES
+// Copies the per-CTA cycle counts of the last launch (n <= 1024) to host memory.
+extern "C" int swa_dev_cycles(unsigned long long* host, int n) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_swa_cycles, sizeof(unsigned long long) * n));
+}
+#endif
 
 }  // namespace swa

@@ -21,8 +21,14 @@ enum : int32_t {
   kStatusTimeout = 1 << 16,    // a device-side wait exceeded its limit
 };
 
+constexpr int kMaxQRunMaps = 7;
+
 struct __align__(64) PrefillParams {
   CUtensorMap q_map;  // 2-D {128, B*Sq*Hq}, box {64, boxh}, 128B swizzle
+  // 3-D {128, Hq, B*Sq} views of q with box {64, rp, 2^(L+1)}: 2^(L+1) consecutive
+  // positions x rp heads in one TMA box (L < n_q3; n_q3 = log2(128 / rp), rp <= 64)
+  CUtensorMap q_runs[kMaxQRunMaps];
+  int n_q3;
   CUtensorMap k_map;  // 4-D {128, Hkv, Skv, B}, box {64, 1, 128, 1}, 128B swizzle
   CUtensorMap v_map;
   const int32_t* idx[2];       // routed positions per branch: [B, idx_stride]
