@@ -49,7 +49,7 @@ FALLBACK_PEAK_TFLOPS = 1590.0
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
@@ -95,7 +95,7 @@ def profile_traffic(workload: str):
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -108,10 +108,20 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait (at most 5 s) for its first sample so
+        # that the samples cover the timed region that follows
+        deadline = time.time() + 5.0
+        while time.time() < deadline and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
+
+    def mark(self, which: str):
+        """Wall-clock bounds of the timed region; only samples inside it are kept."""
+        setattr(self, which, datetime.datetime.now())
 
     def stop(self):
         if self.proc is None:
@@ -124,19 +134,30 @@ class ClockSampler:
         self.fh.close()
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        t_begin = getattr(self, "begin", None)
+        t_end = getattr(self, "end", None)
+        rows = []
         with open(self.path) as fh:
             for line in fh:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
                     continue
                 try:
-                    sms.append(float(parts[1]))
-                    maxes.append(float(parts[2]))
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
                 except ValueError:
-                    continue
-                for name, val in zip(names, parts[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(name)
+                    ts = None
+                rows.append((ts, parts))
+        inside = [r for r in rows if r[0] is not None and t_begin is not None and t_end is not None
+                  and t_begin <= r[0] <= t_end]
+        for _, parts in (inside or rows):  # all samples if the timestamps cannot be matched
+            try:
+                sms.append(float(parts[2]))
+                maxes.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
         os.unlink(self.path)
         if not sms:
             return None
@@ -271,6 +292,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     clocks.start()
+    clocks.mark("begin")
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -278,6 +300,7 @@ def main():
         step(record=True)
     t1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark("end")
     barrier()
     clock_info = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
