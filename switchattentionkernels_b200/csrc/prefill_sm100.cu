@@ -32,7 +32,7 @@
 //                          epilogue of the tile.
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs)
 // overwrites the first 64 columns of S_i and is consumed by the next PV MMA.  P is
-// published in two halves of 64 keys (one per key-half warpgroup).
+// published in two chunks (keys [32 c, +32) of each key half, c = 0, 1).
 // Key tiles of a unit start at the 64-aligned key at or below its first legal key.
 //
 // Numerics follow the reference: FP32 scores, log2-domain online softmax with
@@ -81,8 +81,8 @@ struct SmemLayout {
   static constexpr int b_kv_full = b_q_empty + 2;
   static constexpr int b_kv_empty = b_kv_full + kStages;
   static constexpr int b_s_full = b_kv_empty + kStages;
-  static constexpr int b_p_half = b_s_full + 2;    // [tile][half]
-  static constexpr int b_o_full = b_p_half + 4;
+  static constexpr int b_p_chunk = b_s_full + 2;   // [tile][key chunk]
+  static constexpr int b_o_full = b_p_chunk + 4;
   static constexpr int b_o_empty = b_o_full + 2;
   static constexpr int b_stage_free = b_o_empty + 2;  // [tile]: the staging slot is this tile's turn
   static constexpr int b_drain = b_stage_free + 2;
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   uint64_t* kv_full = bars + SmemLayout::b_kv_full;
   uint64_t* kv_empty = bars + SmemLayout::b_kv_empty;
   uint64_t* s_full = bars + SmemLayout::b_s_full;
-  uint64_t* p_half = bars + SmemLayout::b_p_half;
+  uint64_t* p_chunk = bars + SmemLayout::b_p_chunk;
   uint64_t* o_full = bars + SmemLayout::b_o_full;
   uint64_t* o_empty = bars + SmemLayout::b_o_empty;
   uint64_t* stage_free = bars + SmemLayout::b_stage_free;
@@ -370,8 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);  // committed after the unit's last S MMA of tile i
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_half[2 * i], 128);
-      mbar_init(&p_half[2 * i + 1], 128);
+      mbar_init(&p_chunk[2 * i], 256);
+      mbar_init(&p_chunk[2 * i + 1], 256);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 256);
       mbar_init(&stage_free[i], 256);
@@ -538,14 +538,17 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       umma_ss_k128_warp(tm_s[i], q_desc[i], k_desc0 + kstage * (kTileBytes >> 4), idesc_s);
     };
     // P V for one tile, in two halves of 64 keys gated by the softmax's half barriers.
+    // P V for one tile in two chunks: chunk c covers keys [32 c, +32) of each key
+    // half (keys 64 h + 32 c .. +31: P columns 32 h + 16 c .., V rows 2048-byte
+    // steps 4 h + 2 c ..), published by the softmax before it exponentiates chunk c + 1.
     auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) -> bool {
+      const uint64_t vb = v_desc0 + vstage * (kTileBytes >> 4);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!mbar_wait(&p_half[2 * i + h], p_use[i] & 1, abort_flag)) { ok = false; return false; }
+      for (int c = 0; c < 2; ++c) {
+        if (!mbar_wait(&p_chunk[2 * i + c], p_use[i] & 1, abort_flag)) { ok = false; return false; }
         tc_fence_after();
-        // keys [64 h, 64 h + 64): P columns [32 h, +32), V rows at byte offset 8192 h
-        umma_ts_k64_warp(tm_o[i], tm_s[i] + 32 * h, v_desc0 + vstage * (kTileBytes >> 4) + h * (8192 >> 4), idesc_o,
-                         (accumulate || h > 0) ? 1u : 0u);
+        umma_ts_k32_warp(tm_o[i], tm_s[i] + 16 * c, vb + (2 * c) * 128, idesc_o, (accumulate || c > 0) ? 1u : 0u);
+        umma_ts_k32_warp(tm_o[i], tm_s[i] + 32 + 16 * c, vb + (4 + 2 * c) * 128, idesc_o, 1u);
       }
       ++p_use[i];
       return true;
@@ -757,27 +760,33 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         }
         const uint64_t negm2 = f2_pack(-m, -m);
         uint64_t acc[4] = {0, 0, 0, 0};
-        uint32_t pk[32];
+        // two chunks of 32 keys; each is published as soon as it is in TMEM, so the
+        // P V MMAs of chunk 0 run while chunk 1 is exponentiated
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const uint64_t x2 = f2_fma(f2_pack(s[2 * q], s[2 * q + 1]), sl2x2, negm2);
-          float p0, p1;
-          if ((q & 3) == 3) {
-            exp2_poly_pair(x2, p0, p1);
-          } else {
-            float x0, x1;
-            f2_unpack(x2, x0, x1);
-            p0 = ex2_approx(x0);
-            p1 = ex2_approx(x1);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int qq = 0; qq < 16; ++qq) {
+            const int q = 16 * c + qq;
+            const uint64_t x2 = f2_fma(f2_pack(s[2 * q], s[2 * q + 1]), sl2x2, negm2);
+            float p0, p1;
+            if ((q & 3) == 3) {
+              exp2_poly_pair(x2, p0, p1);
+            } else {
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              p0 = ex2_approx(x0);
+              p1 = ex2_approx(x1);
+            }
+            acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
+            pk[qq] = pack_bf16x2(p0, p1);
           }
-          acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
-          pk[q] = pack_bf16x2(p0, p1);
+          tmem_st_x16(tm_s + 32 * half + 16 * c, pk);
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&p_chunk[2 * tile + c]);
         }
         tr.ev(16, s_use);
-        tmem_st_x32(tm_s + 32 * half, pk);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&p_half[2 * tile + half]);
         tr.ev(13, s_use);
         float a0, a1, b0, b1, c0, c1, d0, d1;
         f2_unpack(acc[0], a0, a1);

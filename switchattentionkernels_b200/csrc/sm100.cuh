@@ -280,6 +280,22 @@ __device__ __forceinline__ void umma_ts_k64_warp(uint32_t d_tmem, uint32_t a_tme
       : "memory");
 }
 
+// Two back-to-back TS MMAs over 32 keys (A = P from TMEM, 8 columns per 16 keys;
+// B = V MN-major, 2048 bytes per 16 keys); `accumulate_first` = 0 makes the first
+// step overwrite D.
+__device__ __forceinline__ void umma_ts_k32_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate_first) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, p1;\n\t.reg .b64 b1;\n\t.reg .b32 t1;\n\t"
+      "setp.ne.b32 pf, %4, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "add.s64 b1, %2, 128;\n\tadd.u32 t1, %1, 8;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, p1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate_first)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm100 version field = 1.
 //   K-major operand : lbo ignored (pass 16), sbo = byte stride between 8-row groups.
 //   MN-major operand: lbo = byte stride between 64-element MN blocks,
