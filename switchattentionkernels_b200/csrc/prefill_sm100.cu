@@ -625,15 +625,20 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         tc_commit_warp(&o_full[1]);
         have = next_unit(cur);
         if (!ok || !have) break;
+        tr.ev(7, step);
         j = 0;
         const uint32_t k0s = kv_it % kStages;
         if (!mbar_wait(&q_full[0], q_use[0] & 1, abort_flag)) { ok = false; break; }
+        tr.ev(8, step);
         ++q_use[0];
         if (!mbar_wait(&kv_full[k0s], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
+        tr.ev(9, step);
         ++kv_it;
         tc_fence_after();
         issue_s_step(0, k0s, cur.n == 1);
+        tr.ev(17, step);
         if (!mbar_wait(&q_full[1], q_use[1] & 1, abort_flag)) { ok = false; break; }
+        tr.ev(18, step);
         ++q_use[1];
         tc_fence_after();
         issue_s_step(1, k0s, cur.n == 1);
@@ -718,10 +723,17 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         float* s = reinterpret_cast<float*>(sr);
         const int k0 = u.j0 * 64 + j * kBK + 64 * half;
         if (!(rb.lo <= k0 && k0 + 64 <= rb.hi)) {
+          // legal keys of this row in [k0, k0 + 64) form [k0 + a, k0 + b): two 32-bit
+          // masks, then one predicated select per entry
+          const int a = min(max(rb.lo - k0, 0), 64);
+          const int b = max(min(rb.hi - k0, 64), a);
+          const uint64_t hi_bits = b >= 64 ? ~0ull : ((1ull << b) - 1);
+          const uint64_t valid = hi_bits & ~((a >= 64) ? ~0ull : ((1ull << a) - 1));
+          const uint32_t v0 = static_cast<uint32_t>(valid), v1 = static_cast<uint32_t>(valid >> 32);
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const int key = k0 + e;
-            if (key < rb.lo || key >= rb.hi) s[e] = -INFINITY;
+          for (int e = 0; e < 32; ++e) {
+            s[e] = select_or_neg_inf(v0, 1u << e, s[e]);
+            s[32 + e] = select_or_neg_inf(v1, 1u << e, s[32 + e]);
           }
         }
         tr.ev(12, s_use + 1);

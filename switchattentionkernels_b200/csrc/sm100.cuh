@@ -416,6 +416,19 @@ __device__ __forceinline__ float lg2_approx(float x) {
   return y;
 }
 
+// x if (mask & bit) != 0, else -inf, as a predicated select: no branch, since the
+// masks of the lanes of a warp differ.
+__device__ __forceinline__ float select_or_neg_inf(uint32_t mask, uint32_t bit, float x) {
+  float y;
+  asm("{\n\t.reg .pred p;\n\t.reg .b32 t;\n\t"
+      "and.b32 t, %1, %2;\n\t"
+      "setp.ne.b32 p, t, 0;\n\t"
+      "selp.f32 %0, %3, 0fFF800000, p;\n\t}"
+      : "=f"(y)
+      : "r"(mask), "r"(bit), "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
