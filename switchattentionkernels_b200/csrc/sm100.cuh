@@ -28,10 +28,6 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool elect_one_lane() {
-  return (threadIdx.x & 31u) == 0u;
-}
-
 // Every wait on a barrier is bounded.  A wait that exceeds kWaitLimitNs sets the
 // CTA-wide abort flag (shared memory) and returns false; every other wait sees
 // the flag and returns false as well, so all roles leave their loops, the CTA
@@ -137,13 +133,6 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c
                : "memory");
 }
 
-// 32-byte global store (sm_100).
-__device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t* r) {
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(ptr), "r"(r[0]), "r"(r[1]), "r"(r[2]),
-               "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory
 // ---------------------------------------------------------------------------
@@ -169,62 +158,13 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Arrive (once) on `bar` when every tcgen05 operation issued so far by this
-// thread has completed.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-// D(tmem) (+)= A(smem desc) * B(smem desc)
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D(tmem) (+)= A(tmem) * B(smem desc)
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Warp-converged forms: the whole warp executes the call (descriptors stay warp
-// uniform) and one elected lane issues the instruction.  Issuing tcgen05.mma from
-// a single lane inside a divergent branch costs 2-3x the MMA's own duration, so
-// the MMA issuer runs these from converged code.
-__device__ __forceinline__ void umma_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
+// Warp-converged issue: the whole warp executes these calls (descriptors stay warp
+// uniform) and one lane chosen by elect.sync issues the tcgen05 instructions.
+// Issuing tcgen05.mma from a single lane inside a divergent branch measured 2-3x
+// the MMA's own duration; converged issue runs at the tensor peak.
+//
+// Arrive (once) on `bar` when every tcgen05 operation issued so far by the
+// elected thread has completed.
 __device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
@@ -258,25 +198,6 @@ __device__ __forceinline__ void umma_ss_k128_warp(uint32_t d_tmem, uint64_t a_de
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc)
-      : "memory");
-}
-
-// Four back-to-back TS MMAs over 64 keys: A = P from TMEM (8 columns per 16 keys),
-// B = V MN-major (2048 bytes per 16 keys).  `accumulate_first` = 0 makes the first
-// step overwrite D.
-__device__ __forceinline__ void umma_ts_k64_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate_first) {
-  asm volatile(
-      "{\n\t.reg .pred e, pf, p1;\n\t.reg .b64 b1, b2, b3;\n\t.reg .b32 t1, t2, t3;\n\t"
-      "setp.ne.b32 pf, %4, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
-      "add.s64 b1, %2, 128;\n\tadd.s64 b2, %2, 256;\n\tadd.s64 b3, %2, 384;\n\t"
-      "add.u32 t1, %1, 8;\n\tadd.u32 t2, %1, 16;\n\tadd.u32 t3, %1, 24;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, p1;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate_first)
       : "memory");
 }
 
@@ -346,15 +267,6 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      SWA_W8(0), SWA_W8(8), SWA_W8(16), SWA_W8(24)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -381,24 +293,9 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Per-warpgroup register reallocation (all warps of a warpgroup execute the same one).
-template <uint32_t N>
-__device__ __forceinline__ void reg_dealloc() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <uint32_t N>
-__device__ __forceinline__ void reg_alloc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
 __device__ __forceinline__ void reg_fence16(uint32_t* r) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
-}
-
-// TMEM address of (lane, column).
-__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
-  return base + (lane << 16) + col;
 }
 
 // ---------------------------------------------------------------------------
