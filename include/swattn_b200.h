@@ -58,6 +58,14 @@ const char* swa_last_error_string(void);
 /* Number of SMs of `device` (the persistent grid size), or a negative code. */
 int swa_num_sms(int device);
 
+/* Failure-detection test hook; no counterpart in the reference.  While `on` is
+ * non-zero, every swa_prefill_forward launch makes its first CTA withhold one
+ * K/V tile load, so the MMA issuer's bounded wait for that tile runs out: the
+ * launch returns with SWA_STATUS_TIMEOUT in workspace[1] after about one second,
+ * having released its tensor memory, and the CUDA context stays usable.  Not for
+ * production use; off by default. */
+void swa_test_withhold_kv_load(int on);
+
 /* Compact a routing mask (uint8/bool [B, S], non-zero = full attention) into
  * the increasing full / local position lists full[B, S], local[B, S]; entries
  * past each row's count are -1.  counts[2*b] = n_full, counts[2*b+1] = n_local.

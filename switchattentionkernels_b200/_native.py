@@ -34,6 +34,7 @@ EXPORTED = (
     "swa_prefill_forward",
     "swa_noalloc_max_batch",
     "swa_prefill_forward_noalloc",
+    "swa_test_withhold_kv_load",
 )
 
 _lock = threading.Lock()
@@ -86,6 +87,8 @@ def _declare(lib) -> None:
         _i, _f,                # window, scale_log2
         _p, _p,                # status_out, stream
     ]
+    lib.swa_test_withhold_kv_load.restype = None
+    lib.swa_test_withhold_kv_load.argtypes = [_i]
 
 
 def load():

@@ -1,4 +1,5 @@
 // C ABI of libswattn_b200 (declared in include/swattn_b200.h).
+#include <atomic>
 #include <cstdio>
 #include <string>
 
@@ -21,6 +22,9 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// failure-detection test hook (swa_test_withhold_kv_load)
+std::atomic<int> g_test_withhold{0};
+
 }  // namespace
 
 namespace swa {
@@ -30,6 +34,8 @@ void set_last_error(const char* msg) { g_last_error = msg; }
 extern "C" {
 
 int swa_abi_version(void) { return 1; }
+
+void swa_test_withhold_kv_load(int on) { g_test_withhold.store(on != 0 ? 1 : 0); }
 
 const char* swa_last_error_string(void) { return g_last_error.c_str(); }
 
@@ -188,6 +194,7 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
   p.pc = 256 / rp;
   p.nhb = r / rp;
   p.boxh = rp < 128 ? rp : 128;
+  p.test_withhold = g_test_withhold.load();
 
   const int64_t per_level = static_cast<int64_t>(p.n_bg) * p.nhb;
   const int64_t items =

@@ -457,10 +457,13 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         auto load_kv = [&](int j, int kv) -> bool {
           const uint32_t s = kv_it % kStages;
           if (!mbar_wait(&kv_empty[s], ((kv_it / kStages) & 1) ^ 1, abort_flag)) return false;
-          // lanes 0 and 1 each issue one 64-column half; lane 0 arms the barrier first
-          if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+          // lanes 0 and 1 each issue one 64-column half; lane 0 arms the barrier first.
+          // (With the failure-detection test hook, CTA 0 never arms or loads its second
+          // ring entry: the MMA warp's bounded wait on it runs out.)
+          const bool withhold = p.test_withhold != 0 && blockIdx.x == 0 && kv_it == 1;
+          if (lane == 0 && !withhold) mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
           __syncwarp();
-          if (lane < 2) {
+          if (lane < 2 && !withhold) {
             uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes + lane * kHalfBytes;
             const CUtensorMap* map = kv == 0 ? &p.k_map : &p.v_map;
             tma_load_4d(dst, map, &kv_full[s], lane * 64, u.g, u.j0 * 64 + j * kBK, u.b);

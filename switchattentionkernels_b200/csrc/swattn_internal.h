@@ -52,6 +52,7 @@ struct __align__(64) PrefillParams {
   int pc;    // positions per unit = 256 / rp
   int nhb;   // head blocks per KV group = (Hq/Hkv) / rp
   int boxh;  // rows per Q TMA box = min(rp, 128)
+  int test_withhold;  // failure-detection test hook: CTA 0 withholds its second K/V tile load
 };
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);
