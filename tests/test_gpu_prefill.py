@@ -85,6 +85,15 @@ def test_gqa_group_sizes(cuda_device, Hq, Hkv):
     _run(q, k, v, mask, 200, f"Hq={Hq},Hkv={Hkv}")
 
 
+@pytest.mark.parametrize("Hq,Hkv,S", [(64, 1, 300), (128, 1, 200), (256, 1, 150), (96, 3, 200)])
+def test_large_gqa_groups(cuda_device, Hq, Hkv, S):
+    # 64 heads per KV head: one Q box covers two positions; 128: one position per
+    # tile; 256: a position's heads span both tiles of a unit; 32 (96/3): 4 per tile
+    q, k, v = _rand_qkv(1, S, S, Hq, Hkv, 17 + Hq, cuda_device)
+    mask = torch.rand(1, S, generator=torch.Generator().manual_seed(Hq)) < 0.5
+    _run(q, k, v, mask, 64, f"Hq={Hq} Hkv={Hkv}")
+
+
 def test_batched_padded_lists(cuda_device):
     B, S = 3, 900
     q, k, v = _rand_qkv(B, S, S, 8, 2, 33, cuda_device)
