@@ -14,12 +14,12 @@
 // Roles (576 threads, one CTA per SM, persistent over a dynamic work counter):
 //   warp 0      producer : takes work units from the global counter (one unit
 //                          ahead) and publishes them through a shared-memory ring;
-//                          TMA Q gather (one box per routed position, the next
-//                          unit's boxes prefetched into L2 one unit ahead) and the
-//                          K/V tile ring (4 entries of 128 keys x 128 dims, K and V
-//                          tiles alternating)
+//                          TMA Q gather (boxes of consecutive routed positions, see
+//                          q_tile_boxes; the next unit's boxes are prefetched into L2
+//                          one unit ahead) and the K/V tile ring (4 entries of 128
+//                          keys x 128 dims, K and V tiles alternating)
 //   warp 1      MMA      : one elected lane issues tcgen05.mma in groups of eight
-//                          (S) or four (P V) instructions:
+//                          (S) or two (P V chunk) instructions:
 //                          S_i = Q_i K^T (SS, K-major) and O_i += P_i V (TS: P in TMEM,
 //                          V MN-major), commits to mbarriers.  Its issue order is one
 //                          continuous stream over key steps: PV_0(j), S_0(j+1),
