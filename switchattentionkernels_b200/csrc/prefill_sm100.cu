@@ -84,19 +84,14 @@ struct SmemLayout {
   static constexpr int b_p_chunk = b_s_full + 2;   // [tile][key chunk]
   static constexpr int b_o_full = b_p_chunk + 4;
   static constexpr int b_o_empty = b_o_full + 2;
-  static constexpr int b_stage_free = b_o_empty + 2;  // [tile]: the staging slot is this tile's turn
-  static constexpr int b_drain = b_stage_free + 2;
+  static constexpr int b_drain = b_o_empty + 2;
   static constexpr int n_bars = b_drain + 1;
   static constexpr uint32_t units = bars + ((n_bars * 8 + 63) / 64) * 64;
   static constexpr uint32_t misc = units + kSchedSlots * sizeof(Unit);
   // row-max exchange [2 parity][2 tile][2 half][128] floats (4 KB), then the row-sum
   // exchange [2 tile][2 half][128] floats (2 KB)
   static constexpr uint32_t xchg = misc + 64;
-  static constexpr uint32_t orows = xchg + 4096 + 2048;  // output row offsets [2 tile][128] int64 (2 KB)
-  // epilogue staging slot: 128 rows x 64 output columns (BF16), shared by the two
-  // tiles in turn, so that the Q buffers are free as soon as a unit's last S MMA is
-  static constexpr uint32_t stage = ((orows + 2048 + 1023) / 1024) * 1024;
-  static constexpr uint32_t total = stage + kHalfBytes;
+  static constexpr uint32_t total = xchg + 4096 + 2048;
 };
 
 constexpr uint32_t kSmemBytes = SmemLayout::total + 1024;  // + alignment slack
@@ -355,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
   uint64_t* p_chunk = bars + SmemLayout::b_p_chunk;
   uint64_t* o_full = bars + SmemLayout::b_o_full;
   uint64_t* o_empty = bars + SmemLayout::b_o_empty;
-  uint64_t* stage_free = bars + SmemLayout::b_stage_free;
   uint64_t* drain = bars + SmemLayout::b_drain;
 
   const int warp = threadIdx.x >> 5;
@@ -374,7 +368,6 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       mbar_init(&p_chunk[2 * i + 1], 256);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 256);
-      mbar_init(&stage_free[i], 256);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -680,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     float* xmax = reinterpret_cast<float*>(smem + SmemLayout::xchg);          // [2 parity][2 tile][2 half][128]
     float* xsum = reinterpret_cast<float*>(smem + SmemLayout::xchg + 4096);   // [2 tile][2 half][128]
-    static_assert(SmemLayout::orows - SmemLayout::xchg == 4096 + 2048, "exchange buffer sizes");
+    static_assert(SmemLayout::total - SmemLayout::xchg == 4096 + 2048, "exchange buffer sizes");
     const int bar_id = 1 + tile;
     uint32_t s_use = 0, o_use = 0;
     bool ok = true;
@@ -811,69 +804,63 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         l += ((a0 + a1) + (b0 + b1)) + ((c0 + c1) + (d0 + d1));
       }
       if (!ok) break;
-      // epilogue: O / l -> BF16 through the shared staging slot, 64 columns per
-      // round (round h: the key-half-h warpgroup stages its columns, then the
-      // tile's eight warps copy them out with coalesced stores); LSE in log2 units.
+      // epilogue: O / l -> BF16 written straight from registers with coalesced
+      // stores: each thread packs its 64 columns (eight 16-byte chunks), the eight
+      // lanes of a group transpose their 8 x 8 chunks with three xor butterflies
+      // (lane L then holds chunk L % 8 of the group's eight rows), so one store
+      // instruction writes four whole 128-byte row halves.  LSE in log2 units.
       tr.ev(20, s_use);
       xsum[tile * 256 + half * 128 + t] = l;
       if (!mbar_wait(&o_full[tile], o_use & 1, abort_flag)) { ok = false; break; }
+      ++o_use;
       tr.ev(21, s_use);
       named_bar_sync(bar_id, 256);
       l += xsum[tile * 256 + (half ^ 1) * 128 + t];
       const float inv_l = 1.0f / l;
-      int64_t* orow_tab = reinterpret_cast<int64_t*>(smem + SmemLayout::orows) + tile * 128;
-      if (half == 0) {
-        if (valid_row) p.lse[orow] = lg2_approx(l) + m;
-        orow_tab[t] = valid_row ? orow : -1;
+      if (half == 0 && valid_row) p.lse[orow] = lg2_approx(l) + m;
+      tc_fence_after();
+      uint32_t ch[8][4];  // ch[j]: chunk j (columns 8 j .. 8 j + 7 of this half) as BF16 pairs
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t orr[32];
+        tmem_ld_x32(tm_o + 32 * c, orr);
+        tmem_ld_wait();
+        reg_fence32(orr);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          ch[4 * c + e / 4][e % 4] = pack_bf16x2(__uint_as_float(orr[2 * e]) * inv_l,
+                                                 __uint_as_float(orr[2 * e + 1]) * inv_l);
       }
-      // the slot alternates tile 0, tile 1, tile 0, ... (one turn per unit each)
-      if (!mbar_wait(&stage_free[tile], (o_use & 1) ^ (tile == 0 ? 1u : 0u), abort_flag)) { ok = false; break; }
-      ++o_use;
-      uint8_t* stg = smem + SmemLayout::stage;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        if (half == h) {
-          tc_fence_after();
-          uint8_t* srow = stg + t * 128;
+      tc_fence_before();
+      mbar_arrive(&o_empty[tile]);  // O_i fully read: the next unit's P V may overwrite it
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t orr[32];
-            tmem_ld_x32(tm_o + 32 * c, orr);
-            tmem_ld_wait();
-            reg_fence32(orr);
+      for (int bit = 2; bit >= 0; --bit) {
+        const int msk = 1 << bit;
+        const bool upper = (lane & msk) != 0;
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(orr[8 * q4 + 0]) * inv_l, __uint_as_float(orr[8 * q4 + 1]) * inv_l);
-              w.y = pack_bf16x2(__uint_as_float(orr[8 * q4 + 2]) * inv_l, __uint_as_float(orr[8 * q4 + 3]) * inv_l);
-              w.z = pack_bf16x2(__uint_as_float(orr[8 * q4 + 4]) * inv_l, __uint_as_float(orr[8 * q4 + 5]) * inv_l);
-              w.w = pack_bf16x2(__uint_as_float(orr[8 * q4 + 6]) * inv_l, __uint_as_float(orr[8 * q4 + 7]) * inv_l);
-              const int chunk = 4 * c + q4;  // 16-byte chunk of this thread's 128-byte row half
-              *reinterpret_cast<uint4*>(srow + ((chunk ^ (t & 7)) << 4)) = w;
+        for (int j = 0; j < 8; ++j) {
+          if (j & msk) continue;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t x = upper ? ch[j][w] : ch[j | msk][w];
+            const uint32_t y = __shfl_xor_sync(0xffffffffu, x, msk);
+            if (upper) {
+              ch[j][w] = y;
+            } else {
+              ch[j | msk][w] = y;
             }
           }
-          tc_fence_before();
-          mbar_arrive(&o_empty[tile]);
         }
-        named_bar_sync(bar_id, 256);
-        tr.ev(23, s_use);
-        {
-          // 1024 16-byte chunks (128 rows x 8): warp wi of the tile copies chunks
-          // [32 (wi + 8 k), +32) = rows 4 (wi + 8 k) .. +3, lane L chunk L & 7 of
-          // row 4 (wi + 8 k) + (L >> 3); each row half is 128 contiguous bytes of `out`.
-          const int wi = (grp & 1) * 4 + (warp & 3);
-          const int ch = lane & 7;
-#pragma unroll
-          for (int k2 = 0; k2 < 4; ++k2) {
-            const int row = 4 * (wi + 8 * k2) + (lane >> 3);
-            const uint4 w = *reinterpret_cast<const uint4*>(stg + row * 128 + ((ch ^ (row & 7)) << 4));
-            const int64_t grow = orow_tab[row];
-            if (grow >= 0) *reinterpret_cast<uint4*>(p.out + grow * 128 + 64 * h + ch * 8) = w;
-          }
-        }
-        if (h == 0) named_bar_sync(bar_id, 256);  // slot read before round 1 refills it
       }
-      mbar_arrive(&stage_free[tile ^ 1]);  // all 256 threads: the other tile's turn
+      const int64_t my_row = valid_row ? orow : -1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int src = (lane & ~7) + j;  // lane holding row j of this group
+        const int64_t grow = __shfl_sync(0xffffffffu, my_row, src);
+        if (grow >= 0)
+          *reinterpret_cast<uint4*>(p.out + grow * 128 + 64 * half + 8 * (lane & 7)) =
+              make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
+      }
       tr.ev(22, s_use);
     }
   }
