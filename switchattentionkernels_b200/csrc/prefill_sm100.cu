@@ -242,7 +242,7 @@ __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit&
       if (qdst != nullptr) {
         tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, bar, half * 64, row);
       } else {
-        tma_prefetch_l2_2d(&p.q_map, half * 64, row);
+        tma_prefetch_l2_2d(&p.q_map, half * 64, row, l2_policy_evict_last());
       }
     }
     return;
@@ -272,13 +272,13 @@ __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit&
         if (qdst != nullptr) {
           tma_load_2d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_map, bar, half * 64, row);
         } else {
-          tma_prefetch_l2_2d(&p.q_map, half * 64, row);
+          tma_prefetch_l2_2d(&p.q_map, half * 64, row, l2_policy_evict_last());
         }
       } else if (qdst != nullptr) {
         tma_load_3d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_runs[lev - 1], bar, half * 64, head0,
                     u.b * p.Sq + pos);
       } else {
-        tma_prefetch_l2_3d(&p.q_runs[lev - 1], half * 64, head0, u.b * p.Sq + pos);
+        tma_prefetch_l2_3d(&p.q_runs[lev - 1], half * 64, head0, u.b * p.Sq + pos, l2_policy_evict_last());
       }
     }
   }

@@ -118,18 +118,27 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Bring a box of a tiled tensor into L2 (no shared-memory destination).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+// L2 policy that keeps lines resident ahead of streaming data (evict-last).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Bring a box of a tiled tensor into L2 (no shared-memory destination), with an
+// L2 cache policy.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
+               "r"(c0), "r"(c1), "l"(policy)
                : "memory");
 }
 
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2)
+               "r"(c0), "r"(c1), "r"(c2), "l"(policy)
                : "memory");
 }
 
