@@ -31,8 +31,9 @@
 //                          tile and O columns [64 h, 64 h + 64)); then the O/LSE
 //                          epilogue of the tile.
 // TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs)
-// overwrites the first 64 columns of S_i and is consumed by the next PV MMA.  P is
-// published in two chunks (keys [32 c, +32) of each key half, c = 0, 1).
+// of key half h overwrites columns 64 h .. 64 h + 31 of S_i (scores that half has
+// already consumed) and is consumed by the next PV MMA.  P is published in two
+// chunks (keys [32 c, +32) of each key half, c = 0, 1).
 // Key tiles of a unit start at the 64-aligned key at or below its first legal key.
 //
 // Numerics follow the reference: FP32 scores, log2-domain online softmax with
@@ -533,9 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     auto issue_s = [&](int i, uint32_t kstage) {
       umma_ss_k128_warp(tm_s[i], q_desc[i], k_desc0 + kstage * (kTileBytes >> 4), idesc_s);
     };
-    // P V for one tile, in two halves of 64 keys gated by the softmax's half barriers.
     // P V for one tile in two chunks: chunk c covers keys [32 c, +32) of each key
-    // half (keys 64 h + 32 c .. +31: P columns 32 h + 16 c .., V rows 2048-byte
+    // half (keys 64 h + 32 c .. +31: P columns 64 h + 16 c .., V rows 2048-byte
     // steps 4 h + 2 c ..), published by the softmax before it exponentiates chunk c + 1.
     auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) -> bool {
       const uint64_t vb = v_desc0 + vstage * (kTileBytes >> 4);
@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (!mbar_wait(&p_chunk[2 * i + c], p_use[i] & 1, abort_flag)) { ok = false; return false; }
         tc_fence_after();
         umma_ts_k32_warp(tm_o[i], tm_s[i] + 16 * c, vb + (2 * c) * 128, idesc_o, (accumulate || c > 0) ? 1u : 0u);
-        umma_ts_k32_warp(tm_o[i], tm_s[i] + 32 + 16 * c, vb + (4 + 2 * c) * 128, idesc_o, 1u);
+        umma_ts_k32_warp(tm_o[i], tm_s[i] + 64 + 16 * c, vb + (4 + 2 * c) * 128, idesc_o, 1u);
       }
       ++p_use[i];
       return true;
@@ -718,14 +718,18 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         reg_fence32(sr + 32);
         float* s = reinterpret_cast<float*>(sr);
         const int k0 = u.j0 * 64 + j * kBK + 64 * half;
-        if (!(rb.lo <= k0 && k0 + 64 <= rb.hi)) {
-          // legal keys of this row in [k0, k0 + 64) form [k0 + a, k0 + b): two 32-bit
-          // masks, then one predicated select per entry
+        const bool need_mask = !(rb.lo <= k0 && k0 + 64 <= rb.hi);
+        // legal keys of this row in [k0, k0 + 64) form [k0 + a, k0 + b): two 32-bit
+        // masks, then one predicated select per entry
+        auto key_mask = [&](int word) -> uint32_t {
           const int a = min(max(rb.lo - k0, 0), 64);
           const int b = max(min(rb.hi - k0, 64), a);
           const uint64_t hi_bits = b >= 64 ? ~0ull : ((1ull << b) - 1);
           const uint64_t valid = hi_bits & ~((a >= 64) ? ~0ull : ((1ull << a) - 1));
-          const uint32_t v0 = static_cast<uint32_t>(valid), v1 = static_cast<uint32_t>(valid >> 32);
+          return static_cast<uint32_t>(valid >> (32 * word));
+        };
+        if (need_mask) {
+          const uint32_t v0 = key_mask(0), v1 = key_mask(1);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             s[e] = select_or_neg_inf(v0, 1u << e, s[e]);
@@ -769,14 +773,31 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         const uint64_t negm2 = f2_pack(-m, -m);
         uint64_t acc[4] = {0, 0, 0, 0};
         // two chunks of 32 keys; each is published as soon as it is in TMEM, so the
-        // P V MMAs of chunk 0 run while chunk 1 is exponentiated
+        // P V MMAs of chunk 0 run while chunk 1 is exponentiated.  Chunk 1's scores
+        // are read from TMEM again (keys 32..63 of this half, which no P store
+        // reaches: P of key half h goes to columns 64 h .. 64 h + 31), so the 32
+        // registers that held them are free while chunk 0 is exponentiated.
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
+          uint32_t sr1[32];
+          const float* sc = s;
+          if (c == 1) {
+            tmem_ld_x32(tm_s + 64 * half + 32, sr1);
+            tmem_ld_wait();
+            reg_fence32(sr1);
+            float* s1 = reinterpret_cast<float*>(sr1);
+            if (need_mask) {
+              const uint32_t v1 = key_mask(1);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) s1[e] = select_or_neg_inf(v1, 1u << e, s1[e]);
+            }
+            sc = s1 - 32;
+          }
 #pragma unroll
           for (int qq = 0; qq < 16; ++qq) {
             const int q = 16 * c + qq;
-            const uint64_t x2 = f2_fma(f2_pack(s[2 * q], s[2 * q + 1]), sl2x2, negm2);
+            const uint64_t x2 = f2_fma(f2_pack(sc[2 * q], sc[2 * q + 1]), sl2x2, negm2);
             float p0, p1;
             if ((q & 3) == 3) {
               exp2_poly_pair(x2, p0, p1);
@@ -789,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
             acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
             pk[qq] = pack_bf16x2(p0, p1);
           }
-          tmem_st_x16(tm_s + 32 * half + 16 * c, pk);
+          tmem_st_x16(tm_s + 64 * half + 16 * c, pk);
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(&p_chunk[2 * tile + c]);
