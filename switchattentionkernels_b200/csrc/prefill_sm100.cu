@@ -102,7 +102,7 @@ struct RowBounds {
 };
 
 // Optional cycle-level event trace of CTA 0 (compiled only with -DSWA_TRACE): each
-// recorder (MMA issuer, softmax warpgroup 0, softmax warpgroup 1) appends
+// recorder (MMA issuer, softmax warpgroup 0, softmax warpgroup 1, producer) appends
 // (event id, key step, clock64) records to its own region of g_swa_trace.
 #ifdef SWA_TRACE
 __device__ unsigned long long* g_swa_trace = nullptr;
@@ -417,12 +417,15 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     };
     uint32_t kv_it = 0;
     uint32_t q_use[2] = {0, 0};
+    Tracer tr(lane == 0 ? 3 : -1);
     Unit u;
     fetch(u);
     for (int k = 0;; ++k) {
+      tr.ev(60, k);
       Unit un;
       un.valid = 0;
       if (u.valid) fetch(un);
+      tr.ev(61, k);
       const int slot = k % kSchedSlots;
       if (!mbar_wait(&sched_empty[slot], ((k / kSchedSlots) & 1) ^ 1, abort_flag)) break;
       if (lane == 0) {
@@ -446,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         q_tile_boxes(p, un, 0, lane, nullptr, nullptr);
         q_tile_boxes(p, un, 1, lane, nullptr, nullptr);
       }
+      tr.ev(62, k);
       bool ok = true;
       if (u.n > 0) {
         auto load_kv = [&](int j, int kv) -> bool {
@@ -469,10 +473,12 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         auto load_q = [&](int i) -> bool {
           // Q_i is free once the previous unit's last S MMA of tile i has completed
           if (!mbar_wait(&q_empty[i], (q_use[i] & 1) ^ 1, abort_flag)) return false;
+          tr.ev(63 + 2 * i, k);
           ++q_use[i];
           if (lane == 0) mbar_arrive_expect_tx(&q_full[i], kTileBytes);
           __syncwarp();
           q_tile_boxes(p, u, i, lane, smem + (i == 0 ? SmemLayout::q0 : SmemLayout::q1), &q_full[i]);
+          tr.ev(64 + 2 * i, k);
           return true;
         };
         // ring order K_0, V_0, K_1, V_1, ...; the Q tiles go between K_0 and V_0 so
