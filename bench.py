@@ -61,6 +61,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default: the workload's 4); smaller values give profiling-size cases")
+    ap.add_argument("--cp", action="store_true",
+                    help="instead of the default line: context-parallel varlen prefill of config 4 over the N ranks "
+                         "(strong scaling; K/V all-gather + metadata + kernel per step)")
     return ap.parse_args()
 
 
@@ -239,6 +242,87 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def run_cp(args, world, rank, local_rank):
+    """Context-parallel prefill of the config-4 packed batch over ``world`` ranks.
+
+    Every rank draws the same batch and keeps only its rows of Q, K and V (zigzag
+    chunks of equal legal-entry cost, ``context_parallel.make_cp_plan``); one step
+    is the public context-parallel forward: the K/V all-gather (NCCL), the rows'
+    metadata and the prefill kernel on the rank's rows.  ``value`` = effective FLOP of the whole batch / the
+    slowest rank's step time (strong scaling: the batch is fixed as N grows).
+    """
+    import torch.distributed as dist
+    from switchattentionkernels_b200 import context_parallel as cp
+
+    cfg_id = 4
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = workloads.make_inputs(cfg_id, device=dev, on_device=True)
+    cfg = w["cfg"]
+    q, k, v, mask, W, cu = w["q"], w["k"], w["v"], w["mask"][0].numpy(), w["window"], w["cu_seqlens"]
+    S, Hq, Hkv = q.shape[1], q.shape[2], k.shape[2]
+    flops_total = workloads.effective_flops(mask[None, :], W, S, Hq, cu_seqlens=cu.numpy())
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29700 + os.getpid() % 200))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    plan = cp.make_cp_plan(S, world, cp.cp_row_costs(mask, W, cu.numpy()))
+    rows = plan.rows(rank)
+    idx = torch.from_numpy(rows).to(dev)
+    ql, kl, vl = (t.index_select(1, idx).contiguous() for t in (q, k, v))
+    del q, k, v
+    lm = mask[rows]
+    fl = torch.from_numpy(np.nonzero(lm)[0]).to(device=dev, dtype=torch.int32)
+    ll = torch.from_numpy(np.nonzero(~lm)[0]).to(device=dev, dtype=torch.int32)
+
+    def step():
+        cp.context_parallel_switch_gqa_prefill_forward(ql, kl, vl, fl, ll, total_len=S, cu_seqlens=cu,
+                                                       window_size=W, validate=False, plan=plan)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.mark("begin")
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark("end")
+    dist.barrier()
+    clock_info = clocks.stop()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_max = float(ms.item())
+    if world == 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        peak_burst, _, peak_src = measured_peaks()
+        value = flops_total / (ms_max * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "effective TFLOP/s, context-parallel varlen prefill", "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": cfg.name, "tokens": S, "sequences": int(cu.numel() - 1), "Hq": Hq, "Hkv": Hkv,
+                       "window": W, "p_full": cfg.p_full,
+                       "parallelism": f"context parallel over {world} ranks: cost-balanced zigzag rows, "
+                                      "K/V all-gather (NCCL)",
+                       "rows_per_rank_max": plan.capacity,
+                       "effective_tflop_per_step": flops_total / 1e12},
+            "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst, "peak_source": peak_src,
+            "gpu_launches": 2 * args.steps,  # metadata kernel + prefill kernel per step (per rank)
+            "clocks": clock_info,
+        }), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     world, rank, local_rank = dist_env()
@@ -247,6 +331,12 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.cp and args.impl == "ours":
+        rc = run_cp(args, world, rank, local_rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return rc
     if args.impl == "reference":
         rc = run_reference(args, world, rank)
         if world > 1:
