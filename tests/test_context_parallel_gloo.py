@@ -1,5 +1,5 @@
 """Context-parallel host logic on CPU ranks (gloo): the zigzag row split, the
-K/V all-gather with its reorder into token order, and the composition (each
+K/V all-gather into token order, and the composition (each
 rank's rows against the gathered K/V with the rows' global key bounds) checked
 against the unsplit FP32 oracle.  The kernel itself runs in the GPU tests."""
 from __future__ import annotations
@@ -26,9 +26,6 @@ def _check_partition(plan):
     for rows in shards:
         assert np.all(np.diff(rows) > 0)
     assert plan.capacity == max(s.size for s in shards)
-    src = plan.gather_map()
-    for r, rows in enumerate(shards):
-        assert np.array_equal(src[rows], r * plan.capacity + np.arange(rows.size))
     return shards
 
 
@@ -159,12 +156,12 @@ def _run(world, mode):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_gather_kv_restores_token_order(world):
+def test_kv_exchange_restores_token_order(world):
     assert _run(world, "gather") == [(r, "ok") for r in range(world)]
 
 
-def test_gather_kv_with_a_rank_that_holds_no_rows():
-    # one token over two ranks: rank 1 holds nothing and still takes part in the gather
+def test_kv_exchange_with_a_rank_that_holds_no_rows():
+    # one token over two ranks: rank 1 holds nothing and still takes part in the exchange
     assert cp.make_cp_plan(1, 2).rows(1).size == 0
     assert _run(2, "tiny") == [(0, "ok"), (1, "ok")]
 
