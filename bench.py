@@ -62,8 +62,10 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default: the workload's 4); smaller values give profiling-size cases")
     ap.add_argument("--cp", action="store_true",
-                    help="instead of the default line: context-parallel varlen prefill of config 4 over the N ranks "
+                    help="instead of the default line: context-parallel prefill over the N ranks "
                          "(strong scaling; K/V all-gather + kernel per step)")
+    ap.add_argument("--cp-config", type=int, choices=[4, 5], default=4,
+                    help="--cp workload: 4 = the varlen packed batch, 5 = one 131072-token sequence of config 5")
     return ap.parse_args()
 
 
@@ -243,7 +245,10 @@ def run_reference(args, world, rank):
 
 # --------------------------------------------------------------------------- GPU arm
 def run_cp(args, world, rank, local_rank):
-    """Context-parallel prefill of the config-4 packed batch over ``world`` ranks.
+    """Context-parallel prefill of one packed batch over ``world`` ranks.
+
+    Workload: config 4 (16 packed sequences) or, with ``--cp-config 5``, the first
+    131072-token sequence of config 5.
 
     Every rank draws the same batch and keeps only its rows of Q, K and V (zigzag
     chunks of equal legal-entry cost, ``context_parallel.make_cp_plan``).  One
@@ -256,12 +261,14 @@ def run_cp(args, world, rank, local_rank):
     import torch.distributed as dist
     from switchattentionkernels_b200 import context_parallel as cp
 
-    cfg_id = 4
+    cfg_id = args.cp_config
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     w = workloads.make_inputs(cfg_id, device=dev, on_device=True)
     cfg = w["cfg"]
-    q, k, v, mask, W, cu = w["q"], w["k"], w["v"], w["mask"][0].numpy(), w["window"], w["cu_seqlens"]
+    q, k, v, mask, W, cu = w["q"][:1], w["k"][:1], w["v"][:1], w["mask"][0].numpy(), w["window"], w["cu_seqlens"]
+    if cu is None:
+        cu = torch.tensor([0, q.shape[1]], dtype=torch.int32)
     S, Hq, Hkv = q.shape[1], q.shape[2], k.shape[2]
     flops_total = workloads.effective_flops(mask[None, :], W, S, Hq, cu_seqlens=cu.numpy())
     if world == 1:
