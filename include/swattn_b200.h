@@ -14,6 +14,9 @@
  *
  * Reference interfaces replaced (YushengZhao/SwitchAttentionKernels):
  *   swa_compact_mask      <- build_switch_query_indices   swiattn_gqa_prefill_varlen.py:306-322
+ *   swa_compact_router    <- the router step before it (outside the reference,
+ *                            README.md:85) fused with the compaction
+ *   swa_compact_*_ws      <- the same two, rows split over several CTAs
  *   swa_prepare_indices   <- _prepare_indices             swiattn_gqa_prefill_varlen.py:271-304
  *   swa_check_cover       <- coverage check               swiattn_gqa_prefill_varlen.py:390-393
  *   swa_build_metadata    <- build_switch_attention_metadata (imported at
@@ -73,6 +76,33 @@ void swa_test_withhold_kv_load(int on);
  * which handles B = 1 only. */
 int swa_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local, int32_t* counts,
                      void* stream);
+
+/* Router output -> routing decision -> compaction in one kernel (no mask
+ * buffer).  The reference leaves the router outside the kernel and compacts a
+ * bool mask (README.md:85, build_switch_query_indices
+ * swiattn_gqa_prefill_varlen.py:306-322); this entry point takes the router's
+ * output instead.  router: dtype SWA_ROUTER_BF16 or SWA_ROUTER_F32, contiguous
+ *   pair = 0: [B, S]    one score per token, full iff score > threshold;
+ *   pair = 1: [B, S, 2] logits (local, full), full iff
+ *             logit_full - logit_local > threshold (0 = argmax, ties local).
+ * Values are compared in FP32; NaN routes to local.  Outputs as
+ * swa_compact_mask. */
+#define SWA_ROUTER_BF16 1
+#define SWA_ROUTER_F32 2
+int swa_compact_router(const void* router, int dtype, int pair, float threshold, int B, int S, int32_t* full,
+                       int32_t* local, int32_t* counts, void* stream);
+
+/* The compactions above with a caller-provided int32 workspace of at least
+ * swa_compact_workspace_elems(B, S) elements (0 when every row fits one CTA):
+ * rows longer than one 4096-token chunk are then split over several CTAs in
+ * two launches (per-chunk counts, then scan and write), instead of one CTA per
+ * row.  Results are identical.  SWA_E_INVALID when the workspace is too small. */
+int64_t swa_compact_workspace_elems(int B, int S);
+int swa_compact_mask_ws(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local, int32_t* counts,
+                        int32_t* workspace, int64_t workspace_elems, void* stream);
+int swa_compact_router_ws(const void* router, int dtype, int pair, float threshold, int B, int S, int32_t* full,
+                          int32_t* local, int32_t* counts, int32_t* workspace, int64_t workspace_elems,
+                          void* stream);
 
 /* Capacity-bucket preparation and validation of one index list per batch row
  * (replaces _prepare_indices, swiattn_gqa_prefill_varlen.py:271-304).

@@ -8,7 +8,11 @@ Follows ``swiattn_gqa_prefill_varlen.py`` of the reference:
 * ``bucket_capacity``   -- the power-of-two capacity of ``_prepare_indices``
   (:287-292);
 * ``prepare_indices``   -- ``_prepare_indices`` (:271-304): -1 padding to the
-  capacity, range and strict-increase validation with the reference messages.
+  capacity, range and strict-increase validation with the reference messages;
+* ``router_mask``       -- the routing decision that produces the mask (the
+  router itself is outside the reference, ``README.md:85``, which fixes only
+  the convention True = full attention): FP32 ``score > threshold``, or FP32
+  ``logit_full - logit_local > threshold`` for ``(local, full)`` logit pairs.
 """
 from __future__ import annotations
 
@@ -45,6 +49,19 @@ def compact_mask_batched(mask: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.n
         local[b, : l.size] = l
         counts[b] = (f.size, l.size)
     return full, local, counts
+
+
+def router_mask(router: np.ndarray, *, pair: bool, threshold: float = 0.0) -> np.ndarray:
+    """Bool ``[B, S]`` routing mask of FP32 router outputs (``[B, S]`` or ``[B, S, 2]``).
+
+    BF16 inputs are widened to FP32 exactly by the caller; the subtraction and
+    the comparison are single FP32 operations, and NaN compares false (local).
+    """
+    r = np.asarray(router, dtype=np.float32)
+    thr = np.float32(threshold)
+    if pair:
+        return (r[..., 1] - r[..., 0]) > thr
+    return r > thr
 
 
 def bucket_capacity(count: int, block_m: int) -> int:

@@ -124,10 +124,62 @@ def build_switch_query_indices_batched(full_mask: torch.Tensor):
     if B == 0 or S == 0:
         return full, local, counts
     lib = _native.load()
+    nws = int(lib.swa_compact_workspace_elems(B, S))
+    ws = torch.empty(max(nws, 1), dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
-        rc = lib.swa_compact_mask(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
-                                  _native.ptr(counts), _native.stream_ptr(dev))
+        rc = lib.swa_compact_mask_ws(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
+                                     _native.ptr(counts), _native.ptr(ws), nws, _native.stream_ptr(dev))
     _native.check(rc, "build_switch_query_indices")
+    return full, local, counts
+
+
+def build_switch_query_indices_from_router(router_out: torch.Tensor, *, threshold: float = 0.0, pair: bool = False):
+    """Router output -> ``(full [B,S], local [B,S], counts [B,2])`` in one kernel, no mask buffer.
+
+    The reference leaves the router outside the kernel and compacts the bool
+    mask it yields (``README.md:85``); this fuses that step with the compaction.
+    ``router_out``: device-resident BF16 or FP32.  ``pair=False``: ``[S]`` or
+    ``[B, S]`` scores, a token goes to full attention iff ``score > threshold``.
+    ``pair=True``: ``[S, 2]`` or ``[B, S, 2]`` logits ``(local, full)``, full iff
+    ``logit_full - logit_local > threshold`` (0: argmax with ties to local).
+    Compared in FP32; NaN routes to local.  Outputs as
+    ``build_switch_query_indices_batched`` (a 1-D / 2-D input is one batch row).
+    """
+    if not isinstance(router_out, torch.Tensor) or not router_out.is_cuda:
+        raise TypeError("router_out must be a device-resident tensor")
+    if router_out.dtype == torch.bfloat16:
+        dtype = _native.ROUTER_BF16
+    elif router_out.dtype == torch.float32:
+        dtype = _native.ROUTER_F32
+    else:
+        raise TypeError("router_out must be bfloat16 or float32")
+    r = router_out
+    if pair:
+        if r.ndim == 2:
+            r = r.unsqueeze(0)
+        if r.ndim != 3 or r.shape[2] != 2:
+            raise ValueError("with pair=True router_out must have shape [S, 2] or [B, S, 2]")
+    else:
+        if r.ndim == 1:
+            r = r.unsqueeze(0)
+        if r.ndim != 2:
+            raise ValueError("router_out must have shape [S] or [B, S]")
+    r = r.contiguous()
+    B, S = int(r.shape[0]), int(r.shape[1])
+    dev = r.device
+    full = torch.empty((B, S), dtype=torch.int32, device=dev)
+    local = torch.empty((B, S), dtype=torch.int32, device=dev)
+    counts = torch.zeros((B, 2), dtype=torch.int32, device=dev)
+    if B == 0 or S == 0:
+        return full, local, counts
+    lib = _native.load()
+    nws = int(lib.swa_compact_workspace_elems(B, S))
+    ws = torch.empty(max(nws, 1), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.swa_compact_router_ws(_native.ptr(r), dtype, 1 if pair else 0, float(threshold), B, S,
+                                       _native.ptr(full), _native.ptr(local), _native.ptr(counts),
+                                       _native.ptr(ws), nws, _native.stream_ptr(dev))
+    _native.check(rc, "build_switch_query_indices_from_router")
     return full, local, counts
 
 

@@ -22,12 +22,18 @@ STATUS_FULL_PAD = 1 << 4
 STATUS_LOCAL_PAD = 1 << 5
 STATUS_COVER = 1 << 6
 STATUS_TIMEOUT = 1 << 16
+ROUTER_BF16 = 1
+ROUTER_F32 = 2
 
 EXPORTED = (
     "swa_abi_version",
     "swa_last_error_string",
     "swa_num_sms",
     "swa_compact_mask",
+    "swa_compact_router",
+    "swa_compact_workspace_elems",
+    "swa_compact_mask_ws",
+    "swa_compact_router_ws",
     "swa_prepare_indices",
     "swa_check_cover",
     "swa_build_metadata",
@@ -55,6 +61,14 @@ def _declare(lib) -> None:
     lib.swa_num_sms.argtypes = [_i]
     lib.swa_compact_mask.restype = _i
     lib.swa_compact_mask.argtypes = [_p, _i, _i, _p, _p, _p, _p]
+    lib.swa_compact_router.restype = _i
+    lib.swa_compact_router.argtypes = [_p, _i, _i, _f, _i, _i, _p, _p, _p, _p]
+    lib.swa_compact_workspace_elems.restype = ctypes.c_int64
+    lib.swa_compact_workspace_elems.argtypes = [_i, _i]
+    lib.swa_compact_mask_ws.restype = _i
+    lib.swa_compact_mask_ws.argtypes = [_p, _i, _i, _p, _p, _p, _p, ctypes.c_int64, _p]
+    lib.swa_compact_router_ws.restype = _i
+    lib.swa_compact_router_ws.argtypes = [_p, _i, _i, _f, _i, _i, _p, _p, _p, _p, ctypes.c_int64, _p]
     lib.swa_prepare_indices.restype = _i
     lib.swa_prepare_indices.argtypes = [_p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _i, _i, _p]
     lib.swa_check_cover.restype = _i

@@ -52,8 +52,57 @@ int swa_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* 
   if (B == 0) return SWA_OK;
   if (mask == nullptr || full == nullptr || local == nullptr || counts == nullptr)
     return fail(SWA_E_INVALID, "null pointer");
-  cudaError_t e = swa::launch_compact_mask(mask, B, S, full, local, counts, static_cast<cudaStream_t>(stream));
+  cudaError_t e = swa::launch_compact_mask(mask, B, S, full, local, counts, nullptr, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "compact_mask launch");
+  return SWA_OK;
+}
+
+static_assert(swa::kRouterBf16 == SWA_ROUTER_BF16 && swa::kRouterF32 == SWA_ROUTER_F32, "router dtype codes");
+
+int swa_compact_router(const void* router, int dtype, int pair, float threshold, int B, int S, int32_t* full,
+                       int32_t* local, int32_t* counts, void* stream) {
+  if (B < 0 || S < 0) return fail(SWA_E_INVALID, "negative shape");
+  if (dtype != SWA_ROUTER_BF16 && dtype != SWA_ROUTER_F32) return fail(SWA_E_INVALID, "router dtype must be bf16 or fp32");
+  if (pair != 0 && pair != 1) return fail(SWA_E_INVALID, "pair must be 0 or 1");
+  if (B == 0) return SWA_OK;
+  if (router == nullptr || full == nullptr || local == nullptr || counts == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  cudaError_t e = swa::launch_compact_router(router, dtype, pair, threshold, B, S, full, local, counts, nullptr,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "compact_router launch");
+  return SWA_OK;
+}
+
+int64_t swa_compact_workspace_elems(int B, int S) { return swa::compact_workspace_elems(B, S); }
+
+int swa_compact_mask_ws(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local, int32_t* counts,
+                        int32_t* workspace, int64_t workspace_elems, void* stream) {
+  if (B < 0 || S < 0) return fail(SWA_E_INVALID, "negative shape");
+  if (B == 0) return SWA_OK;
+  if (mask == nullptr || full == nullptr || local == nullptr || counts == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  const int64_t need = swa::compact_workspace_elems(B, S);
+  if (need > 0 && (workspace == nullptr || workspace_elems < need)) return fail(SWA_E_INVALID, "workspace too small");
+  cudaError_t e = swa::launch_compact_mask(mask, B, S, full, local, counts, need > 0 ? workspace : nullptr,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "compact_mask launch");
+  return SWA_OK;
+}
+
+int swa_compact_router_ws(const void* router, int dtype, int pair, float threshold, int B, int S, int32_t* full,
+                          int32_t* local, int32_t* counts, int32_t* workspace, int64_t workspace_elems,
+                          void* stream) {
+  if (B < 0 || S < 0) return fail(SWA_E_INVALID, "negative shape");
+  if (dtype != SWA_ROUTER_BF16 && dtype != SWA_ROUTER_F32) return fail(SWA_E_INVALID, "router dtype must be bf16 or fp32");
+  if (pair != 0 && pair != 1) return fail(SWA_E_INVALID, "pair must be 0 or 1");
+  if (B == 0) return SWA_OK;
+  if (router == nullptr || full == nullptr || local == nullptr || counts == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  const int64_t need = swa::compact_workspace_elems(B, S);
+  if (need > 0 && (workspace == nullptr || workspace_elems < need)) return fail(SWA_E_INVALID, "workspace too small");
+  cudaError_t e = swa::launch_compact_router(router, dtype, pair, threshold, B, S, full, local, counts,
+                                             need > 0 ? workspace : nullptr, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "compact_router launch");
   return SWA_OK;
 }
 

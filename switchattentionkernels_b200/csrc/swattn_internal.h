@@ -61,8 +61,18 @@ cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream
 void set_last_error(const char* msg);
 uint32_t prefill_smem_bytes();
 
+// Workspace (int32 elements) the compaction takes to split rows over several
+// CTAs; 0 when every row fits one CTA.  With ws == nullptr the compaction runs
+// one CTA per row.
+int64_t compact_workspace_elems(int B, int S);
 cudaError_t launch_compact_mask(const uint8_t* mask, int B, int S, int32_t* full, int32_t* local,
-                                int32_t* counts, cudaStream_t stream);
+                                int32_t* counts, int32_t* ws, cudaStream_t stream);
+
+// Router output element types of swa_compact_router (values of SWA_ROUTER_*).
+constexpr int kRouterBf16 = 1;
+constexpr int kRouterF32 = 2;
+cudaError_t launch_compact_router(const void* router, int dtype, int pair, float threshold, int B, int S,
+                                  int32_t* full, int32_t* local, int32_t* counts, int32_t* ws, cudaStream_t stream);
 
 cudaError_t launch_prepare_indices(const int32_t* idx, int B, int N, int seq_len, int padded_rows, int cap,
                                    int32_t* padded, int32_t* count, int32_t* status, int range_bit, int order_bit,

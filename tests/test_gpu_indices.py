@@ -78,3 +78,106 @@ def test_prepare_indices_errors(cuda_device, bad, msg):
     with pytest.raises(ValueError, match=msg.replace("(", r"\(").replace(")", r"\)").replace("[", r"\[")):
         varlen._prepare_indices(torch.tensor(bad, dtype=torch.int32, device=cuda_device), seq_len=5000,
                                 block_m=64)
+
+
+def _router_case(B, S, dtype, pair, seed):
+    g = torch.Generator().manual_seed(seed)
+    shape = (B, S, 2) if pair else (B, S)
+    r = torch.randn(shape, generator=g).to(dtype)
+    flat = r.view(-1)
+    if flat.numel() > 20:
+        flat[3] = float("nan")
+        flat[10:14] = 0.0        # ties (pairs) and scores equal to a zero threshold
+    return r
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("pair", [False, True])
+@pytest.mark.parametrize("B,S", [(1, 1), (1, 17), (2, 1000), (3, 16384), (1, 16385), (2, 40001)])
+@pytest.mark.parametrize("threshold", [0.0, 0.7])
+def test_router_compaction_bit_exact(cuda_device, dtype, pair, B, S, threshold):
+    from switchattentionkernels_b200 import build_switch_query_indices_from_router
+    r = _router_case(B, S, dtype, pair, seed=B * 100003 + S)
+    full, local, counts = build_switch_query_indices_from_router(r.to(cuda_device), threshold=threshold, pair=pair)
+    mask = oracle_idx.router_mask(r.float().numpy(), pair=pair, threshold=threshold)
+    rf, rl, rc = oracle_idx.compact_mask_batched(mask)
+    assert np.array_equal(full.cpu().numpy(), rf)
+    assert np.array_equal(local.cpu().numpy(), rl)
+    assert np.array_equal(counts.cpu().numpy(), rc)
+
+
+@pytest.mark.parametrize("pair", [False, True])
+def test_router_compaction_unaligned_and_1d(cuda_device, pair):
+    from switchattentionkernels_b200 import build_switch_query_indices_from_router
+    S = 5003
+    per = 2 if pair else 1
+    g = torch.Generator().manual_seed(11)
+    big = torch.randn(S * per + 1, generator=g).to(torch.bfloat16).to(cuda_device)
+    r = big[1:].view(S, 2) if pair else big[1:]   # starts 2 bytes past a 16-byte boundary
+    full, local, counts = build_switch_query_indices_from_router(r, threshold=0.1, pair=pair)
+    mask = oracle_idx.router_mask(r.float().cpu().numpy()[None], pair=pair, threshold=0.1)
+    rf, rl, rc = oracle_idx.compact_mask_batched(mask)
+    assert np.array_equal(full.cpu().numpy(), rf) and np.array_equal(local.cpu().numpy(), rl)
+    assert np.array_equal(counts.cpu().numpy(), rc)
+
+
+def test_router_compaction_errors(cuda_device):
+    from switchattentionkernels_b200 import build_switch_query_indices_from_router
+    with pytest.raises(TypeError):
+        build_switch_query_indices_from_router(torch.zeros(10, dtype=torch.float16, device=cuda_device))
+    with pytest.raises(ValueError):
+        build_switch_query_indices_from_router(torch.zeros(2, 10, 3, device=cuda_device), pair=True)
+    with pytest.raises(TypeError):
+        build_switch_query_indices_from_router(torch.zeros(10))
+
+
+@pytest.mark.parametrize("B,S,p", [(1, 1 << 20, 0.3), (3, 100003, 0.5), (2, 4097, 0.5), (2, 70000, 0.0),
+                                   (2, 70000, 1.0)])
+def test_chunked_compaction_bit_exact(cuda_device, B, S, p):
+    # rows longer than one 4096-token chunk are split over several CTAs
+    g = torch.Generator().manual_seed(B + S)
+    mask = torch.rand(B, S, generator=g) < p
+    full, local, counts = build_switch_query_indices_batched(mask.to(cuda_device))
+    rf, rl, rc = oracle_idx.compact_mask_batched(mask.numpy())
+    assert np.array_equal(counts.cpu().numpy(), rc)
+    assert np.array_equal(full.cpu().numpy(), rf)
+    assert np.array_equal(local.cpu().numpy(), rl)
+
+
+def test_chunked_compaction_unaligned_rows(cuda_device):
+    B, S = 3, 9001   # odd row length: rows 1 and 2 start off a 16-byte boundary
+    g = torch.Generator().manual_seed(5)
+    mask = torch.rand(B, S, generator=g) < 0.4
+    full, local, counts = build_switch_query_indices_batched(mask.to(cuda_device))
+    rf, rl, rc = oracle_idx.compact_mask_batched(mask.numpy())
+    assert np.array_equal(full.cpu().numpy(), rf) and np.array_equal(local.cpu().numpy(), rl)
+    assert np.array_equal(counts.cpu().numpy(), rc)
+
+
+def test_chunked_and_single_cta_paths_agree(cuda_device):
+    from switchattentionkernels_b200 import _native
+    lib = _native.load()
+    B, S = 2, 50000
+    g = torch.Generator().manual_seed(9)
+    mask = (torch.rand(B, S, generator=g) < 0.2).to(cuda_device)
+    outs = []
+    for chunked in (False, True):
+        full = torch.empty(B, S, dtype=torch.int32, device=cuda_device)
+        local = torch.empty_like(full)
+        counts = torch.empty(B, 2, dtype=torch.int32, device=cuda_device)
+        if chunked:
+            n = int(lib.swa_compact_workspace_elems(B, S))
+            assert n == B * ((S + 4095) // 4096)
+            ws = torch.empty(n, dtype=torch.int32, device=cuda_device)
+            rc = lib.swa_compact_mask_ws(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
+                                         _native.ptr(counts), _native.ptr(ws), n, _native.stream_ptr(cuda_device))
+            assert lib.swa_compact_mask_ws(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
+                                           _native.ptr(counts), _native.ptr(ws), n - 1,
+                                           _native.stream_ptr(cuda_device)) != 0   # workspace too small
+        else:
+            rc = lib.swa_compact_mask(_native.ptr(mask), B, S, _native.ptr(full), _native.ptr(local),
+                                      _native.ptr(counts), _native.stream_ptr(cuda_device))
+        assert rc == 0
+        outs.append((full.cpu(), local.cpu(), counts.cpu()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
