@@ -104,6 +104,23 @@ int swa_compact_router_ws(const void* router, int dtype, int pair, float thresho
                           int32_t* local, int32_t* counts, int32_t* workspace, int64_t workspace_elems,
                           void* stream);
 
+/* Decode step (no counterpart in the reference, which is prefill only): one
+ * new query token per sequence against its KV cache, routed per sequence.
+ *   q [B, Hq, 128] bf16; k_cache, v_cache [B, Smax, Hkv, 128] bf16;
+ *   seq_lens int32 [B]: cached keys of sequence b including the new token
+ *   (1 <= L <= Smax; the new token's K/V sit at row L - 1);
+ *   route uint8 [B]: non-zero = full causal attention (keys [0, L)), zero =
+ *   sliding window (keys [max(0, L - window), L));
+ *   out [B, Hq, 128] bf16, lse [B, Hq] fp32 (log2 domain, as the prefill).
+ * workspace: at least swa_decode_workspace_bytes(B, Smax, Hq, Hkv) bytes,
+ * 16-byte aligned; int32 workspace[0] receives the status bits
+ * (SWA_STATUS_TIMEOUT) of the launch. */
+size_t swa_decode_workspace_bytes(int B, int Smax, int Hq, int Hkv);
+int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_lens,
+                       const uint8_t* route, void* out, float* lse, int B, int Smax, int Hq, int Hkv,
+                       int head_dim, int window, float scale_log2, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* Capacity-bucket preparation and validation of one index list per batch row
  * (replaces _prepare_indices, swiattn_gqa_prefill_varlen.py:271-304).
  *   idx [B, N]; trailing_pad = 0: all N entries are routed rows (the reference

@@ -111,6 +111,36 @@ def prefill_rows(q, k, v, b: int, positions, is_local: bool, *, window: int, sm_
     return O, LSE
 
 
+def decode_rows(q, k, v, seq_lens, route_full, *, window: int, sm_scale=None):
+    """Exact FP32 decode step: ``(O [B, Hq, D], LSE [B, Hq])``.
+
+    The row semantics of the reference kernels (``swiattn_gqa_prefill.py:145-158``:
+    full rows see keys ``[0, t]``, local rows ``[t - W + 1, t]``) at the last
+    position ``t = L - 1`` of each sequence, ``L = seq_lens[b]``; ``q`` is
+    ``[B, Hq, D]``, ``k`` / ``v`` are ``[B, Smax, Hkv, D]``.  The reference itself is
+    prefill only; this is its formula for one row per sequence.
+    """
+    B, Hq, D = q.shape
+    Hkv = k.shape[2]
+    r = Hq // Hkv
+    sl2 = scale_log2_of(sm_scale, D)
+    O = torch.empty((B, Hq, D), dtype=torch.float32)
+    LSE = torch.empty((B, Hq), dtype=torch.float32)
+    for b in range(B):
+        L = int(seq_lens[b])
+        lo = 0 if bool(route_full[b]) else max(0, L - window)
+        qb = q[b].float().view(Hkv, r, D)
+        kb = k[b, lo:L].float()
+        vb = v[b, lo:L].float()
+        s = torch.einsum("grd,lgd->grl", qb, kb) * sl2
+        m = s.amax(dim=-1, keepdim=True)
+        pe = torch.exp2(s - m)
+        den = pe.sum(dim=-1, keepdim=True)
+        O[b] = (torch.einsum("grl,lgd->grd", pe, vb) / den).reshape(Hq, D)
+        LSE[b] = (m + torch.log2(den)).reshape(Hq)
+    return O, LSE
+
+
 def prefill_dense(q, k, v, full_lists, local_lists, *, window: int, sm_scale=None, metadata=None,
                   subset=None, budget_bytes: int = 1 << 28):
     """Exact FP32 result.  ``q``: ``[B,Sq,Hq,D]``, ``k``/``v``: ``[B,Skv,Hkv,D]`` (any float dtype, CPU).

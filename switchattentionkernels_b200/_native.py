@@ -41,6 +41,8 @@ EXPORTED = (
     "swa_noalloc_max_batch",
     "swa_prefill_forward_noalloc",
     "swa_test_withhold_kv_load",
+    "swa_decode_workspace_bytes",
+    "swa_decode_forward",
 )
 
 _lock = threading.Lock()
@@ -103,6 +105,16 @@ def _declare(lib) -> None:
     ]
     lib.swa_test_withhold_kv_load.restype = None
     lib.swa_test_withhold_kv_load.argtypes = [_i]
+    lib.swa_decode_workspace_bytes.restype = _sz
+    lib.swa_decode_workspace_bytes.argtypes = [_i, _i, _i, _i]
+    lib.swa_decode_forward.restype = _i
+    lib.swa_decode_forward.argtypes = [
+        _p, _p, _p, _p, _p,    # q, k_cache, v_cache, seq_lens, route
+        _p, _p,                # out, lse
+        _i, _i, _i, _i, _i,    # B, Smax, Hq, Hkv, head_dim
+        _i, _f,                # window, scale_log2
+        _p, _sz, _p,           # workspace, workspace_bytes, stream
+    ]
 
 
 def load():

@@ -1,4 +1,5 @@
 // C ABI of libswattn_b200 (declared in include/swattn_b200.h).
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <string>
@@ -142,6 +143,110 @@ int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_le
                                              q_segment_ids, kv_segment_ids, full_starts, local_starts, causal_ends,
                                              static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "build_metadata launch");
+  return SWA_OK;
+}
+
+namespace {
+
+// Split of the decode step's key axis: enough (split, unit) CTAs for a few
+// waves over the SMs, each split a multiple of 64 keys and at least 256.
+struct DecodeSplit {
+  int nhb, splits, split_keys;
+};
+
+DecodeSplit decode_split(int B, int Smax, int Hq, int Hkv, int num_sms) {
+  DecodeSplit d{};
+  const int r = Hq / Hkv;
+  d.nhb = (r + 15) / 16;
+  const int64_t units = static_cast<int64_t>(B) * Hkv * d.nhb;
+  const int64_t want = 4LL * num_sms;
+  int splits = static_cast<int>(std::max<int64_t>(1, (want + units - 1) / units));
+  splits = std::min(splits, std::max(1, (Smax + 255) / 256));
+  int sk = (Smax + splits - 1) / splits;
+  sk = (sk + 63) / 64 * 64;
+  d.split_keys = std::max(sk, 64);
+  d.splits = (Smax + d.split_keys - 1) / d.split_keys;
+  return d;
+}
+
+size_t decode_ws_bytes(int B, int Hkv, const DecodeSplit& d) {
+  const size_t parts = static_cast<size_t>(B) * Hkv * d.nhb * d.splits;
+  return 16 + parts * 16 * 2 * sizeof(float) + parts * 16 * 128 * sizeof(float);
+}
+
+int device_sms(int* nsm) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (major != 10) return fail(SWA_E_UNSUPPORTED, "this library targets sm_100 (B200) devices");
+  return SWA_OK;
+}
+
+}  // namespace
+
+size_t swa_decode_workspace_bytes(int B, int Smax, int Hq, int Hkv) {
+  if (B <= 0 || Smax <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) return 0;
+  int nsm = 0;
+  if (device_sms(&nsm) != SWA_OK) return 0;
+  return decode_ws_bytes(B, Hkv, decode_split(B, Smax, Hq, Hkv, nsm));
+}
+
+int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_lens,
+                       const uint8_t* route, void* out, float* lse, int B, int Smax, int Hq, int Hkv,
+                       int head_dim, int window, float scale_log2, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
+  if (B <= 0 || Smax <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
+  if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
+  if (window <= 0) return fail(SWA_E_INVALID, "window_size must be positive");
+  if (!(scale_log2 > 0.0f)) return fail(SWA_E_INVALID, "softmax scale must be positive");
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || seq_lens == nullptr || route == nullptr ||
+      out == nullptr || lse == nullptr || workspace == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) || !aligned16(workspace))
+    return fail(SWA_E_INVALID, "q/k/v/out/workspace must be 16-byte aligned");
+  if (static_cast<int64_t>(B) * Smax * Hkv >= (int64_t(1) << 31))
+    return fail(SWA_E_UNSUPPORTED, "KV cache too large for 32-bit row indices");
+  int nsm = 0;
+  int rc = device_sms(&nsm);
+  if (rc != SWA_OK) return rc;
+  const DecodeSplit d = decode_split(B, Smax, Hq, Hkv, nsm);
+  if (workspace_bytes < decode_ws_bytes(B, Hkv, d)) return fail(SWA_E_INVALID, "workspace too small");
+
+  swa::DecodeParams p{};
+  const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Smax), static_cast<uint64_t>(B)};
+  const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Smax) * Hkv * 256};
+  const uint32_t kb[4] = {64, 1, 64, 1};
+  if (!swa::make_bf16_map_sw128(&p.k_map, k_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+  if (!swa::make_bf16_map_sw128(&p.v_map, v_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  const size_t parts = static_cast<size_t>(B) * Hkv * d.nhb * d.splits;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.status = reinterpret_cast<int32_t*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + 16);
+  p.part_o = reinterpret_cast<float*>(ws + 16 + parts * 16 * 2 * sizeof(float));
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.seq_lens = seq_lens;
+  p.route = route;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.B = B;
+  p.Smax = Smax;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.r = Hq / Hkv;
+  p.nhb = d.nhb;
+  p.splits = d.splits;
+  p.split_keys = d.split_keys;
+  p.window = window;
+  p.scale_log2 = scale_log2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(p.status, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  e = swa::launch_decode(p, s);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return SWA_OK;
 }
 

@@ -1,0 +1,376 @@
+// Switch Attention GQA decode step on B200 (sm_100a): one new query token per
+// sequence attends to its KV cache, through full causal attention (keys
+// [0, L)) or the causal sliding window (keys [max(0, L - W), L)), where L is
+// the sequence's cached length including the new token.  This is the
+// reference's row semantics (swiattn_gqa_prefill.py:145-158) at the last
+// position t = L - 1 of each sequence, with the routing decided per sequence.
+//
+// The step is HBM-bound: every K/V element is read once and used by the r
+// query heads of its group (about r FLOP per byte).  Layout of the work:
+//   grid (split, KV group x head block, batch); a head block is 16 query heads
+//   of one group (rows beyond r are zero), a split a contiguous range of the
+//   sequence's legal keys.
+//   warp 4  producer : TMA loads of 64-key K and V tiles (128B swizzle, two
+//                      64-dim halves each) into a 4-entry ring (mbarriers).
+//   warps 0-3 math   : warp w takes keys [16 w, 16 w + 16) of every tile:
+//                      S = Q K^T and O += P V with mma.sync m16n8k16 (BF16 in,
+//                      FP32 accumulate; the 16-row M dimension holds the
+//                      head block), online softmax in the log2 domain, P
+//                      rounded to BF16 before P V as in the prefill path.
+//   The four warps' (max, sum, O) are merged in shared memory; the split's
+//   partial goes to the workspace and a second kernel merges the splits and
+//   writes O (BF16) and LSE (FP32, log2 units).
+// Tensor cores run far below their peak here (M = 16 covers r <= 16 heads);
+// the bound is HBM bandwidth, which the TMA ring keeps busy.
+#include "sm100.cuh"
+#include "swattn_internal.h"
+
+namespace swa {
+
+namespace {
+
+constexpr int kDecStages = 4;
+constexpr int kDecTileKeys = 64;
+constexpr int kDecHalfBytes = kDecTileKeys * 128;        // 64 keys x 64 dims x 2 B
+constexpr int kDecStageBytes = 4 * kDecHalfBytes;        // K h0, K h1, V h0, V h1
+constexpr int kDecThreads = 160;                         // 4 math warps + 1 producer warp
+constexpr int kDecQBytes = 2 * 16 * 128;                 // 16 rows x 2 halves x 128 B
+
+struct DecSmem {
+  static constexpr uint32_t stages = 0;
+  static constexpr uint32_t q = stages + kDecStages * kDecStageBytes;
+  static constexpr uint32_t bars = q + kDecQBytes;       // full[4], empty[4]
+  static constexpr uint32_t misc = bars + 2 * kDecStages * 8;
+  static constexpr uint32_t ml = misc + 16;              // [4 warps][16 rows][2] floats
+  static constexpr uint32_t total = ml + 4 * 16 * 2 * 4;
+};
+constexpr uint32_t kDecSmemBytes = DecSmem::total + 1024;
+
+// byte offset of 16-byte chunk `c` (0..15 over the 128 dims) of row `row` in a
+// tile stored as two 64-dim halves of `rows` x 128 B rows, 128B swizzle
+__device__ __forceinline__ uint32_t swz(int rows, int row, int c) {
+  return static_cast<uint32_t>((c >> 3) * rows * 128 + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+struct DecRange {
+  int s0, s1;  // keys of this split
+};
+
+__device__ __forceinline__ DecRange split_range(const DecodeParams& p, int b, int split) {
+  const int L = min(max(p.seq_lens[b], 0), p.Smax);
+  const int lo = p.route[b] != 0 ? 0 : max(0, L - p.window);
+  const int s0 = lo + split * p.split_keys;
+  return DecRange{s0, min(L, s0 + p.split_keys)};
+}
+
+__global__ void __launch_bounds__(kDecThreads, 1) switch_decode_kernel(const __grid_constant__ DecodeParams p) {
+  const int split = blockIdx.x;
+  const int g = blockIdx.y / p.nhb;
+  const int hb = blockIdx.y % p.nhb;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t part = ((static_cast<int64_t>(b) * p.Hkv + g) * p.nhb + hb) * p.splits + split;
+  float* po = p.part_o + part * 16 * 128;
+  float* pml = p.part_ml + part * 16 * 2;
+  const DecRange rg = split_range(p, b, split);
+  if (rg.s1 <= rg.s0) {  // nothing of this sequence falls in this split
+    for (int i = threadIdx.x; i < 16 * 128; i += kDecThreads) po[i] = 0.0f;
+    if (threadIdx.x < 16) {
+      pml[2 * threadIdx.x] = -INFINITY;
+      pml[2 * threadIdx.x + 1] = 0.0f;
+    }
+    return;
+  }
+  const int ntiles = (rg.s1 - rg.s0 + kDecTileKeys - 1) / kDecTileKeys;
+
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DecSmem::bars);
+  uint64_t* empty = full + kDecStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + DecSmem::misc);
+  float* ml = reinterpret_cast<float*>(smem + DecSmem::ml);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  // Q head block into shared memory (two 64-dim halves, 128B swizzle): thread t
+  // copies 16-byte chunks; rows of heads past r are zero
+  const int head0 = g * p.r + hb * 16;
+  for (int i = threadIdx.x; i < 16 * 16; i += kDecThreads) {
+    const int row = i >> 4, c = i & 15;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (hb * 16 + row < p.r)
+      val = *reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(b) * p.Hq + head0 + row) * 128 + 8 * c);
+    *reinterpret_cast<uint4*>(smem + DecSmem::q + swz(16, row, c)) = val;
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.k_map);
+      tma_prefetch_desc(&p.v_map);
+      int t = 0;
+      for (; t < ntiles; ++t) {
+        const int s = t % kDecStages;
+        if (!mbar_wait(&empty[s], ((t / kDecStages) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], kDecStageBytes);
+        uint8_t* dst = smem + DecSmem::stages + s * kDecStageBytes;
+        const int key0 = rg.s0 + t * kDecTileKeys;
+        tma_load_4d(dst, &p.k_map, &full[s], 0, g, key0, b);
+        tma_load_4d(dst + kDecHalfBytes, &p.k_map, &full[s], 64, g, key0, b);
+        tma_load_4d(dst + 2 * kDecHalfBytes, &p.v_map, &full[s], 0, g, key0, b);
+        tma_load_4d(dst + 3 * kDecHalfBytes, &p.v_map, &full[s], 64, g, key0, b);
+      }
+      if (*abort_flag) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int u = max(0, t - kDecStages); u < t; ++u) {
+          volatile int dummy = 0;
+          mbar_wait(&full[u % kDecStages], (u / kDecStages) & 1, &dummy);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ math warps
+    const uint32_t q_base = smem_u32(smem + DecSmem::q);
+    uint32_t qa[8][4];  // A fragments of the 16 x 128 Q block, one per 16-dim k step
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int mat = lane >> 3;
+      const int row = (mat & 1) * 8 + (lane & 7);
+      const int c = 2 * ks + (mat >> 1);
+      ldsm_x4(q_base + swz(16, row, c), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    }
+    const int qr = lane >> 2;          // rows qr and qr + 8 of the head block
+    const int qc = 2 * (lane & 3);     // columns qc, qc + 1 of each 8-wide n tile
+    float m[2] = {-INFINITY, -INFINITY};
+    float l[2] = {0.0f, 0.0f};
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    const float sl2 = p.scale_log2;
+    const int klo = p.route[b] != 0 ? 0 : max(0, min(max(p.seq_lens[b], 0), p.Smax) - p.window);
+    const int khi = rg.s1;
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % kDecStages;
+      if (!mbar_wait(&full[s], (t / kDecStages) & 1, abort_flag)) break;
+      const uint32_t kb = smem_u32(smem + DecSmem::stages + s * kDecStageBytes);
+      const uint32_t vb = kb + 2 * kDecHalfBytes;
+      // S = Q K^T for this warp's 16 keys (two n tiles of 8)
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int mat = lane >> 3;
+        const int key = 16 * warp + (mat >> 1) * 8 + (lane & 7);
+        const int c = 2 * ks + (mat & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
+        mma_bf16(sc[0], qa[ks], b0, b1);
+        mma_bf16(sc[1], qa[ks], b2, b3);
+      }
+      // mask, online softmax (rows qr, qr + 8)
+      const int key0 = rg.s0 + t * kDecTileKeys + 16 * warp;
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key0 + 8 * n + qc + (e & 1);
+          const float x = (key >= klo && key < khi) ? sc[n][e] * sl2 : -INFINITY;
+          sc[n][e] = x;
+          mx[e >> 1] = fmaxf(mx[e >> 1], x);
+        }
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float mn = fmaxf(m[h], mx[h]);
+        alpha[h] = (mn == -INFINITY) ? 1.0f : ex2_approx(m[h] - mn);
+        m[h] = mn;
+        l[h] *= alpha[h];
+      }
+      uint32_t pa[4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mh = m[e >> 1];
+          pv[e] = (mh == -INFINITY) ? 0.0f : ex2_approx(sc[n][e] - mh);
+          l[e >> 1] += pv[e];
+        }
+        pa[2 * n] = pack_bf16x2(pv[0], pv[1]);
+        pa[2 * n + 1] = pack_bf16x2(pv[2], pv[3]);
+      }
+      // O of earlier tiles to the new running maximum
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= alpha[0];
+        o[n][1] *= alpha[0];
+        o[n][2] *= alpha[1];
+        o[n][3] *= alpha[1];
+      }
+      // O += P V: P (16 rows x 16 keys) as the A fragment, V via transposed ldmatrix
+      const uint32_t a[4] = {pa[0], pa[1], pa[2], pa[3]};
+#pragma unroll
+      for (int nd = 0; nd < 16; nd += 2) {
+        const int mat = lane >> 3;
+        const int key = 16 * warp + (mat & 1) * 8 + (lane & 7);
+        const int c = nd + (mat >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
+        mma_bf16(o[nd], a, b0, b1);
+        mma_bf16(o[nd + 1], a, b2, b3);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // row sums over the quad
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+    }
+    if ((lane & 3) == 0) {
+      ml[(warp * 16 + qr) * 2] = m[0];
+      ml[(warp * 16 + qr) * 2 + 1] = l[0];
+      ml[(warp * 16 + qr + 8) * 2] = m[1];
+      ml[(warp * 16 + qr + 8) * 2 + 1] = l[1];
+    }
+    named_bar_sync(1, 128);
+    // A warp that gave up a wait set the flag before this barrier, so all four
+    // agree.  Then loads may still be landing in the ring: leave it alone.
+    if (*abort_flag) goto done;
+    {
+    // merge the four warps: scale to the block maximum, sum into the partial
+    float f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = qr + 8 * h;
+      float mc = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) mc = fmaxf(mc, ml[(w * 16 + row) * 2]);
+      f[h] = (m[h] == -INFINITY) ? 0.0f : ex2_approx(m[h] - mc);
+      if (warp == 0 && (lane & 3) == 0) {
+        float lc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const float mw = ml[(w * 16 + row) * 2];
+          lc += (mw == -INFINITY) ? 0.0f : ml[(w * 16 + row) * 2 + 1] * ex2_approx(mw - mc);
+        }
+        pml[2 * row] = mc;
+        pml[2 * row + 1] = lc;
+      }
+    }
+    // the ring is drained: reuse stage memory as a [16][128] FP32 accumulator
+    float* acc = reinterpret_cast<float*>(smem + DecSmem::stages);
+    for (int i = threadIdx.x; i < 16 * 128; i += 128) acc[i] = 0.0f;
+    named_bar_sync(1, 128);
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      atomicAdd(&acc[qr * 128 + 8 * n + qc], o[n][0] * f[0]);
+      atomicAdd(&acc[qr * 128 + 8 * n + qc + 1], o[n][1] * f[0]);
+      atomicAdd(&acc[(qr + 8) * 128 + 8 * n + qc], o[n][2] * f[1]);
+      atomicAdd(&acc[(qr + 8) * 128 + 8 * n + qc + 1], o[n][3] * f[1]);
+    }
+    named_bar_sync(1, 128);
+    for (int i = threadIdx.x; i < 16 * 128 / 4; i += 128)
+      reinterpret_cast<float4*>(po)[i] = reinterpret_cast<const float4*>(acc)[i];
+    }
+  }
+done:
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(p.status, kStatusTimeout);
+}
+
+// Merge the splits of one (batch, KV group, head block): O = sum_s O_s 2^(m_s - M) / L,
+// L = sum_s l_s 2^(m_s - M), LSE = log2 L + M (log2 units, as the prefill path).
+__global__ void __launch_bounds__(128) switch_decode_combine_kernel(const __grid_constant__ DecodeParams p) {
+  const int g = blockIdx.x / p.nhb;
+  const int hb = blockIdx.x % p.nhb;
+  const int b = blockIdx.y;
+  const int64_t part0 = ((static_cast<int64_t>(b) * p.Hkv + g) * p.nhb + hb) * p.splits;
+  __shared__ float sM[16], sL[16];
+  if (threadIdx.x < 16) {
+    const int row = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[((part0 + s) * 16 + row) * 2]);
+    float L = 0.0f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float ms = p.part_ml[((part0 + s) * 16 + row) * 2];
+      if (ms != -INFINITY) L += p.part_ml[((part0 + s) * 16 + row) * 2 + 1] * ex2_approx(ms - M);
+    }
+    sM[row] = M;
+    sL[row] = L;
+    const int h = hb * 16 + row;
+    if (h < p.r) p.lse[static_cast<int64_t>(b) * p.Hq + g * p.r + h] = lg2_approx(L) + M;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * 64; i += 128) {  // pairs of columns
+    const int row = i >> 6, c2 = (i & 63) * 2;
+    const int h = hb * 16 + row;
+    if (h >= p.r) continue;
+    float a0 = 0.0f, a1 = 0.0f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float ms = p.part_ml[((part0 + s) * 16 + row) * 2];
+      if (ms == -INFINITY) continue;
+      const float w = ex2_approx(ms - sM[row]);
+      const float2 v = *reinterpret_cast<const float2*>(p.part_o + ((part0 + s) * 16 + row) * 128 + c2);
+      a0 += v.x * w;
+      a1 += v.y * w;
+    }
+    const float inv = 1.0f / sL[row];
+    *reinterpret_cast<uint32_t*>(p.out + (static_cast<int64_t>(b) * p.Hq + g * p.r + h) * 128 + c2) =
+        pack_bf16x2(a0 * inv, a1 * inv);
+  }
+}
+
+}  // namespace
+
+uint32_t decode_smem_bytes() { return kDecSmemBytes; }
+
+cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(switch_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const dim3 grid(params.splits, params.Hkv * params.nhb, params.B);
+  switch_decode_kernel<<<grid, kDecThreads, kDecSmemBytes, stream>>>(params);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  switch_decode_combine_kernel<<<dim3(params.Hkv * params.nhb, params.B), 128, 0, stream>>>(params);
+  return cudaGetLastError();
+}
+
+}  // namespace swa

@@ -57,6 +57,24 @@ struct __align__(64) PrefillParams {
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);
 
+// Decode step: one query token per sequence against its KV cache.
+struct __align__(64) DecodeParams {
+  CUtensorMap k_map;  // 4-D {128, Hkv, Smax, B}, box {64, 1, 64, 1}, 128B swizzle
+  CUtensorMap v_map;
+  const __nv_bfloat16* q;   // [B, Hq, 128]
+  const int32_t* seq_lens;  // [B] cached keys including the new token
+  const uint8_t* route;     // [B] non-zero = full attention
+  __nv_bfloat16* out;       // [B, Hq, 128]
+  float* lse;               // [B, Hq]
+  float* part_o;            // [B, Hkv, nhb, splits, 16, 128] split partials
+  float* part_ml;           // [B, Hkv, nhb, splits, 16, 2] (max, sum) of each partial row
+  int32_t* status;
+  int B, Smax, Hq, Hkv, r, nhb, splits, split_keys, window;
+  float scale_log2;
+};
+cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream);
+uint32_t decode_smem_bytes();
+
 // Record the message returned by swa_last_error_string() on this thread.
 void set_last_error(const char* msg);
 uint32_t prefill_smem_bytes();

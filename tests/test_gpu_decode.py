@@ -1,0 +1,96 @@
+"""Decode step on the GPU against the FP32 oracle (and the prefill kernel's row
+at the same position), with the tolerances of the prefill path."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _parity import O_MAX_ABS, O_MEAN_ABS, LSE_MAX_ABS
+from oracle import attention as oracle_attn
+from switchattentionkernels_b200 import _core
+from switchattentionkernels_b200.decode import switch_gqa_decode_forward
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(dev, B, Smax, Hq, Hkv, seed, lens=None, p_full=0.5):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, 128, generator=g).bfloat16()
+    k = torch.randn(B, Smax, Hkv, 128, generator=g).bfloat16()
+    v = torch.randn(B, Smax, Hkv, 128, generator=g).bfloat16()
+    if lens is None:
+        lens = torch.randint(1, Smax + 1, (B,), generator=g)
+        lens[0] = Smax
+        if B > 1:
+            lens[1] = 1
+    lens = torch.as_tensor(lens, dtype=torch.int32)
+    route = torch.rand(B, generator=g) < p_full
+    return q, k, v, lens, route
+
+
+def _check(O, L, Oref, Lref, label):
+    O = O.float().cpu()
+    L = L.cpu()
+    err = (O - Oref).abs()
+    assert torch.isfinite(O).all(), label
+    assert err.max().item() <= O_MAX_ABS, f"{label}: O max-abs {err.max().item():.3e}"
+    assert err.mean().item() <= O_MEAN_ABS, f"{label}: O mean-abs {err.mean().item():.3e}"
+    lerr = (L - Lref).abs().max().item()
+    assert lerr <= LSE_MAX_ABS, f"{label}: LSE max-abs {lerr:.3e}"
+
+
+@pytest.mark.parametrize("B,Smax,Hq,Hkv,W", [
+    (1, 1, 8, 2, 16), (3, 100, 8, 2, 1), (5, 1000, 32, 8, 200), (4, 5000, 64, 8, 4096), (2, 3000, 32, 1, 512),
+    (7, 777, 6, 3, 64), (3, 2049, 40, 8, 1000), (33, 700, 32, 8, 128), (2, 20000, 32, 4, 2048),
+])
+def test_decode_matches_oracle(cuda_device, B, Smax, Hq, Hkv, W):
+    q, k, v, lens, route = _case(cuda_device, B, Smax, Hq, Hkv, seed=B * 7919 + Smax + W)
+    O, L = switch_gqa_decode_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                                     lens.to(cuda_device), route.to(cuda_device), window_size=W)
+    torch.cuda.synchronize()
+    Oref, Lref = oracle_attn.decode_rows(q, k, v, lens.numpy(), route.numpy(), window=W)
+    _check(O, L, Oref, Lref, f"B={B} Smax={Smax} Hq={Hq} Hkv={Hkv} W={W}")
+
+
+@pytest.mark.parametrize("p_full", [0.0, 1.0])
+def test_decode_all_one_branch_and_sm_scale(cuda_device, p_full):
+    q, k, v, lens, route = _case(cuda_device, 6, 2500, 16, 4, seed=3, p_full=p_full)
+    O, L = switch_gqa_decode_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                                     lens.to(cuda_device), route.to(cuda_device), window_size=300, sm_scale=0.05)
+    Oref, Lref = oracle_attn.decode_rows(q, k, v, lens.numpy(), route.numpy(), window=300, sm_scale=0.05)
+    _check(O, L, Oref, Lref, f"p_full={p_full}")
+
+
+def test_decode_equals_the_prefill_row_at_the_last_position(cuda_device):
+    dev = cuda_device
+    B, S, Hq, Hkv, W = 3, 1500, 16, 4, 300
+    g = torch.Generator().manual_seed(17)
+    qf = torch.randn(B, S, Hq, 128, generator=g).bfloat16().to(dev)
+    k = torch.randn(B, S, Hkv, 128, generator=g).bfloat16().to(dev)
+    v = torch.randn(B, S, Hkv, 128, generator=g).bfloat16().to(dev)
+    route = torch.tensor([True, False, True])
+    # the prefill path with every position routed like the last one
+    mask = route[:, None].expand(B, S).to(dev).contiguous()
+    full, local, counts = _core.build_switch_query_indices_batched(mask)
+    Op, Lp = _core.forward(qf, k, v, full, local, window_size=W, query_counts=counts)
+    lens = torch.full((B,), S, dtype=torch.int32, device=dev)
+    O, L = switch_gqa_decode_forward(qf[:, -1].contiguous(), k, v, lens, route.to(dev), window_size=W)
+    torch.cuda.synchronize()
+    _check(O, L, Op[:, -1].float().cpu(), Lp[:, -1].cpu(), "decode vs prefill row")
+
+
+def test_decode_arguments(cuda_device):
+    dev = cuda_device
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16, device=dev)
+    k = torch.zeros(2, 10, 2, 128, dtype=torch.bfloat16, device=dev)
+    lens = torch.ones(2, dtype=torch.int32, device=dev)
+    route = torch.ones(2, dtype=torch.bool, device=dev)
+    with pytest.raises(ValueError):
+        switch_gqa_decode_forward(q, k, k, lens, route, window_size=0)
+    with pytest.raises(ValueError):
+        switch_gqa_decode_forward(q, k, k, lens.long(), route)
+    with pytest.raises(TypeError):
+        switch_gqa_decode_forward(q.float(), k, k, lens, route)
+    O, L = switch_gqa_decode_forward(q.unsqueeze(1), k, k, lens, route)
+    assert O.shape == (2, 1, 8, 128) and L.shape == (2, 1, 8)

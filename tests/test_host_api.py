@@ -142,7 +142,7 @@ def test_bucket_capacity_matches_oracle(count, block_m):
 
 def test_library_exports_every_header_symbol():
     header = open(os.path.join(ROOT, "include", "swattn_b200.h")).read()
-    declared = set(re.findall(r"^(?:int|int64_t|void|const char\*)\s+(swa_\w+)\(", header, flags=re.M))
+    declared = set(re.findall(r"^(?:int|int64_t|size_t|void|const char\*)\s+(swa_\w+)\(", header, flags=re.M))
     assert declared == set(_native.EXPORTED)
     lib = _native.load()  # loads without a GPU; no compute call is made
     for name in declared:
