@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--cp", action="store_true",
                     help="instead of the default line: context-parallel prefill over the N ranks "
                          "(strong scaling; K/V all-gather + kernel per step)")
+    ap.add_argument("--decode", action="store_true",
+                    help="instead of the default line: one decode step (one new token per sequence) over a KV cache")
     ap.add_argument("--cp-config", type=int, choices=[4, 5], default=4,
                     help="--cp workload: 4 = the varlen packed batch, 5 = one 131072-token sequence of config 5")
     return ap.parse_args()
@@ -244,6 +246,76 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def run_decode(args, world, rank, local_rank):
+    """Decode step of the config-3 model shape: 64 sequences with 16K-32K cached
+    keys each, Hq 32 / Hkv 8, W 1024, each new token routed full with p = 0.125.
+
+    HBM-bound: ``value`` = legal K/V bytes read per step / step time (GB/s),
+    against the measured copy bandwidth; ``tokens_per_s`` = sequences / step
+    time.  With N ranks every rank runs its own batch (weak scaling).
+    """
+    from switchattentionkernels_b200.decode import switch_gqa_decode_forward
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, Smax, Hq, Hkv, W, p_full = 64, 32768, 32, 8, 1024, 0.125
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    q = torch.randn((B, Hq, 128), generator=g, device=dev).bfloat16()
+    k = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
+    v = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
+    lens = torch.randint(Smax // 2, Smax + 1, (B,), generator=g, device=dev, dtype=torch.int32)
+    route = torch.rand((B,), generator=g, device=dev) < p_full
+    L = lens.cpu().numpy().astype(np.int64)
+    keys = np.where(route.cpu().numpy(), L, np.minimum(L, W))
+    kv_bytes = float(keys.sum()) * Hkv * 128 * 2 * 2
+    for _ in range(args.warmup):
+        switch_gqa_decode_forward(q, k, v, lens, route, window_size=W)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.mark("begin")
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        switch_gqa_decode_forward(q, k, v, lens, route, window_size=W)
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark("end")
+    clock_info = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.destroy_process_group()
+    if rank == 0:
+        hbm = None
+        path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        if os.path.exists(path):
+            with open(path) as fh:
+                hbm = float(json.load(fh).get("hbm_gbs", 0.0)) or None
+        peak = hbm or 6650.0
+        gbs = kv_bytes * world / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "decode step: legal K/V bytes read per second", "value": gbs, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "tokens_per_s": B * world / (ms * 1e-3),
+            "config": {"workload": "decode: 64 sequences, 16K-32K cached keys, Hq 32, Hkv 8, W 1024, p_full 0.125",
+                       "kv_bytes_per_step": kv_bytes},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "peak_source": "measured hbm_gbs" if hbm else "fallback"},
+            "gpu_launches": 2 * args.steps,  # split-KV kernel + merge per step
+            "clocks": clock_info,
+        }), flush=True)
+    return 0
+
+
 def run_cp(args, world, rank, local_rank):
     """Context-parallel prefill of one packed batch over ``world`` ranks.
 
@@ -342,6 +414,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.decode and args.impl == "ours":
+        return run_decode(args, world, rank, local_rank)
     if args.cp and args.impl == "ours":
         rc = run_cp(args, world, rank, local_rank)
         if world > 1:

@@ -148,8 +148,12 @@ int swa_build_metadata(const int32_t* cu_seqlens, int nseg, int q_len, int kv_le
 
 namespace {
 
-// Split of the decode step's key axis: enough (split, unit) CTAs for a few
-// waves over the SMs, each split a multiple of 64 keys and at least 256.
+// Split of the decode step's key axis.  Which sequences attend to all their
+// keys is device data, so splits are sized for the longest possible range
+// (Smax): about four waves of CTAs over the SMs if every range were full,
+// clamped to 256..2048 keys (a multiple of 64) so that a long full-attention
+// sequence is spread over many CTAs instead of forming the tail; splits past a
+// sequence's range exit at once.
 struct DecodeSplit {
   int nhb, splits, split_keys;
 };
@@ -159,12 +163,11 @@ DecodeSplit decode_split(int B, int Smax, int Hq, int Hkv, int num_sms) {
   const int r = Hq / Hkv;
   d.nhb = (r + 15) / 16;
   const int64_t units = static_cast<int64_t>(B) * Hkv * d.nhb;
-  const int64_t want = 4LL * num_sms;
-  int splits = static_cast<int>(std::max<int64_t>(1, (want + units - 1) / units));
-  splits = std::min(splits, std::max(1, (Smax + 255) / 256));
-  int sk = (Smax + splits - 1) / splits;
+  int64_t sk = (static_cast<int64_t>(Smax) * units + 4LL * num_sms - 1) / (4LL * num_sms);
   sk = (sk + 63) / 64 * 64;
-  d.split_keys = std::max(sk, 64);
+  sk = std::min<int64_t>(std::max<int64_t>(sk, 256), 2048);
+  sk = std::min<int64_t>(sk, (static_cast<int64_t>(Smax) + 63) / 64 * 64);
+  d.split_keys = static_cast<int>(sk);
   d.splits = (Smax + d.split_keys - 1) / d.split_keys;
   return d;
 }
