@@ -111,6 +111,46 @@ def prefill_rows(q, k, v, b: int, positions, is_local: bool, *, window: int, sm_
     return O, LSE
 
 
+def prefill_backward(q, k, v, dout, full_lists, local_lists, *, window: int, sm_scale=None, metadata=None):
+    """FP32 ``(dq, dk, dv)`` of the prefill forward for the upstream gradient ``dout``.
+
+    Autograd over the same restatement as ``prefill_rows`` (masks of
+    ``swiattn_gqa_prefill.py:145-158`` / metadata bounds, scaled softmax, P V);
+    the reference itself is forward only.  Rows without a legal key carry no
+    gradient.  Small cases only: one dense ``[rows, heads, Skv]`` score block per
+    (batch, branch).
+    """
+    B, Sq, Hq, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    r = Hq // Hkv
+    scale = sm_scale if sm_scale is not None else (1.0 / D) ** 0.5
+    qf = q.detach().float().clone().requires_grad_(True)
+    kf = k.detach().float().clone().requires_grad_(True)
+    vf = v.detach().float().clone().requires_grad_(True)
+    loss = torch.zeros(())
+    for b in range(B):
+        for is_local, lst in ((False, full_lists[b]), (True, local_lists[b])):
+            pos = np.asarray(lst, dtype=np.int64)
+            if pos.size == 0:
+                continue
+            lo, hi = row_bounds(pos, is_local, window, Skv, metadata)
+            keep = hi > lo
+            pos, lo, hi = pos[keep], lo[keep], hi[keep]
+            if pos.size == 0:
+                continue
+            n = pos.size
+            qc = qf[b, torch.from_numpy(pos)].view(n, Hkv, r, D)
+            s = torch.einsum("ngrd,lgd->ngrl", qc, kf[b]) * scale
+            keys = torch.arange(Skv)
+            legal = (keys[None, :] >= torch.from_numpy(lo)[:, None]) & (keys[None, :] < torch.from_numpy(hi)[:, None])
+            s = s.masked_fill(~legal[:, None, None, :], float("-inf"))
+            o = torch.einsum("ngrl,lgd->ngrd", torch.softmax(s, dim=-1), vf[b]).reshape(n, Hq, D)
+            loss = loss + (o * dout[b, torch.from_numpy(pos)].float()).sum()
+    loss.backward()
+    zero = lambda t, g: g if g is not None else torch.zeros_like(t)  # noqa: E731
+    return zero(qf, qf.grad), zero(kf, kf.grad), zero(vf, vf.grad)
+
+
 def decode_rows(q, k, v, seq_lens, route_full, *, window: int, sm_scale=None):
     """Exact FP32 decode step: ``(O [B, Hq, D], LSE [B, Hq])``.
 

@@ -43,6 +43,7 @@ EXPORTED = (
     "swa_test_withhold_kv_load",
     "swa_decode_workspace_bytes",
     "swa_decode_forward",
+    "swa_prefill_backward",
 )
 
 _lock = threading.Lock()
@@ -105,6 +106,16 @@ def _declare(lib) -> None:
     ]
     lib.swa_test_withhold_kv_load.restype = None
     lib.swa_test_withhold_kv_load.argtypes = [_i]
+    lib.swa_prefill_backward.restype = _i
+    lib.swa_prefill_backward.argtypes = [
+        _p, _p, _p, _p, _p, _p,  # q, k, v, o, lse, dout
+        _p, _p, _i, _i, _p,      # full_idx, local_idx, full_stride, local_stride, counts
+        _p, _p, _p,              # full_starts, local_starts, causal_ends
+        _p, _p, _p,              # dq, dk, dv
+        _i, _i, _i, _i, _i, _i,  # B, Sq, Skv, Hq, Hkv, head_dim
+        _i, _f,                  # window, scale_log2
+        _p, _sz, _p,             # workspace, workspace_bytes, stream
+    ]
     lib.swa_decode_workspace_bytes.restype = _sz
     lib.swa_decode_workspace_bytes.argtypes = [_i, _i, _i, _i]
     lib.swa_decode_forward.restype = _i

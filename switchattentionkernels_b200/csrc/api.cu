@@ -253,6 +253,75 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
   return SWA_OK;
 }
 
+int swa_prefill_backward(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                         const void* dout, const int32_t* full_idx, const int32_t* local_idx, int full_stride,
+                         int local_stride, const int32_t* counts, const int32_t* full_starts,
+                         const int32_t* local_starts, const int32_t* causal_ends, void* dq, void* dk, void* dv,
+                         int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window, float scale_log2,
+                         float* workspace, size_t workspace_bytes, void* stream) {
+  if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
+  if (B <= 0 || Sq <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
+  if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
+  if (window <= 0) return fail(SWA_E_INVALID, "window_size must be positive");
+  if (!(scale_log2 > 0.0f)) return fail(SWA_E_INVALID, "softmax scale must be positive");
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || lse == nullptr || dout == nullptr ||
+      dq == nullptr || dk == nullptr || dv == nullptr || counts == nullptr || workspace == nullptr)
+    return fail(SWA_E_INVALID, "null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dout) || !aligned16(dq) ||
+      !aligned16(dk) || !aligned16(dv))
+    return fail(SWA_E_INVALID, "tensors must be 16-byte aligned");
+  if (full_stride < 0 || local_stride < 0 || (full_stride > 0 && full_idx == nullptr) ||
+      (local_stride > 0 && local_idx == nullptr))
+    return fail(SWA_E_INVALID, "bad index lists");
+  const bool has_meta = causal_ends != nullptr;
+  if (has_meta && (full_starts == nullptr || local_starts == nullptr))
+    return fail(SWA_E_INVALID, "metadata needs full_starts, local_starts and causal_ends");
+  if (workspace_bytes < static_cast<size_t>(B) * Sq * Hq * sizeof(float))
+    return fail(SWA_E_INVALID, "workspace must hold B * Sq * Hq floats");
+  if (static_cast<int64_t>(B) * Sq * Hq >= (int64_t(1) << 31) || static_cast<int64_t>(B) * Skv * Hkv >= (int64_t(1) << 31))
+    return fail(SWA_E_UNSUPPORTED, "tensor too large for 32-bit row indices");
+  int nsm = 0;
+  int rc = device_sms(&nsm);
+  if (rc != SWA_OK) return rc;
+  swa::BwdParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.o = static_cast<const __nv_bfloat16*>(o);
+  p.dout = static_cast<const __nv_bfloat16*>(dout);
+  p.lse = lse;
+  p.dsum = workspace;
+  p.idx[0] = full_idx;
+  p.idx[1] = local_idx;
+  p.idx_stride[0] = full_idx ? full_stride : 0;
+  p.idx_stride[1] = local_idx ? local_stride : 0;
+  p.counts = counts;
+  p.starts[0] = full_starts;
+  p.starts[1] = local_starts;
+  p.ends = causal_ends;
+  p.dq = static_cast<__nv_bfloat16*>(dq);
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.B = B;
+  p.Sq = Sq;
+  p.Skv = Skv;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.r = Hq / Hkv;
+  p.window = window;
+  p.scale_log2 = scale_log2;
+  p.scale = scale_log2 / 1.4426950408889634f;
+  for (int br = 0; br < 2; ++br)
+    p.nblk[br] = static_cast<int>((static_cast<int64_t>(p.idx_stride[br]) * p.r + 63) / 64);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // rows that no list routes keep a zero gradient
+  cudaError_t e = cudaMemsetAsync(dq, 0, static_cast<size_t>(B) * Sq * Hq * 128 * 2, s);
+  if (e != cudaSuccess) return cuda_fail(e, "dq reset");
+  e = swa::launch_backward(p, nsm, s);
+  if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+  return SWA_OK;
+}
+
 int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
                         const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
                         const int32_t* counts, int counts_batch_major, int count_full, int count_local,

@@ -1,0 +1,419 @@
+// Switch Attention GQA prefill backward (sm_100a): dQ, dK, dV from the forward's
+// output O and log2-domain LSE, for both routing branches.  The reference is
+// forward only (swiattn_gqa_prefill_varlen.py:14); the gradients are those of
+// its forward: P = 2^(S * scale_log2 - LSE) over the row's legal keys (masks
+// swiattn_gqa_prefill.py:145-158, varlen bounds swiattn_gqa_prefill_varlen.py:186-196),
+// dP = dO V^T, dS = P (dP - D) with D = rowsum(dO * O), dQ = scale dS K,
+// dK = scale dS^T Q, dV = P^T dO.
+//
+// Rows are packed as in the forward: packed row R of (branch, batch b, KV group
+// g) is routed slot R / r of the branch's list and query head g r + R % r, so
+// the r heads that share K/V sit in one matrix dimension and dK / dV sum over
+// them inside the matrix products.
+//   bwd_dsum_kernel : D for every (position, head), one warp per row.
+//   bwd_dq_kernel   : one CTA per 64 packed rows (16 per warp); loops over the
+//                     64-key tiles of the rows' union key range: S = Q K^T and
+//                     dP = dO V^T, dS, dQ += dS K.
+//   bwd_dkv_kernel  : one CTA per 64-key tile (16 keys per warp); loops over
+//                     the packed rows whose key range meets the tile (a slot
+//                     range found by binary search in the sorted index lists),
+//                     32 rows at a time: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO,
+//                     dK += dS^T Q.
+// The products run on mma.sync m16n8k16 (BF16 in, FP32 accumulate; P and dS are
+// rounded to BF16 as operands), with every operand read from row-major
+// swizzled shared tiles by plain or transposed ldmatrix.  Tiles are staged by
+// plain 16-byte loads with block barriers.  This is the first, synchronous
+// version of the backward; porting it to tcgen05 with a TMA pipeline is the
+// next step for its speed.
+#include "mma_sync.cuh"
+#include "sm100.cuh"
+#include "swattn_internal.h"
+
+namespace swa {
+
+namespace {
+
+constexpr int kBwdThreads = 128;
+constexpr int kQRows = 64;   // dQ pass: packed rows per CTA
+constexpr int kTile = 64;    // keys per tile
+constexpr int kKvRows = 32;  // dK/dV pass: packed rows per step
+
+__device__ __forceinline__ void bwd_row_bounds(const BwdParams& p, int branch, int pos, int& lo, int& hi) {
+  if (p.ends != nullptr) {
+    lo = max(p.starts[branch][pos], 0);
+    hi = min(p.ends[pos], p.Skv);
+  } else {
+    lo = branch ? max(pos - p.window + 1, 0) : 0;
+    hi = min(pos + 1, p.Skv);
+  }
+}
+
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
+  __nv_bfloat162 h;
+  memcpy(&h, &u, 4);
+  return __bfloat1622float2(h);
+}
+
+// Stage `rows` packed rows starting at R0 of (branch, b, g) into swizzled tiles
+// of Q and dO, with each row's LSE, D and key bounds (empty bounds for absent
+// rows).  Returns nothing; every thread takes part.
+__device__ __forceinline__ void stage_rows(const BwdParams& p, int branch, int b, int g, int cnt, int R0, int rows,
+                                           uint8_t* sq, uint8_t* sdo, float* slse, float* sD, int* slo, int* shi,
+                                           int* spos) {
+  const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
+  for (int i = threadIdx.x; i < rows; i += kBwdThreads) {
+    const int R = R0 + i;
+    const int slot = R / p.r;
+    int pos = -1, lo = 0, hi = 0;
+    float lse = 0.0f, d = 0.0f;
+    if (slot < cnt) {
+      pos = idx[slot];
+      if (pos >= 0 && pos < p.Sq) {
+        const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
+        bwd_row_bounds(p, branch, pos, lo, hi);
+        lse = p.lse[row];
+        d = p.dsum[row];
+        if (!(lse > -INFINITY)) hi = lo;  // a row without legal keys has no gradient
+      } else {
+        pos = -1;
+      }
+    }
+    spos[i] = pos;
+    slo[i] = lo;
+    shi[i] = hi;
+    slse[i] = lse;
+    sD[i] = d;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * 16; i += kBwdThreads) {
+    const int rr = i >> 4, c = i & 15;
+    const int pos = spos[rr];
+    uint4 qv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0);
+    if (pos >= 0) {
+      const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r;
+      qv = *reinterpret_cast<const uint4*>(p.q + row * 128 + 8 * c);
+      dv = *reinterpret_cast<const uint4*>(p.dout + row * 128 + 8 * c);
+    }
+    *reinterpret_cast<uint4*>(sq + swz(rows, rr, c)) = qv;
+    *reinterpret_cast<uint4*>(sdo + swz(rows, rr, c)) = dv;
+  }
+}
+
+// Stage keys [k0, k0 + 64) of (b, g) of K and V (zeros past Skv).
+__device__ __forceinline__ void stage_keys(const BwdParams& p, int b, int g, int k0, uint8_t* sk, uint8_t* sv) {
+  for (int i = threadIdx.x; i < kTile * 16; i += kBwdThreads) {
+    const int kr = i >> 4, c = i & 15;
+    const int key = k0 + kr;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (key < p.Skv) {
+      const int64_t row = (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g;
+      kv = *reinterpret_cast<const uint4*>(p.k + row * 128 + 8 * c);
+      vv = *reinterpret_cast<const uint4*>(p.v + row * 128 + 8 * c);
+    }
+    *reinterpret_cast<uint4*>(sk + swz(kTile, kr, c)) = kv;
+    *reinterpret_cast<uint4*>(sv + swz(kTile, kr, c)) = vv;
+  }
+}
+
+__global__ void __launch_bounds__(256) bwd_dsum_kernel(const __grid_constant__ BwdParams p) {
+  const int64_t rows = static_cast<int64_t>(p.B) * p.Sq * p.Hq;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+    const uint2 a = *reinterpret_cast<const uint2*>(p.dout + row * 128 + 4 * lane);
+    const uint2 o = *reinterpret_cast<const uint2*>(p.o + row * 128 + 4 * lane);
+    const float2 a0 = bf2_to_f2(a.x), a1 = bf2_to_f2(a.y), o0 = bf2_to_f2(o.x), o1 = bf2_to_f2(o.y);
+    float s = a0.x * o0.x + a0.y * o0.y + a1.x * o1.x + a1.y * o1.y;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) p.dsum[row] = s;
+  }
+}
+
+struct DqSmem {
+  static constexpr uint32_t q = 0;
+  static constexpr uint32_t dout = q + kQRows * 256;
+  static constexpr uint32_t k = dout + kQRows * 256;
+  static constexpr uint32_t v = k + kTile * 256;
+  static constexpr uint32_t info = v + kTile * 256;  // lse, D (float), lo, hi, pos (int) x 64
+  static constexpr uint32_t total = info + 5 * kQRows * 4 + 16;
+};
+
+__global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+  const int g = blockIdx.y, b = blockIdx.z;
+  int blk = blockIdx.x, branch = 0;
+  if (blk >= p.nblk[0]) {
+    blk -= p.nblk[0];
+    branch = 1;
+  }
+  const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+  const int R0 = blk * kQRows;
+  if (R0 >= cnt * p.r) return;
+  extern __shared__ uint8_t bsm_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* slse = reinterpret_cast<float*>(smem + DqSmem::info);
+  float* sD = slse + kQRows;
+  int* slo = reinterpret_cast<int*>(sD + kQRows);
+  int* shi = slo + kQRows;
+  int* spos = shi + kQRows;
+  int* range = spos + kQRows;  // union key range of the CTA's rows
+  if (threadIdx.x == 0) {
+    range[0] = 0x7fffffff;
+    range[1] = 0;
+  }
+  stage_rows(p, branch, b, g, cnt, R0, kQRows, smem + DqSmem::q, smem + DqSmem::dout, slse, sD, slo, shi, spos);
+  if (threadIdx.x < kQRows && shi[threadIdx.x] > slo[threadIdx.x]) {
+    atomicMin(&range[0], slo[threadIdx.x]);
+    atomicMax(&range[1], shi[threadIdx.x]);
+  }
+  __syncthreads();
+  const int lo_u = range[0], hi_u = range[1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mat = lane >> 3, mr = lane & 7;
+  const int r0 = 16 * warp + (lane >> 2), r1 = r0 + 8;
+  const uint32_t aq = smem_u32(smem + DqSmem::q), ado = smem_u32(smem + DqSmem::dout);
+  const uint32_t ak = smem_u32(smem + DqSmem::k), av = smem_u32(smem + DqSmem::v);
+  const float sl2 = p.scale_log2;
+  float dq[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.0f;
+  for (int k0 = lo_u < hi_u ? (lo_u / kTile) * kTile : hi_u; k0 < hi_u; k0 += kTile) {
+    __syncthreads();  // the previous tile is consumed
+    stage_keys(p, b, g, k0, smem + DqSmem::k, smem + DqSmem::v);
+    __syncthreads();
+    float s[8][4], dp[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = dp[n][0] = dp[n][1] = dp[n][2] = dp[n][3] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t qa[4], da[4];
+      const int arow = 16 * warp + (mat & 1) * 8 + mr, ac = 2 * ks + (mat >> 1);
+      ldsm_x4(aq + swz(kQRows, arow, ac), qa[0], qa[1], qa[2], qa[3]);
+      ldsm_x4(ado + swz(kQRows, arow, ac), da[0], da[1], da[2], da[3]);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int key = 16 * np + (mat >> 1) * 8 + mr, bc = 2 * ks + (mat & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(ak + swz(kTile, key, bc), b0, b1, b2, b3);
+        mma_bf16(s[2 * np], qa, b0, b1);
+        mma_bf16(s[2 * np + 1], qa, b2, b3);
+        ldsm_x4(av + swz(kTile, key, bc), b0, b1, b2, b3);
+        mma_bf16(dp[2 * np], da, b0, b1);
+        mma_bf16(dp[2 * np + 1], da, b2, b3);
+      }
+    }
+    // dS = P (dP - D) on the rows' legal keys
+    const int lo0 = slo[r0], hi0 = shi[r0], lo1 = slo[r1], hi1 = shi[r1];
+    const float l0 = slse[r0], l1 = slse[r1], d0 = sD[r0], d1 = sD[r1];
+    uint32_t dsa[4][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      float ds[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + 8 * n + 2 * (lane & 3) + (e & 1);
+        const bool top = e < 2;
+        const bool legal = key >= (top ? lo0 : lo1) && key < (top ? hi0 : hi1);
+        const float pv = legal ? ex2_approx(s[n][e] * sl2 - (top ? l0 : l1)) : 0.0f;
+        ds[e] = pv * (dp[n][e] - (top ? d0 : d1));
+      }
+      dsa[n >> 1][(n & 1) * 2] = pack_bf16x2(ds[0], ds[1]);
+      dsa[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+    }
+    // dQ += dS K (K read transposed: the key dimension is the reduction)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int nd = 0; nd < 16; nd += 2) {
+        const int key = 16 * kk + (mat & 1) * 8 + mr, bc = nd + (mat >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(ak + swz(kTile, key, bc), b0, b1, b2, b3);
+        mma_bf16(dq[nd], dsa[kk], b0, b1);
+        mma_bf16(dq[nd + 1], dsa[kk], b2, b3);
+      }
+    }
+  }
+  // write dQ (scaled) of the present rows
+  const float sc = p.scale;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int rr = h ? r1 : r0;
+    const int pos = spos[rr];
+    if (pos < 0) continue;
+    const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r;
+#pragma unroll
+    for (int nd = 0; nd < 16; ++nd) {
+      const int col = 8 * nd + 2 * (lane & 3);
+      *reinterpret_cast<uint32_t*>(p.dq + row * 128 + col) =
+          pack_bf16x2(dq[nd][2 * h] * sc, dq[nd][2 * h + 1] * sc);
+    }
+  }
+}
+
+struct DkvSmem {
+  static constexpr uint32_t k = 0;
+  static constexpr uint32_t v = k + kTile * 256;
+  static constexpr uint32_t q = v + kTile * 256;
+  static constexpr uint32_t dout = q + kKvRows * 256;
+  static constexpr uint32_t info = dout + kKvRows * 256;  // lse, D, lo, hi, pos x 32
+  static constexpr uint32_t total = info + 5 * kKvRows * 4 + 16;
+};
+
+// First slot in [0, cnt) whose row satisfies pred (pred is monotone: false...true).
+template <typename Pred>
+__device__ __forceinline__ int first_slot(int cnt, Pred pred) {
+  int lo = 0, hi = cnt;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (pred(mid))
+      hi = mid;
+    else
+      lo = mid + 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_constant__ BwdParams p) {
+  const int k0 = blockIdx.x * kTile, g = blockIdx.y, b = blockIdx.z;
+  extern __shared__ uint8_t bsm_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* slse = reinterpret_cast<float*>(smem + DkvSmem::info);
+  float* sD = slse + kKvRows;
+  int* slo = reinterpret_cast<int*>(sD + kKvRows);
+  int* shi = slo + kKvRows;
+  int* spos = shi + kKvRows;
+  int* srange = spos + kKvRows;
+  stage_keys(p, b, g, k0, smem + DkvSmem::k, smem + DkvSmem::v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mat = lane >> 3, mr = lane & 7;
+  const int kr0 = 16 * warp + (lane >> 2), kr1 = kr0 + 8;  // key rows of this thread
+  const uint32_t ak = smem_u32(smem + DkvSmem::k), av = smem_u32(smem + DkvSmem::v);
+  const uint32_t aq = smem_u32(smem + DkvSmem::q), ado = smem_u32(smem + DkvSmem::dout);
+  const float sl2 = p.scale_log2;
+  float dk[16][4], dv[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) dk[n][0] = dk[n][1] = dk[n][2] = dk[n][3] = dv[n][0] = dv[n][1] = dv[n][2] = dv[n][3] = 0.0f;
+  for (int branch = 0; branch < 2; ++branch) {
+    const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // rows whose key range [lo, hi) meets [k0, k0 + 64): hi > k0 and lo < k0 + 64; both
+      // bounds are non-decreasing along the increasing routed positions
+      const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
+      auto bounds = [&](int slot, int& lo, int& hi) {
+        const int pos = min(max(idx[slot], 0), p.Sq - 1);
+        bwd_row_bounds(p, branch, pos, lo, hi);
+      };
+      srange[0] = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return hi > k0; });
+      srange[1] = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return lo >= k0 + kTile; });
+    }
+    __syncthreads();
+    const int s_lo = srange[0], s_hi = max(srange[1], srange[0]);
+    for (int R0 = s_lo * p.r; R0 < s_hi * p.r; R0 += kKvRows) {
+      __syncthreads();  // the previous rows are consumed
+      stage_rows(p, branch, b, g, s_hi, R0, kKvRows, smem + DkvSmem::q, smem + DkvSmem::dout, slse, sD, slo, shi,
+                 spos);
+      __syncthreads();
+      float st[4][4], dpt[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) st[n][0] = st[n][1] = st[n][2] = st[n][3] = dpt[n][0] = dpt[n][1] = dpt[n][2] = dpt[n][3] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t ka[4], va[4];
+        const int arow = 16 * warp + (mat & 1) * 8 + mr, ac = 2 * ks + (mat >> 1);
+        ldsm_x4(ak + swz(kTile, arow, ac), ka[0], ka[1], ka[2], ka[3]);
+        ldsm_x4(av + swz(kTile, arow, ac), va[0], va[1], va[2], va[3]);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          const int row = 16 * np + (mat >> 1) * 8 + mr, bc = 2 * ks + (mat & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(aq + swz(kKvRows, row, bc), b0, b1, b2, b3);
+          mma_bf16(st[2 * np], ka, b0, b1);
+          mma_bf16(st[2 * np + 1], ka, b2, b3);
+          ldsm_x4(ado + swz(kKvRows, row, bc), b0, b1, b2, b3);
+          mma_bf16(dpt[2 * np], va, b0, b1);
+          mma_bf16(dpt[2 * np + 1], va, b2, b3);
+        }
+      }
+      // P^T and dS^T of this warp's keys (rows) against the staged packed rows (columns)
+      uint32_t pa[2][4], da[2][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        float pv[4], ds[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = 8 * n + 2 * (lane & 3) + (e & 1);
+          const int key = k0 + (e < 2 ? kr0 : kr1);
+          const bool legal = key >= slo[col] && key < shi[col];
+          pv[e] = legal ? ex2_approx(st[n][e] * sl2 - slse[col]) : 0.0f;
+          ds[e] = pv[e] * (dpt[n][e] - sD[col]);
+        }
+        pa[n >> 1][(n & 1) * 2] = pack_bf16x2(pv[0], pv[1]);
+        pa[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+        da[n >> 1][(n & 1) * 2] = pack_bf16x2(ds[0], ds[1]);
+        da[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+      }
+      // dV += P^T dO, dK += dS^T Q (dO and Q read transposed: the rows are the reduction)
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+        for (int nd = 0; nd < 16; nd += 2) {
+          const int row = 16 * kk + (mat & 1) * 8 + mr, bc = nd + (mat >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(ado + swz(kKvRows, row, bc), b0, b1, b2, b3);
+          mma_bf16(dv[nd], pa[kk], b0, b1);
+          mma_bf16(dv[nd + 1], pa[kk], b2, b3);
+          ldsm_x4_t(aq + swz(kKvRows, row, bc), b0, b1, b2, b3);
+          mma_bf16(dk[nd], da[kk], b0, b1);
+          mma_bf16(dk[nd + 1], da[kk], b2, b3);
+        }
+      }
+    }
+  }
+  const float sc = p.scale;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int key = k0 + (h ? kr1 : kr0);
+    if (key >= p.Skv) continue;
+    const int64_t row = (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g;
+#pragma unroll
+    for (int nd = 0; nd < 16; ++nd) {
+      const int col = 8 * nd + 2 * (lane & 3);
+      *reinterpret_cast<uint32_t*>(p.dk + row * 128 + col) = pack_bf16x2(dk[nd][2 * h] * sc, dk[nd][2 * h + 1] * sc);
+      *reinterpret_cast<uint32_t*>(p.dv + row * 128 + col) = pack_bf16x2(dv[nd][2 * h], dv[nd][2 * h + 1]);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint32_t dq_smem = DqSmem::total + 1024, dkv_smem = DkvSmem::total + 1024;
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dq_smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv_smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int64_t rows = static_cast<int64_t>(params.B) * params.Sq * params.Hq;
+  const int64_t want = (rows + 7) / 8;
+  const int dsum_blocks = static_cast<int>(want < 16LL * num_sms ? want : 16LL * num_sms);
+  bwd_dsum_kernel<<<dsum_blocks, 256, 0, stream>>>(params);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const dim3 gq(params.nblk[0] + params.nblk[1], params.Hkv, params.B);
+  if (gq.x > 0) bwd_dq_kernel<<<gq, kBwdThreads, dq_smem, stream>>>(params);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const dim3 gkv((params.Skv + kTile - 1) / kTile, params.Hkv, params.B);
+  bwd_dkv_kernel<<<gkv, kBwdThreads, dkv_smem, stream>>>(params);
+  return cudaGetLastError();
+}
+
+}  // namespace swa

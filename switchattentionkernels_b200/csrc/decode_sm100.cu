@@ -26,6 +26,7 @@
 // math warps to hide the mma.sync / ldmatrix latencies; one CTA per SM with a
 // 4-entry ring streamed 15 % slower on the mixed batch and 26 % slower on
 // all-window batches.
+#include "mma_sync.cuh"
 #include "sm100.cuh"
 #include "swattn_internal.h"
 
@@ -49,32 +50,6 @@ struct DecSmem {
   static constexpr uint32_t total = ml + 4 * 16 * 2 * 4;
 };
 constexpr uint32_t kDecSmemBytes = DecSmem::total + 1024;
-
-// byte offset of 16-byte chunk `c` (0..15 over the 128 dims) of row `row` in a
-// tile stored as two 64-dim halves of `rows` x 128 B rows, 128B swizzle
-__device__ __forceinline__ uint32_t swz(int rows, int row, int c) {
-  return static_cast<uint32_t>((c >> 3) * rows * 128 + row * 128 + (((c & 7) ^ (row & 7)) << 4));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 struct DecRange {
   int s0, s1;  // keys of this split

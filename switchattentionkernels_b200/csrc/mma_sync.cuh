@@ -1,0 +1,38 @@
+// Warp-level mma.sync / ldmatrix helpers for the kernels whose tensor work is
+// small next to their memory traffic or that are not yet ported to tcgen05
+// (decode step, backward pass).  Tiles in shared memory are stored as two
+// 64-dim halves of `rows` x 128-byte rows with the 128B swizzle (the layout a
+// TMA box of 64 BF16 columns writes), so 16-byte chunk c of row `row` lives at
+// swz(rows, row, c).
+#pragma once
+
+#include <cstdint>
+
+namespace swa {
+
+__device__ __forceinline__ uint32_t swz(int rows, int row, int c) {
+  return static_cast<uint32_t>((c >> 3) * rows * 128 + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D (16x8, FP32) += A (16x16, BF16, row-major fragment) * B (16x8, BF16, column fragment)
+__device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+}  // namespace swa

@@ -73,6 +73,23 @@ struct __align__(64) DecodeParams {
   float scale_log2;
 };
 cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream);
+
+// Prefill backward: dQ, dK, dV of both branches.
+struct BwdParams {
+  const __nv_bfloat16 *q, *k, *v, *o, *dout;
+  const float* lse;          // [B, Sq, Hq] forward LSE (log2 units)
+  float* dsum;               // [B, Sq, Hq] rowsum(dO * O) (workspace)
+  const int32_t* idx[2];     // [B, stride] routed positions of each branch, -1 padded
+  int idx_stride[2];
+  const int32_t* counts;     // [B, 2] (n_full, n_local)
+  const int32_t* starts[2];  // metadata (nullable)
+  const int32_t* ends;
+  __nv_bfloat16 *dq, *dk, *dv;
+  int B, Sq, Skv, Hq, Hkv, r, window;
+  float scale_log2, scale;   // softmax scale in log2 units and in natural units
+  int nblk[2];               // 64-row blocks of each branch per (batch, KV group)
+};
+cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream);
 uint32_t decode_smem_bytes();
 
 // Record the message returned by swa_last_error_string() on this thread.
