@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--cp", action="store_true",
                     help="instead of the default line: context-parallel prefill over the N ranks "
                          "(strong scaling; K/V all-gather + kernel per step)")
+    ap.add_argument("--backward", action="store_true",
+                    help="instead of the default line: the prefill backward (dQ, dK, dV) of the config-3 workload")
     ap.add_argument("--decode", action="store_true",
                     help="instead of the default line: one decode step (one new token per sequence) over a KV cache")
     ap.add_argument("--cp-config", type=int, choices=[4, 5], default=4,
@@ -246,6 +248,73 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def run_backward(args, world, rank, local_rank):
+    """Prefill backward of the config-3 workload (``--batch`` sequences per GPU).
+
+    One step = dQ, dK, dV from the forward's O and LSE for a random upstream
+    gradient (rowsum pass, dQ pass, dK/dV pass).  ``value`` uses the usual
+    convention of 2.5 x the forward's effective FLOP (five matrix products of
+    the forward's size, over the legal entries only).
+    """
+    from switchattentionkernels_b200 import _core, build_switch_query_indices_batched
+    from switchattentionkernels_b200.backward import switch_gqa_prefill_backward
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = workloads.make_inputs(CONFIG_ID, device=dev, on_device=True, seed_offset=1000 * rank,
+                              batch_override=args.batch)
+    cfg = w["cfg"]
+    q, k, v, mask, W = w["q"], w["k"], w["v"], w["mask"], w["window"]
+    full, local, counts = build_switch_query_indices_batched(mask.to(dev))
+    out, lse = _core.forward(q, k, v, full, local, window_size=W, query_counts=counts)
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    dout = torch.randn(out.shape, generator=g, device=dev).bfloat16()
+    flops = 2.5 * workloads.effective_flops(mask.numpy(), W, q.shape[1], q.shape[2])
+
+    def step():
+        switch_gqa_prefill_backward(q, k, v, out, lse, dout, full, local, window_size=W, query_counts=counts)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.mark("begin")
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark("end")
+    clock_info = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.destroy_process_group()
+    if rank == 0:
+        peak_burst, _, peak_src = measured_peaks()
+        value = flops * world / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "prefill backward: effective TFLOP/s (2.5 x forward, unmasked entries)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "B_per_gpu": q.shape[0], "effective_tflop_per_step": flops / 1e12},
+            "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak_burst, "unit": UNIT,
+                         "frac": value / world / peak_burst, "peak_source": f"{peak_src} bf16_tflops (burst)"},
+            "gpu_launches": 3 * args.steps,  # rowsum, dQ pass, dK/dV pass per step
+            "clocks": clock_info,
+        }), flush=True)
+    return 0
+
+
 def run_decode(args, world, rank, local_rank):
     """Decode step of the config-3 model shape: 64 sequences with 16K-32K cached
     keys each, Hq 32 / Hkv 8, W 1024, each new token routed full with p = 0.125.
@@ -416,6 +485,8 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     if args.decode and args.impl == "ours":
         return run_decode(args, world, rank, local_rank)
+    if args.backward and args.impl == "ours":
+        return run_backward(args, world, rank, local_rank)
     if args.cp and args.impl == "ours":
         rc = run_cp(args, world, rank, local_rank)
         if world > 1:

@@ -22,9 +22,8 @@
 // The products run on mma.sync m16n8k16 (BF16 in, FP32 accumulate; P and dS are
 // rounded to BF16 as operands), with every operand read from row-major
 // swizzled shared tiles by plain or transposed ldmatrix.  Tiles are staged by
-// plain 16-byte loads with block barriers.  This is the first, synchronous
-// version of the backward; porting it to tcgen05 with a TMA pipeline is the
-// next step for its speed.
+// cp.async into double buffers, so the next tile's loads run under the current
+// tile's products.  Porting the products to tcgen05 is the next step for speed.
 #include "mma_sync.cuh"
 #include "sm100.cuh"
 #include "swattn_internal.h"
@@ -54,64 +53,78 @@ __device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
   return __bfloat1622float2(h);
 }
 
-// Stage `rows` packed rows starting at R0 of (branch, b, g) into swizzled tiles
-// of Q and dO, with each row's LSE, D and key bounds (empty bounds for absent
-// rows).  Returns nothing; every thread takes part.
-__device__ __forceinline__ void stage_rows(const BwdParams& p, int branch, int b, int g, int cnt, int R0, int rows,
-                                           uint8_t* sq, uint8_t* sdo, float* slse, float* sD, int* slo, int* shi,
-                                           int* spos) {
-  const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
-  for (int i = threadIdx.x; i < rows; i += kBwdThreads) {
-    const int R = R0 + i;
-    const int slot = R / p.r;
-    int pos = -1, lo = 0, hi = 0;
-    float lse = 0.0f, d = 0.0f;
-    if (slot < cnt) {
-      pos = idx[slot];
-      if (pos >= 0 && pos < p.Sq) {
-        const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
-        bwd_row_bounds(p, branch, pos, lo, hi);
-        lse = p.lse[row];
-        d = p.dsum[row];
-        if (!(lse > -INFINITY)) hi = lo;  // a row without legal keys has no gradient
-      } else {
-        pos = -1;
-      }
+// Per-row data of packed row R of (branch, b, g): position (-1 when absent),
+// legal key range (empty for absent rows and rows without legal keys), LSE, D.
+struct RowReg {
+  int pos, lo, hi;
+  float lse, d;
+};
+
+__device__ __forceinline__ RowReg load_row(const BwdParams& p, int branch, int b, int g, int cnt, int R) {
+  RowReg x{-1, 0, 0, 0.0f, 0.0f};
+  const int slot = R / p.r;
+  if (slot < cnt) {
+    const int pos = p.idx[branch][static_cast<int64_t>(b) * p.idx_stride[branch] + slot];
+    if (pos >= 0 && pos < p.Sq) {
+      const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
+      x.pos = pos;
+      bwd_row_bounds(p, branch, pos, x.lo, x.hi);
+      x.lse = p.lse[row];
+      x.d = p.dsum[row];
+      if (!(x.lse > -INFINITY)) x.hi = x.lo;  // a row without legal keys has no gradient
     }
-    spos[i] = pos;
-    slo[i] = lo;
-    shi[i] = hi;
-    slse[i] = lse;
-    sD[i] = d;
   }
-  __syncthreads();
+  return x;
+}
+
+struct RowInfo {  // shared-memory arrays of a block of packed rows
+  float* lse;
+  float* d;
+  int* lo;
+  int* hi;
+  int* pos;
+  __device__ __forceinline__ void put(int i, const RowReg& x) const {
+    pos[i] = x.pos;
+    lo[i] = x.lo;
+    hi[i] = x.hi;
+    lse[i] = x.lse;
+    d[i] = x.d;
+  }
+};
+
+__device__ __forceinline__ RowInfo row_info_at(uint8_t* base, int rows) {
+  RowInfo r;
+  r.lse = reinterpret_cast<float*>(base);
+  r.d = r.lse + rows;
+  r.lo = reinterpret_cast<int*>(r.d + rows);
+  r.hi = r.lo + rows;
+  r.pos = r.hi + rows;
+  return r;
+}
+
+// Asynchronous gather of the Q and dO rows of a block (positions already in
+// shared memory); absent rows are zero-filled.
+__device__ __forceinline__ void gather_rows_async(const BwdParams& p, int b, int g, int R0, int rows, const int* spos,
+                                                  uint8_t* sq, uint8_t* sdo) {
   for (int i = threadIdx.x; i < rows * 16; i += kBwdThreads) {
     const int rr = i >> 4, c = i & 15;
     const int pos = spos[rr];
-    uint4 qv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0);
-    if (pos >= 0) {
-      const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r;
-      qv = *reinterpret_cast<const uint4*>(p.q + row * 128 + 8 * c);
-      dv = *reinterpret_cast<const uint4*>(p.dout + row * 128 + 8 * c);
-    }
-    *reinterpret_cast<uint4*>(sq + swz(rows, rr, c)) = qv;
-    *reinterpret_cast<uint4*>(sdo + swz(rows, rr, c)) = dv;
+    const bool ok = pos >= 0;
+    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
+    cp_async_16(smem_u32(sq + swz(rows, rr, c)), p.q + row * 128 + 8 * c, ok);
+    cp_async_16(smem_u32(sdo + swz(rows, rr, c)), p.dout + row * 128 + 8 * c, ok);
   }
 }
 
-// Stage keys [k0, k0 + 64) of (b, g) of K and V (zeros past Skv).
-__device__ __forceinline__ void stage_keys(const BwdParams& p, int b, int g, int k0, uint8_t* sk, uint8_t* sv) {
+// Asynchronous load of keys [k0, k0 + 64) of (b, g) of K and V (zeros past Skv).
+__device__ __forceinline__ void gather_keys_async(const BwdParams& p, int b, int g, int k0, uint8_t* sk, uint8_t* sv) {
   for (int i = threadIdx.x; i < kTile * 16; i += kBwdThreads) {
     const int kr = i >> 4, c = i & 15;
     const int key = k0 + kr;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (key < p.Skv) {
-      const int64_t row = (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g;
-      kv = *reinterpret_cast<const uint4*>(p.k + row * 128 + 8 * c);
-      vv = *reinterpret_cast<const uint4*>(p.v + row * 128 + 8 * c);
-    }
-    *reinterpret_cast<uint4*>(sk + swz(kTile, kr, c)) = kv;
-    *reinterpret_cast<uint4*>(sv + swz(kTile, kr, c)) = vv;
+    const bool ok = key < p.Skv;
+    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g : 0;
+    cp_async_16(smem_u32(sk + swz(kTile, kr, c)), p.k + row * 128 + 8 * c, ok);
+    cp_async_16(smem_u32(sv + swz(kTile, kr, c)), p.v + row * 128 + 8 * c, ok);
   }
 }
 
@@ -133,9 +146,8 @@ __global__ void __launch_bounds__(256) bwd_dsum_kernel(const __grid_constant__ B
 struct DqSmem {
   static constexpr uint32_t q = 0;
   static constexpr uint32_t dout = q + kQRows * 256;
-  static constexpr uint32_t k = dout + kQRows * 256;
-  static constexpr uint32_t v = k + kTile * 256;
-  static constexpr uint32_t info = v + kTile * 256;  // lse, D (float), lo, hi, pos (int) x 64
+  static constexpr uint32_t kv = dout + kQRows * 256;         // 2 x (K tile, V tile)
+  static constexpr uint32_t info = kv + 2 * 2 * kTile * 256;  // lse, D, lo, hi, pos x 64, range
   static constexpr uint32_t total = info + 5 * kQRows * 4 + 16;
 };
 
@@ -152,36 +164,51 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_consta
   extern __shared__ uint8_t bsm_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  float* slse = reinterpret_cast<float*>(smem + DqSmem::info);
-  float* sD = slse + kQRows;
-  int* slo = reinterpret_cast<int*>(sD + kQRows);
-  int* shi = slo + kQRows;
-  int* spos = shi + kQRows;
-  int* range = spos + kQRows;  // union key range of the CTA's rows
+  const RowInfo ri = row_info_at(smem + DqSmem::info, kQRows);
+  int* range = ri.pos + kQRows;  // union key range of the CTA's rows
   if (threadIdx.x == 0) {
     range[0] = 0x7fffffff;
     range[1] = 0;
   }
-  stage_rows(p, branch, b, g, cnt, R0, kQRows, smem + DqSmem::q, smem + DqSmem::dout, slse, sD, slo, shi, spos);
-  if (threadIdx.x < kQRows && shi[threadIdx.x] > slo[threadIdx.x]) {
-    atomicMin(&range[0], slo[threadIdx.x]);
-    atomicMax(&range[1], shi[threadIdx.x]);
+  if (threadIdx.x < kQRows) ri.put(threadIdx.x, load_row(p, branch, b, g, cnt, R0 + threadIdx.x));
+  __syncthreads();
+  gather_rows_async(p, b, g, R0, kQRows, ri.pos, smem + DqSmem::q, smem + DqSmem::dout);
+  cp_async_commit();
+  if (threadIdx.x < kQRows && ri.hi[threadIdx.x] > ri.lo[threadIdx.x]) {
+    atomicMin(&range[0], ri.lo[threadIdx.x]);
+    atomicMax(&range[1], ri.hi[threadIdx.x]);
   }
   __syncthreads();
   const int lo_u = range[0], hi_u = range[1];
+  const int kfirst = lo_u < hi_u ? (lo_u / kTile) * kTile : hi_u;
+  const int ntiles = lo_u < hi_u ? (hi_u - kfirst + kTile - 1) / kTile : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mat = lane >> 3, mr = lane & 7;
   const int r0 = 16 * warp + (lane >> 2), r1 = r0 + 8;
   const uint32_t aq = smem_u32(smem + DqSmem::q), ado = smem_u32(smem + DqSmem::dout);
-  const uint32_t ak = smem_u32(smem + DqSmem::k), av = smem_u32(smem + DqSmem::v);
   const float sl2 = p.scale_log2;
+  const int lo0 = ri.lo[r0], hi0 = ri.hi[r0], lo1 = ri.lo[r1], hi1 = ri.hi[r1];
+  const float l0 = ri.lse[r0], l1 = ri.lse[r1], d0 = ri.d[r0], d1 = ri.d[r1];
   float dq[16][4];
 #pragma unroll
   for (int n = 0; n < 16; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.0f;
-  for (int k0 = lo_u < hi_u ? (lo_u / kTile) * kTile : hi_u; k0 < hi_u; k0 += kTile) {
-    __syncthreads();  // the previous tile is consumed
-    stage_keys(p, b, g, k0, smem + DqSmem::k, smem + DqSmem::v);
+  if (ntiles > 0) {
+    gather_keys_async(p, b, g, kfirst, smem + DqSmem::kv, smem + DqSmem::kv + kTile * 256);
+    cp_async_commit();
+  }
+  for (int t = 0; t < ntiles; ++t) {
+    const int k0 = kfirst + t * kTile;
+    uint8_t* kvb = smem + DqSmem::kv + (t & 1) * 2 * kTile * 256;
+    if (t + 1 < ntiles) {
+      uint8_t* nb = smem + DqSmem::kv + ((t + 1) & 1) * 2 * kTile * 256;
+      gather_keys_async(p, b, g, k0 + kTile, nb, nb + kTile * 256);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
+    const uint32_t ak = smem_u32(kvb), av = smem_u32(kvb + kTile * 256);
     float s[8][4], dp[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = dp[n][0] = dp[n][1] = dp[n][2] = dp[n][3] = 0.0f;
@@ -204,8 +231,6 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_consta
       }
     }
     // dS = P (dP - D) on the rows' legal keys
-    const int lo0 = slo[r0], hi0 = shi[r0], lo1 = slo[r1], hi1 = shi[r1];
-    const float l0 = slse[r0], l1 = slse[r1], d0 = sD[r0], d1 = sD[r1];
     uint32_t dsa[4][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
@@ -233,13 +258,15 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_consta
         mma_bf16(dq[nd + 1], dsa[kk], b2, b3);
       }
     }
+    __syncthreads();  // this K/V buffer is refilled two tiles later
   }
+  cp_async_wait<0>();  // (no tile: the row gather is still outstanding)
   // write dQ (scaled) of the present rows
   const float sc = p.scale;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int rr = h ? r1 : r0;
-    const int pos = spos[rr];
+    const int pos = ri.pos[rr];
     if (pos < 0) continue;
     const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r;
 #pragma unroll
@@ -254,10 +281,10 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_consta
 struct DkvSmem {
   static constexpr uint32_t k = 0;
   static constexpr uint32_t v = k + kTile * 256;
-  static constexpr uint32_t q = v + kTile * 256;
-  static constexpr uint32_t dout = q + kKvRows * 256;
-  static constexpr uint32_t info = dout + kKvRows * 256;  // lse, D, lo, hi, pos x 32
-  static constexpr uint32_t total = info + 5 * kKvRows * 4 + 16;
+  static constexpr uint32_t rows = v + kTile * 256;                // 2 x (Q rows, dO rows)
+  static constexpr uint32_t info = rows + 2 * 2 * kKvRows * 256;   // 2 x (lse, D, lo, hi, pos x 32)
+  static constexpr uint32_t info_bytes = 5 * kKvRows * 4;
+  static constexpr uint32_t total = info + 2 * info_bytes + 16;
 };
 
 // First slot in [0, cnt) whose row satisfies pred (pred is monotone: false...true).
@@ -279,18 +306,13 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_const
   extern __shared__ uint8_t bsm_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  float* slse = reinterpret_cast<float*>(smem + DkvSmem::info);
-  float* sD = slse + kKvRows;
-  int* slo = reinterpret_cast<int*>(sD + kKvRows);
-  int* shi = slo + kKvRows;
-  int* spos = shi + kKvRows;
-  int* srange = spos + kKvRows;
-  stage_keys(p, b, g, k0, smem + DkvSmem::k, smem + DkvSmem::v);
+  int* srange = reinterpret_cast<int*>(smem + DkvSmem::info + 2 * DkvSmem::info_bytes);
+  gather_keys_async(p, b, g, k0, smem + DkvSmem::k, smem + DkvSmem::v);
+  cp_async_commit();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mat = lane >> 3, mr = lane & 7;
   const int kr0 = 16 * warp + (lane >> 2), kr1 = kr0 + 8;  // key rows of this thread
   const uint32_t ak = smem_u32(smem + DkvSmem::k), av = smem_u32(smem + DkvSmem::v);
-  const uint32_t aq = smem_u32(smem + DkvSmem::q), ado = smem_u32(smem + DkvSmem::dout);
   const float sl2 = p.scale_log2;
   float dk[16][4], dv[16][4];
 #pragma unroll
@@ -311,11 +333,38 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_const
     }
     __syncthreads();
     const int s_lo = srange[0], s_hi = max(srange[1], srange[0]);
-    for (int R0 = s_lo * p.r; R0 < s_hi * p.r; R0 += kKvRows) {
-      __syncthreads();  // the previous rows are consumed
-      stage_rows(p, branch, b, g, s_hi, R0, kKvRows, smem + DkvSmem::q, smem + DkvSmem::dout, slse, sD, slo, shi,
-                 spos);
+    const int Rb = s_lo * p.r;
+    const int steps = ((s_hi - s_lo) * p.r + kKvRows - 1) / kKvRows;
+    if (steps == 0) continue;
+    // software pipeline over blocks of 32 rows: the row data of block t + 2 is
+    // loaded into registers and the Q / dO gather of block t + 1 is in flight
+    // while block t is computed
+    RowReg x{};
+    if (threadIdx.x < kKvRows) row_info_at(smem + DkvSmem::info, kKvRows).put(threadIdx.x, load_row(p, branch, b, g, s_hi, Rb + threadIdx.x));
+    __syncthreads();
+    gather_rows_async(p, b, g, Rb, kKvRows, row_info_at(smem + DkvSmem::info, kKvRows).pos, smem + DkvSmem::rows,
+                      smem + DkvSmem::rows + kKvRows * 256);
+    cp_async_commit();
+    if (steps > 1 && threadIdx.x < kKvRows) x = load_row(p, branch, b, g, s_hi, Rb + kKvRows + threadIdx.x);
+    for (int t = 0; t < steps; ++t) {
+      const int cur = t & 1, nxt = cur ^ 1;
+      const RowInfo ri = row_info_at(smem + DkvSmem::info + cur * DkvSmem::info_bytes, kKvRows);
+      uint8_t* sq = smem + DkvSmem::rows + cur * 2 * kKvRows * 256;
+      uint8_t* sdo = sq + kKvRows * 256;
+      if (t + 1 < steps) {
+        const RowInfo rn = row_info_at(smem + DkvSmem::info + nxt * DkvSmem::info_bytes, kKvRows);
+        if (threadIdx.x < kKvRows) rn.put(threadIdx.x, x);
+        __syncthreads();
+        uint8_t* nq = smem + DkvSmem::rows + nxt * 2 * kKvRows * 256;
+        gather_rows_async(p, b, g, Rb + (t + 1) * kKvRows, kKvRows, rn.pos, nq, nq + kKvRows * 256);
+        cp_async_commit();
+        if (t + 2 < steps && threadIdx.x < kKvRows) x = load_row(p, branch, b, g, s_hi, Rb + (t + 2) * kKvRows + threadIdx.x);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
       __syncthreads();
+      const uint32_t aq = smem_u32(sq), ado = smem_u32(sdo);
       float st[4][4], dpt[4][4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) st[n][0] = st[n][1] = st[n][2] = st[n][3] = dpt[n][0] = dpt[n][1] = dpt[n][2] = dpt[n][3] = 0.0f;
@@ -346,9 +395,9 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_const
         for (int e = 0; e < 4; ++e) {
           const int col = 8 * n + 2 * (lane & 3) + (e & 1);
           const int key = k0 + (e < 2 ? kr0 : kr1);
-          const bool legal = key >= slo[col] && key < shi[col];
-          pv[e] = legal ? ex2_approx(st[n][e] * sl2 - slse[col]) : 0.0f;
-          ds[e] = pv[e] * (dpt[n][e] - sD[col]);
+          const bool legal = key >= ri.lo[col] && key < ri.hi[col];
+          pv[e] = legal ? ex2_approx(st[n][e] * sl2 - ri.lse[col]) : 0.0f;
+          ds[e] = pv[e] * (dpt[n][e] - ri.d[col]);
         }
         pa[n >> 1][(n & 1) * 2] = pack_bf16x2(pv[0], pv[1]);
         pa[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
@@ -370,8 +419,10 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_const
           mma_bf16(dk[nd + 1], da[kk], b2, b3);
         }
       }
+      __syncthreads();  // these row buffers are refilled two blocks later
     }
   }
+  cp_async_wait<0>();  // (no rows at all: the K/V load is still outstanding)
   const float sc = p.scale;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
