@@ -110,7 +110,8 @@ int swa_compact_router_ws(const void* router, int dtype, int pair, float thresho
  * units) and dout (bf16, like o).  Index lists: -1 padded [B, stride] rows with
  * counts[2*b] = n_full, counts[2*b+1] = n_local (as swa_compact_mask writes
  * them); metadata as in swa_prefill_forward (nullable).  workspace: at least
- * B * Sq * Hq floats (rowsum(dout * o)). */
+ * B * Sq * Hq floats (rowsum(dout * o)) followed by a 16-byte status word whose
+ * first int32 receives SWA_STATUS_TIMEOUT if a bounded device wait gave up. */
 int swa_prefill_backward(const void* q, const void* k, const void* v, const void* o, const float* lse,
                          const void* dout, const int32_t* full_idx, const int32_t* local_idx, int full_stride,
                          int local_stride, const int32_t* counts, const int32_t* full_starts,

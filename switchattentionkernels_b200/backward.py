@@ -9,10 +9,12 @@ rows, and the dK / dV pass over 64-key tiles.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _core, _native
-from ._core import LOG2E
+from ._core import LOG2E, _raise_status
 
 
 def _lists(full, local, query_counts, B, dev):
@@ -64,7 +66,7 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    ws = torch.empty(B * Sq * Hq, dtype=torch.float32, device=dev)
+    ws = torch.empty(B * Sq * Hq + 4, dtype=torch.float32, device=dev)
     fs = ls = ce = None
     if metadata is not None:
         fs, ls, ce = metadata.full_starts, metadata.local_starts, metadata.causal_ends
@@ -77,6 +79,8 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
             _native.ptr(dq), _native.ptr(dk), _native.ptr(dv), B, Sq, Skv, Hq, Hkv, D, int(window_size),
             float(scale), _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
     _native.check(rc, "switch_gqa_prefill_backward")
+    if os.environ.get("SWA_CHECK_STATUS") == "1":
+        _raise_status(int(ws[B * Sq * Hq:].view(torch.int32)[0].item()))
     return dq, dk, dv
 
 

@@ -276,8 +276,8 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   const bool has_meta = causal_ends != nullptr;
   if (has_meta && (full_starts == nullptr || local_starts == nullptr))
     return fail(SWA_E_INVALID, "metadata needs full_starts, local_starts and causal_ends");
-  if (workspace_bytes < static_cast<size_t>(B) * Sq * Hq * sizeof(float))
-    return fail(SWA_E_INVALID, "workspace must hold B * Sq * Hq floats");
+  if (workspace_bytes < static_cast<size_t>(B) * Sq * Hq * sizeof(float) + 16)
+    return fail(SWA_E_INVALID, "workspace must hold B * Sq * Hq floats and a 16-byte status word");
   if (static_cast<int64_t>(B) * Sq * Hq >= (int64_t(1) << 31) || static_cast<int64_t>(B) * Skv * Hkv >= (int64_t(1) << 31))
     return fail(SWA_E_UNSUPPORTED, "tensor too large for 32-bit row indices");
   int nsm = 0;
@@ -291,6 +291,7 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   p.dout = static_cast<const __nv_bfloat16*>(dout);
   p.lse = lse;
   p.dsum = workspace;
+  p.status = reinterpret_cast<int32_t*>(workspace + static_cast<size_t>(B) * Sq * Hq);
   p.idx[0] = full_idx;
   p.idx[1] = local_idx;
   p.idx_stride[0] = full_idx ? full_stride : 0;
@@ -317,6 +318,8 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   // rows that no list routes keep a zero gradient
   cudaError_t e = cudaMemsetAsync(dq, 0, static_cast<size_t>(B) * Sq * Hq * 128 * 2, s);
   if (e != cudaSuccess) return cuda_fail(e, "dq reset");
+  e = cudaMemsetAsync(p.status, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
   e = swa::launch_backward(p, nsm, s);
   if (e != cudaSuccess) return cuda_fail(e, "backward launch");
   return SWA_OK;

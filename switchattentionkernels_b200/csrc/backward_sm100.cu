@@ -438,17 +438,294 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_const
   }
 }
 
+// ---------------------------------------------------------------------------
+// dK / dV pass on the 5th-generation tensor cores.  One CTA per 128-key tile of
+// (b, g), 320 threads:
+//   warp 0     K and V tiles of the CTA (cp.async into 128B-swizzled tiles, the
+//              layout the MMA descriptors read).
+//   warp 1     MMA      : per row block S^T = K Q^T and dP^T = V dO^T (SS, both
+//                         K-major), then, once P^T / dS^T are in TMEM,
+//                         dV += P^T dO and dK += dS^T Q (TS, dO / Q MN-major).
+//   warps 2-9  elementwise: two threads per key (TMEM lane = key), 64 rows each:
+//                         P^T = 2^(S^T scale_log2 - LSE_row) on the legal
+//                         entries, dS^T = P^T (dP^T - D_row), written as BF16
+//                         pairs over the S^T / dP^T columns of the thread's own
+//                         64 rows; they also gather the blocks of 128 packed rows
+//                         of Q and dO with each row's LSE, D and key bounds into a
+//                         2-entry ring (block it + 2 once the products of block
+//                         it have freed its entry: a single producer warp that
+//                         shares schedulers with these warps could not keep up);
+//                         finally the dK / dV epilogue.
+// TMEM: S^T | dP^T | dV | dK, 128 columns each.
+constexpr int kTcKeys = 128;
+constexpr int kTcRows = 128;
+constexpr int kTcThreads = 320;
+constexpr uint32_t kTcTile = 128 * 256;  // 128 rows x 128 dims BF16 (two 16 KB halves)
+
+struct TcSmem {
+  static constexpr uint32_t k = 0;
+  static constexpr uint32_t v = k + kTcTile;
+  static constexpr uint32_t stage = v + kTcTile;             // 2 x (Q, dO)
+  static constexpr uint32_t info = stage + 2 * 2 * kTcTile;   // 2 x (lse, D, lo, hi, pos) x 128
+  static constexpr uint32_t info_bytes = 5 * kTcRows * 4;
+  static constexpr uint32_t bars = info + 2 * info_bytes;     // kv_full, full[2], empty[2], s_full, p_full, done
+  static constexpr uint32_t misc = bars + 8 * 8;              // tmem holder, abort flag, slot ranges
+  static constexpr uint32_t total = misc + 64;
+};
+constexpr uint32_t kTcSmemBytes = TcSmem::total + 1024;
+
+// A bounded wait whose outcome is the same in every lane of the warp (the
+// warp-collective tcgen05 instructions after it need the whole warp).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_constant__ BwdParams p) {
+  const int k0 = blockIdx.x * kTcKeys, g = blockIdx.y, b = blockIdx.z;
+  extern __shared__ uint8_t bsm_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
+  uint64_t* kv_full = bars;
+  uint64_t* full = bars + 1;
+  uint64_t* empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* done = bars + 7;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + TcSmem::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::misc + 4);
+  int* ranges = reinterpret_cast<int*>(smem + TcSmem::misc + 8);  // s_lo[2], s_hi[2], tiles[2]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 256);  // every elementwise thread, once its copies landed
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 256);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    // rows of each branch whose key range [lo, hi) meets [k0, k0 + 128): a slot range,
+    // both bounds being non-decreasing along the increasing routed positions
+    for (int branch = 0; branch < 2; ++branch) {
+      const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+      const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
+      auto bounds = [&](int slot, int& lo, int& hi) {
+        const int pos = min(max(idx[slot], 0), p.Sq - 1);
+        bwd_row_bounds(p, branch, pos, lo, hi);
+      };
+      const int s_lo = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return hi > k0; });
+      const int s_hi = max(s_lo, first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return lo >= k0 + kTcKeys; }));
+      ranges[branch] = s_lo;
+      ranges[2 + branch] = s_hi;
+      ranges[4 + branch] = ((s_hi - s_lo) * p.r + kTcRows - 1) / kTcRows;
+    }
+  }
+  if (warp == 0) {
+    __syncwarp();  // tcgen05.alloc is warp-collective: lane 0 comes from the set-up above
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int ntiles = ranges[4] + ranges[5];
+  const uint32_t tm_st = tmem, tm_dpt = tmem + 128, tm_dv = tmem + 256, tm_dk = tmem + 384;
+
+  // Gather of row block `it` (rows of branch 0, then of branch 1) into ring entry
+  // it & 1 by the 256 elementwise threads: thread pair 2 j, 2 j + 1 loads row j's
+  // position, bounds, LSE and D and issues the row's 2 x 16 chunk copies (8
+  // chunks each); every thread arrives on full[it & 1] once its copies landed.
+  // No barrier among the threads, so a thread that left on a timed-out wait
+  // cannot hold the others.
+  auto gather_block = [&](int it, int et) {
+    const int branch = it < ranges[4] ? 0 : 1;
+    const int t = branch ? it - ranges[4] : it;
+    const int R0 = ranges[branch] * p.r + t * kTcRows;
+    const int s = it & 1;
+    const int rr = et >> 1, c0 = (et & 1) * 8;
+    const RowReg x = load_row(p, branch, b, g, ranges[2 + branch], R0 + rr);
+    if (c0 == 0) row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows).put(rr, x);
+    const bool ok = x.pos >= 0;
+    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + x.pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
+    uint8_t* sq = smem + TcSmem::stage + s * 2 * kTcTile;
+    uint8_t* sdo = sq + kTcTile;
+#pragma unroll
+    for (int c = c0; c < c0 + 8; ++c) {
+      cp_async_16(smem_u32(sq + swz(kTcRows, rr, c)), p.q + row * 128 + 8 * c, ok);
+      cp_async_16(smem_u32(sdo + swz(kTcRows, rr, c)), p.dout + row * 128 + 8 * c, ok);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    fence_proxy_async_smem();
+    mbar_arrive(&full[s]);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ K / V tiles
+    for (int i = lane; i < kTcKeys * 16; i += 32) {
+      const int kr = i >> 4, c = i & 15;
+      const int key = k0 + kr;
+      const bool ok = key < p.Skv;
+      const int64_t row = ok ? (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g : 0;
+      cp_async_16(smem_u32(smem + TcSmem::k + swz(kTcKeys, kr, c)), p.k + row * 128 + 8 * c, ok);
+      cp_async_16(smem_u32(smem + TcSmem::v + swz(kTcKeys, kr, c)), p.v + row * 128 + 8 * c, ok);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(kv_full);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
+    const uint64_t k_desc = make_smem_desc_sw128(smem_u32(smem + TcSmem::k), 16, 1024);
+    const uint64_t v_desc = make_smem_desc_sw128(smem_u32(smem + TcSmem::v), 16, 1024);
+    bool ok = ntiles == 0 || warp_wait(kv_full, 0, abort_flag);
+    for (int it = 0; it < ntiles && ok; ++it) {
+      const int s = it & 1;
+      if (!warp_wait(&full[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcTile), doa = qa + kTcTile;
+      umma_ss_k128_warp(tm_st, k_desc, make_smem_desc_sw128(qa, 16, 1024), idesc_s);
+      umma_ss_k128_warp(tm_dpt, v_desc, make_smem_desc_sw128(doa, 16, 1024), idesc_s);
+      tc_commit_warp(s_full);
+      if (!warp_wait(p_full, it & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t do_mn = make_smem_desc_sw128(doa, kTcTile / 2, 1024);
+      const uint64_t q_mn = make_smem_desc_sw128(qa, kTcTile / 2, 1024);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // rows 32 c .. 32 c + 31 (BF16 pairs in columns 64 (c / 2) + 16 (c % 2))
+        const uint32_t acol = 64 * (c >> 1) + 16 * (c & 1);
+        const uint32_t acc = (it > 0 || c > 0) ? 1u : 0u;
+        umma_ts_k32_warp(tm_dv, tm_st + acol, do_mn + 2 * c * 128, idesc_o, acc);
+        umma_ts_k32_warp(tm_dk, tm_dpt + acol, q_mn + 2 * c * 128, idesc_o, acc);
+      }
+      tc_commit_warp(&empty[s]);
+    }
+    // all MMAs complete before the epilogue reads (and before the CTA frees TMEM)
+    tc_commit_warp(done);
+  } else {
+    // ------------------------------------------------------------ elementwise + epilogue
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int key_row = 32 * quarter + lane;
+    const int key = k0 + key_row;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
+    const float sl2 = p.scale_log2;
+    const int et = threadIdx.x - 64;  // 0..255 among the elementwise threads
+    bool ok = true;
+    for (int it = 0; it < ntiles && it < 2; ++it) gather_block(it, et);
+    for (int it = 0; it < ntiles; ++it) {
+      const int s = it & 1;
+      if (!warp_wait(s_full, it & 1, abort_flag)) { ok = false; break; }
+      // (already complete: acquires the row data the other threads wrote)
+      if (!warp_wait(&full[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const RowInfo ri = row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t sr[32], dr[32];
+        const uint32_t col = 64 * half + 32 * cc;
+        tmem_ld_x32(tm_st + lane_off + col, sr);
+        tmem_ld_x32(tm_dpt + lane_off + col, dr);
+        tmem_ld_wait();
+        reg_fence32(sr);
+        reg_fence32(dr);
+        uint32_t pk[16], dk2[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int rr = col + 2 * j + e;  // row of the block
+            const bool legal = key >= ri.lo[rr] && key < ri.hi[rr];
+            pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ri.lse[rr]) : 0.0f;
+            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ri.d[rr]);
+          }
+          pk[j] = pack_bf16x2(pv[0], pv[1]);
+          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
+        }
+        // over this thread's own, already read columns: 64 half + 16 cc .. + 15
+        tmem_st_x16(tm_st + lane_off + 64 * half + 16 * cc, pk);
+        tmem_st_x16(tm_dpt + lane_off + 64 * half + 16 * cc, dk2);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (it + 2 < ntiles) {
+        // ring entry s is free once the dV / dK products of block it have read it
+        // (they follow p_full, so every thread is done with its row data too)
+        if (!warp_wait(&empty[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
+        gather_block(it + 2, et);
+      }
+    }
+    // epilogue: dK (scaled) and dV of this thread's key, dims 64 half .. 64 half + 63.
+    // tcgen05.ld is warp-collective: every lane loads (the condition is made warp
+    // uniform), only the stores of keys past Skv are skipped.
+    if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
+    tc_fence_after();
+    const bool store = key < p.Skv;
+    const int64_t row = (static_cast<int64_t>(b) * p.Skv + (store ? key : 0)) * p.Hkv + g;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      __nv_bfloat16* dst = (t == 0 ? p.dk : p.dv) + row * 128 + 64 * half;
+      const float sc = t == 0 ? p.scale : 1.0f;
+      const uint32_t src = (t == 0 ? tm_dk : tm_dv) + lane_off + 64 * half;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        if (ntiles > 0 && ok) {
+          tmem_ld_x32(src + 32 * cc, r);
+          tmem_ld_wait();
+          reg_fence32(r);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        if (store) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
+            *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
+          }
+        }
+      }
+    }
+  }
+  // teardown: the MMA warp's `done` commit covers every MMA it issued
+  if (warp == 1) {
+    volatile int dummy = 0;
+    mbar_wait(done, 0, &dummy);
+  }
+  if (warp == 0) asm volatile("cp.async.wait_all;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(p.status, kStatusTimeout);
+}
+
 }  // namespace
 
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint32_t dq_smem = DqSmem::total + 1024, dkv_smem = DkvSmem::total + 1024;
+  const uint32_t dq_smem = DqSmem::total + 1024;
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dq_smem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv_smem);
+    e = cudaFuncSetAttribute(bwd_dkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -462,8 +739,8 @@ cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t s
   if (gq.x > 0) bwd_dq_kernel<<<gq, kBwdThreads, dq_smem, stream>>>(params);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const dim3 gkv((params.Skv + kTile - 1) / kTile, params.Hkv, params.B);
-  bwd_dkv_kernel<<<gkv, kBwdThreads, dkv_smem, stream>>>(params);
+  const dim3 gkv((params.Skv + kTcKeys - 1) / kTcKeys, params.Hkv, params.B);
+  bwd_dkv_tc_kernel<<<gkv, kTcThreads, kTcSmemBytes, stream>>>(params);
   return cudaGetLastError();
 }
 

@@ -88,6 +88,7 @@ struct BwdParams {
   int B, Sq, Skv, Hq, Hkv, r, window;
   float scale_log2, scale;   // softmax scale in log2 units and in natural units
   int nblk[2];               // 64-row blocks of each branch per (batch, KV group)
+  int32_t* status;           // kStatusTimeout when a bounded wait gave up
 };
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream);
 uint32_t decode_smem_bytes();
