@@ -536,19 +536,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   const int ntiles = ranges[4] + ranges[5];
   const uint32_t tm_st = tmem, tm_dpt = tmem + 128, tm_dv = tmem + 256, tm_dk = tmem + 384;
 
-  // Gather of row block `it` (rows of branch 0, then of branch 1) into ring entry
-  // it & 1 by the 256 elementwise threads: thread pair 2 j, 2 j + 1 loads row j's
-  // position, bounds, LSE and D and issues the row's 2 x 16 chunk copies (8
-  // chunks each); every thread arrives on full[it & 1] once its copies landed.
-  // No barrier among the threads, so a thread that left on a timed-out wait
-  // cannot hold the others.
-  auto gather_block = [&](int it, int et) {
+  // Row blocks (rows of branch 0, then of branch 1) go through a 2-entry ring,
+  // filled by the 256 elementwise threads: thread pair 2 j, 2 j + 1 takes row j
+  // of a block (its position, bounds, LSE and D, and 8 of its 16 chunks of Q and
+  // dO each); every thread arrives on full[entry] once its copies landed.  No
+  // barrier among the threads, so a thread that left on a timed-out wait cannot
+  // hold the others.
+  const int et = threadIdx.x - 64;  // 0..255 among the elementwise threads
+  auto block_row = [&](int it) -> RowReg {
+    const int branch = it < ranges[4] ? 0 : 1;
+    const int t = branch ? it - ranges[4] : it;
+    const int R0 = ranges[branch] * p.r + t * kTcRows;
+    return load_row(p, branch, b, g, ranges[2 + branch], R0 + (et >> 1));
+  };
+  auto issue_block = [&](int it, const RowReg& x) {
     const int branch = it < ranges[4] ? 0 : 1;
     const int t = branch ? it - ranges[4] : it;
     const int R0 = ranges[branch] * p.r + t * kTcRows;
     const int s = it & 1;
     const int rr = et >> 1, c0 = (et & 1) * 8;
-    const RowReg x = load_row(p, branch, b, g, ranges[2 + branch], R0 + rr);
     if (c0 == 0) row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows).put(rr, x);
     const bool ok = x.pos >= 0;
     const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + x.pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
@@ -559,9 +565,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       cp_async_16(smem_u32(sq + swz(kTcRows, rr, c)), p.q + row * 128 + 8 * c, ok);
       cp_async_16(smem_u32(sdo + swz(kTcRows, rr, c)), p.dout + row * 128 + 8 * c, ok);
     }
+  };
+  auto land_block = [&](int it) {
     asm volatile("cp.async.wait_all;" ::: "memory");
     fence_proxy_async_smem();
-    mbar_arrive(&full[s]);
+    mbar_arrive(&full[it & 1]);
   };
 
   if (warp == 0) {
@@ -616,14 +624,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     const int key = k0 + key_row;
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     const float sl2 = p.scale_log2;
-    const int et = threadIdx.x - 64;  // 0..255 among the elementwise threads
     bool ok = true;
-    for (int it = 0; it < ntiles && it < 2; ++it) gather_block(it, et);
+    for (int it = 0; it < ntiles && it < 2; ++it) {
+      issue_block(it, block_row(it));
+      land_block(it);
+    }
+    RowReg xn{};
     for (int it = 0; it < ntiles; ++it) {
       const int s = it & 1;
       if (!warp_wait(s_full, it & 1, abort_flag)) { ok = false; break; }
       // (already complete: acquires the row data the other threads wrote)
       if (!warp_wait(&full[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
+      if (it + 2 < ntiles) xn = block_row(it + 2);  // loads in flight during this block
       tc_fence_after();
       const RowInfo ri = row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows);
 #pragma unroll
@@ -656,13 +668,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
+      // block it + 1's copies were issued one block ago: retire them now, while the
+      // dV / dK products of this block run (the S MMAs of block it + 1 follow them)
+      if (it + 1 >= 2 && it + 1 < ntiles) land_block(it + 1);
       if (it + 2 < ntiles) {
         // ring entry s is free once the dV / dK products of block it have read it
         // (they follow p_full, so every thread is done with its row data too)
         if (!warp_wait(&empty[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
-        gather_block(it + 2, et);
+        issue_block(it + 2, xn);
       }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort: copies still in flight)
     // epilogue: dK (scaled) and dV of this thread's key, dims 64 half .. 64 half + 63.
     // tcgen05.ld is warp-collective: every lane loads (the condition is made warp
     // uniform), only the stores of keys past Skv are skipped.
