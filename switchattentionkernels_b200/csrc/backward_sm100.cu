@@ -14,16 +14,14 @@
 //   bwd_dq_kernel   : one CTA per 64 packed rows (16 per warp); loops over the
 //                     64-key tiles of the rows' union key range: S = Q K^T and
 //                     dP = dO V^T, dS, dQ += dS K.
-//   bwd_dkv_kernel  : one CTA per 64-key tile (16 keys per warp); loops over
-//                     the packed rows whose key range meets the tile (a slot
-//                     range found by binary search in the sorted index lists),
-//                     32 rows at a time: S^T = K Q^T, dP^T = V dO^T, dV += P^T dO,
-//                     dK += dS^T Q.
-// The products run on mma.sync m16n8k16 (BF16 in, FP32 accumulate; P and dS are
-// rounded to BF16 as operands), with every operand read from row-major
-// swizzled shared tiles by plain or transposed ldmatrix.  Tiles are staged by
-// cp.async into double buffers, so the next tile's loads run under the current
-// tile's products.  Porting the products to tcgen05 is the next step for speed.
+//   bwd_dkv_tc_kernel: one CTA per 128-key tile; loops over the packed rows
+//                     whose key range meets the tile (a slot range per branch,
+//                     found by binary search in the sorted index lists), 128 at
+//                     a time, on tcgen05 (see its comment below).
+// The dQ pass runs on mma.sync m16n8k16 (BF16 in, FP32 accumulate; P and dS
+// rounded to BF16 as operands), every operand read from row-major swizzled
+// shared tiles by plain or transposed ldmatrix, K/V tiles double-buffered by
+// cp.async; porting it to tcgen05 like the dK/dV pass is the next step.
 #include "mma_sync.cuh"
 #include "sm100.cuh"
 #include "swattn_internal.h"
@@ -35,7 +33,6 @@ namespace {
 constexpr int kBwdThreads = 128;
 constexpr int kQRows = 64;   // dQ pass: packed rows per CTA
 constexpr int kTile = 64;    // keys per tile
-constexpr int kKvRows = 32;  // dK/dV pass: packed rows per step
 
 __device__ __forceinline__ void bwd_row_bounds(const BwdParams& p, int branch, int pos, int& lo, int& hi) {
   if (p.ends != nullptr) {
@@ -278,15 +275,6 @@ __global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_consta
   }
 }
 
-struct DkvSmem {
-  static constexpr uint32_t k = 0;
-  static constexpr uint32_t v = k + kTile * 256;
-  static constexpr uint32_t rows = v + kTile * 256;                // 2 x (Q rows, dO rows)
-  static constexpr uint32_t info = rows + 2 * 2 * kKvRows * 256;   // 2 x (lse, D, lo, hi, pos x 32)
-  static constexpr uint32_t info_bytes = 5 * kKvRows * 4;
-  static constexpr uint32_t total = info + 2 * info_bytes + 16;
-};
-
 // First slot in [0, cnt) whose row satisfies pred (pred is monotone: false...true).
 template <typename Pred>
 __device__ __forceinline__ int first_slot(int cnt, Pred pred) {
@@ -299,143 +287,6 @@ __device__ __forceinline__ int first_slot(int cnt, Pred pred) {
       lo = mid + 1;
   }
   return lo;
-}
-
-__global__ void __launch_bounds__(kBwdThreads) bwd_dkv_kernel(const __grid_constant__ BwdParams p) {
-  const int k0 = blockIdx.x * kTile, g = blockIdx.y, b = blockIdx.z;
-  extern __shared__ uint8_t bsm_raw[];
-  uint8_t* smem =
-      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  int* srange = reinterpret_cast<int*>(smem + DkvSmem::info + 2 * DkvSmem::info_bytes);
-  gather_keys_async(p, b, g, k0, smem + DkvSmem::k, smem + DkvSmem::v);
-  cp_async_commit();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mat = lane >> 3, mr = lane & 7;
-  const int kr0 = 16 * warp + (lane >> 2), kr1 = kr0 + 8;  // key rows of this thread
-  const uint32_t ak = smem_u32(smem + DkvSmem::k), av = smem_u32(smem + DkvSmem::v);
-  const float sl2 = p.scale_log2;
-  float dk[16][4], dv[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) dk[n][0] = dk[n][1] = dk[n][2] = dk[n][3] = dv[n][0] = dv[n][1] = dv[n][2] = dv[n][3] = 0.0f;
-  for (int branch = 0; branch < 2; ++branch) {
-    const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      // rows whose key range [lo, hi) meets [k0, k0 + 64): hi > k0 and lo < k0 + 64; both
-      // bounds are non-decreasing along the increasing routed positions
-      const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
-      auto bounds = [&](int slot, int& lo, int& hi) {
-        const int pos = min(max(idx[slot], 0), p.Sq - 1);
-        bwd_row_bounds(p, branch, pos, lo, hi);
-      };
-      srange[0] = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return hi > k0; });
-      srange[1] = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return lo >= k0 + kTile; });
-    }
-    __syncthreads();
-    const int s_lo = srange[0], s_hi = max(srange[1], srange[0]);
-    const int Rb = s_lo * p.r;
-    const int steps = ((s_hi - s_lo) * p.r + kKvRows - 1) / kKvRows;
-    if (steps == 0) continue;
-    // software pipeline over blocks of 32 rows: the row data of block t + 2 is
-    // loaded into registers and the Q / dO gather of block t + 1 is in flight
-    // while block t is computed
-    RowReg x{};
-    if (threadIdx.x < kKvRows) row_info_at(smem + DkvSmem::info, kKvRows).put(threadIdx.x, load_row(p, branch, b, g, s_hi, Rb + threadIdx.x));
-    __syncthreads();
-    gather_rows_async(p, b, g, Rb, kKvRows, row_info_at(smem + DkvSmem::info, kKvRows).pos, smem + DkvSmem::rows,
-                      smem + DkvSmem::rows + kKvRows * 256);
-    cp_async_commit();
-    if (steps > 1 && threadIdx.x < kKvRows) x = load_row(p, branch, b, g, s_hi, Rb + kKvRows + threadIdx.x);
-    for (int t = 0; t < steps; ++t) {
-      const int cur = t & 1, nxt = cur ^ 1;
-      const RowInfo ri = row_info_at(smem + DkvSmem::info + cur * DkvSmem::info_bytes, kKvRows);
-      uint8_t* sq = smem + DkvSmem::rows + cur * 2 * kKvRows * 256;
-      uint8_t* sdo = sq + kKvRows * 256;
-      if (t + 1 < steps) {
-        const RowInfo rn = row_info_at(smem + DkvSmem::info + nxt * DkvSmem::info_bytes, kKvRows);
-        if (threadIdx.x < kKvRows) rn.put(threadIdx.x, x);
-        __syncthreads();
-        uint8_t* nq = smem + DkvSmem::rows + nxt * 2 * kKvRows * 256;
-        gather_rows_async(p, b, g, Rb + (t + 1) * kKvRows, kKvRows, rn.pos, nq, nq + kKvRows * 256);
-        cp_async_commit();
-        if (t + 2 < steps && threadIdx.x < kKvRows) x = load_row(p, branch, b, g, s_hi, Rb + (t + 2) * kKvRows + threadIdx.x);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
-      __syncthreads();
-      const uint32_t aq = smem_u32(sq), ado = smem_u32(sdo);
-      float st[4][4], dpt[4][4];
-#pragma unroll
-      for (int n = 0; n < 4; ++n) st[n][0] = st[n][1] = st[n][2] = st[n][3] = dpt[n][0] = dpt[n][1] = dpt[n][2] = dpt[n][3] = 0.0f;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t ka[4], va[4];
-        const int arow = 16 * warp + (mat & 1) * 8 + mr, ac = 2 * ks + (mat >> 1);
-        ldsm_x4(ak + swz(kTile, arow, ac), ka[0], ka[1], ka[2], ka[3]);
-        ldsm_x4(av + swz(kTile, arow, ac), va[0], va[1], va[2], va[3]);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          const int row = 16 * np + (mat >> 1) * 8 + mr, bc = 2 * ks + (mat & 1);
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(aq + swz(kKvRows, row, bc), b0, b1, b2, b3);
-          mma_bf16(st[2 * np], ka, b0, b1);
-          mma_bf16(st[2 * np + 1], ka, b2, b3);
-          ldsm_x4(ado + swz(kKvRows, row, bc), b0, b1, b2, b3);
-          mma_bf16(dpt[2 * np], va, b0, b1);
-          mma_bf16(dpt[2 * np + 1], va, b2, b3);
-        }
-      }
-      // P^T and dS^T of this warp's keys (rows) against the staged packed rows (columns)
-      uint32_t pa[2][4], da[2][4];
-#pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        float pv[4], ds[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = 8 * n + 2 * (lane & 3) + (e & 1);
-          const int key = k0 + (e < 2 ? kr0 : kr1);
-          const bool legal = key >= ri.lo[col] && key < ri.hi[col];
-          pv[e] = legal ? ex2_approx(st[n][e] * sl2 - ri.lse[col]) : 0.0f;
-          ds[e] = pv[e] * (dpt[n][e] - ri.d[col]);
-        }
-        pa[n >> 1][(n & 1) * 2] = pack_bf16x2(pv[0], pv[1]);
-        pa[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
-        da[n >> 1][(n & 1) * 2] = pack_bf16x2(ds[0], ds[1]);
-        da[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
-      }
-      // dV += P^T dO, dK += dS^T Q (dO and Q read transposed: the rows are the reduction)
-#pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-#pragma unroll
-        for (int nd = 0; nd < 16; nd += 2) {
-          const int row = 16 * kk + (mat & 1) * 8 + mr, bc = nd + (mat >> 1);
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(ado + swz(kKvRows, row, bc), b0, b1, b2, b3);
-          mma_bf16(dv[nd], pa[kk], b0, b1);
-          mma_bf16(dv[nd + 1], pa[kk], b2, b3);
-          ldsm_x4_t(aq + swz(kKvRows, row, bc), b0, b1, b2, b3);
-          mma_bf16(dk[nd], da[kk], b0, b1);
-          mma_bf16(dk[nd + 1], da[kk], b2, b3);
-        }
-      }
-      __syncthreads();  // these row buffers are refilled two blocks later
-    }
-  }
-  cp_async_wait<0>();  // (no rows at all: the K/V load is still outstanding)
-  const float sc = p.scale;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int key = k0 + (h ? kr1 : kr0);
-    if (key >= p.Skv) continue;
-    const int64_t row = (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g;
-#pragma unroll
-    for (int nd = 0; nd < 16; ++nd) {
-      const int col = 8 * nd + 2 * (lane & 3);
-      *reinterpret_cast<uint32_t*>(p.dk + row * 128 + col) = pack_bf16x2(dk[nd][2 * h] * sc, dk[nd][2 * h + 1] * sc);
-      *reinterpret_cast<uint32_t*>(p.dv + row * 128 + col) = pack_bf16x2(dv[nd][2 * h], dv[nd][2 * h + 1]);
-    }
-  }
 }
 
 // ---------------------------------------------------------------------------
