@@ -291,36 +291,37 @@ __device__ __forceinline__ int first_slot(int cnt, Pred pred) {
 
 // ---------------------------------------------------------------------------
 // dK / dV pass on the 5th-generation tensor cores.  One CTA per 128-key tile of
-// (b, g), 320 threads:
+// (b, g), 320 threads, over blocks of 64 packed rows:
 //   warp 0     K and V tiles of the CTA (cp.async into 128B-swizzled tiles, the
 //              layout the MMA descriptors read).
-//   warp 1     MMA      : per row block S^T = K Q^T and dP^T = V dO^T (SS, both
-//                         K-major), then, once P^T / dS^T are in TMEM,
-//                         dV += P^T dO and dK += dS^T Q (TS, dO / Q MN-major).
-//   warps 2-9  elementwise: two threads per key (TMEM lane = key), 64 rows each:
-//                         P^T = 2^(S^T scale_log2 - LSE_row) on the legal
-//                         entries, dS^T = P^T (dP^T - D_row), written as BF16
-//                         pairs over the S^T / dP^T columns of the thread's own
-//                         64 rows; they also gather the blocks of 128 packed rows
-//                         of Q and dO with each row's LSE, D and key bounds into a
-//                         2-entry ring (block it + 2 once the products of block
-//                         it have freed its entry: a single producer warp that
-//                         shares schedulers with these warps could not keep up);
-//                         finally the dK / dV epilogue.
-// TMEM: S^T | dP^T | dV | dK, 128 columns each.
+//   warp 1     MMA: per block t, S^T = K Q^T and dP^T = V dO^T (SS, N = 64, both
+//              K-major) into TMEM buffer t & 1; then, once P^T / dS^T of block
+//              t - 1 are in TMEM, dV += P^T dO and dK += dS^T Q (TS, dO / Q
+//              MN-major).  The products of block t + 1 thus run while the
+//              elementwise warps work on block t.
+//   warps 2-9  elementwise: two threads per key (TMEM lane = key), 32 rows each:
+//              P^T = 2^(S^T scale_log2 - LSE_row) on the legal entries,
+//              dS^T = P^T (dP^T - D_row), written as BF16 pairs over the thread's
+//              own, already read S^T / dP^T columns.  They also fill a 4-entry
+//              ring with the blocks' Q / dO rows and each row's LSE, D and key
+//              bounds (a single producer warp sharing schedulers with these warps
+//              could not keep up), then write dK / dV.
+// TMEM: S^T[2] | dP^T[2] (64 columns each) | dV | dK.
 constexpr int kTcKeys = 128;
-constexpr int kTcRows = 128;
+constexpr int kTcRows = 64;
+constexpr int kTcStages = 4;
 constexpr int kTcThreads = 320;
-constexpr uint32_t kTcTile = 128 * 256;  // 128 rows x 128 dims BF16 (two 16 KB halves)
+constexpr uint32_t kTcKvTile = 128 * 256;   // 128 keys x 128 dims BF16 (two 16 KB halves)
+constexpr uint32_t kTcRowTile = 64 * 256;   // 64 rows x 128 dims BF16 (two 8 KB halves)
 
 struct TcSmem {
   static constexpr uint32_t k = 0;
-  static constexpr uint32_t v = k + kTcTile;
-  static constexpr uint32_t stage = v + kTcTile;             // 2 x (Q, dO)
-  static constexpr uint32_t info = stage + 2 * 2 * kTcTile;   // 2 x (lse, D, lo, hi, pos) x 128
+  static constexpr uint32_t v = k + kTcKvTile;
+  static constexpr uint32_t stage = v + kTcKvTile;                   // kTcStages x (Q, dO)
+  static constexpr uint32_t info = stage + kTcStages * 2 * kTcRowTile;
   static constexpr uint32_t info_bytes = 5 * kTcRows * 4;
-  static constexpr uint32_t bars = info + 2 * info_bytes;     // kv_full, full[2], empty[2], s_full, p_full, done
-  static constexpr uint32_t misc = bars + 8 * 8;              // tmem holder, abort flag, slot ranges
+  static constexpr uint32_t bars = info + kTcStages * info_bytes;   // kv, full[4], empty[4], s_full[2], p_full[2], done
+  static constexpr uint32_t misc = bars + 16 * 8;                    // tmem holder, abort flag, slot ranges
   static constexpr uint32_t total = misc + 64;
 };
 constexpr uint32_t kTcSmemBytes = TcSmem::total + 1024;
@@ -338,24 +339,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
   uint64_t* kv_full = bars;
-  uint64_t* full = bars + 1;
-  uint64_t* empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* done = bars + 7;
+  uint64_t* full = bars + 1;                   // [kTcStages]
+  uint64_t* empty = full + kTcStages;          // [kTcStages]
+  uint64_t* s_full = empty + kTcStages;        // [2]
+  uint64_t* p_full = s_full + 2;               // [2]
+  uint64_t* done = p_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + TcSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::misc + 4);
-  int* ranges = reinterpret_cast<int*>(smem + TcSmem::misc + 8);  // s_lo[2], s_hi[2], tiles[2]
+  int* ranges = reinterpret_cast<int*>(smem + TcSmem::misc + 8);  // s_lo[2], s_hi[2], blocks[2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 256);  // every elementwise thread, once its copies landed
       mbar_init(&empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 256);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 256);
+    }
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -384,13 +387,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int ntiles = ranges[4] + ranges[5];
-  const uint32_t tm_st = tmem, tm_dpt = tmem + 128, tm_dv = tmem + 256, tm_dk = tmem + 384;
+  const int nblocks = ranges[4] + ranges[5];
+  const uint32_t tm_dv = tmem + 256, tm_dk = tmem + 384;
+  auto tm_st = [&](int t) { return tmem + 64 * (t & 1); };
+  auto tm_dpt = [&](int t) { return tmem + 128 + 64 * (t & 1); };
 
-  // Row blocks (rows of branch 0, then of branch 1) go through a 2-entry ring,
-  // filled by the 256 elementwise threads: thread pair 2 j, 2 j + 1 takes row j
-  // of a block (its position, bounds, LSE and D, and 8 of its 16 chunks of Q and
-  // dO each); every thread arrives on full[entry] once its copies landed.  No
+  // Row blocks (rows of branch 0, then of branch 1) go through a 4-entry ring,
+  // filled by the 256 elementwise threads: threads 4 j .. 4 j + 3 take row j of a
+  // block (its position, bounds, LSE and D, and 4 of its 16 chunks of Q and dO
+  // each); every thread arrives on full[entry] once its copies landed.  No
   // barrier among the threads, so a thread that left on a timed-out wait cannot
   // hold the others.
   const int et = threadIdx.x - 64;  // 0..255 among the elementwise threads
@@ -398,21 +403,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     const int branch = it < ranges[4] ? 0 : 1;
     const int t = branch ? it - ranges[4] : it;
     const int R0 = ranges[branch] * p.r + t * kTcRows;
-    return load_row(p, branch, b, g, ranges[2 + branch], R0 + (et >> 1));
+    return load_row(p, branch, b, g, ranges[2 + branch], R0 + (et >> 2));
   };
   auto issue_block = [&](int it, const RowReg& x) {
     const int branch = it < ranges[4] ? 0 : 1;
     const int t = branch ? it - ranges[4] : it;
     const int R0 = ranges[branch] * p.r + t * kTcRows;
-    const int s = it & 1;
-    const int rr = et >> 1, c0 = (et & 1) * 8;
+    const int s = it % kTcStages;
+    const int rr = et >> 2, c0 = (et & 3) * 4;
     if (c0 == 0) row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows).put(rr, x);
     const bool ok = x.pos >= 0;
     const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + x.pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
-    uint8_t* sq = smem + TcSmem::stage + s * 2 * kTcTile;
-    uint8_t* sdo = sq + kTcTile;
+    uint8_t* sq = smem + TcSmem::stage + s * 2 * kTcRowTile;
+    uint8_t* sdo = sq + kTcRowTile;
 #pragma unroll
-    for (int c = c0; c < c0 + 8; ++c) {
+    for (int c = c0; c < c0 + 4; ++c) {
       cp_async_16(smem_u32(sq + swz(kTcRows, rr, c)), p.q + row * 128 + 8 * c, ok);
       cp_async_16(smem_u32(sdo + swz(kTcRows, rr, c)), p.dout + row * 128 + 8 * c, ok);
     }
@@ -420,7 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   auto land_block = [&](int it) {
     asm volatile("cp.async.wait_all;" ::: "memory");
     fence_proxy_async_smem();
-    mbar_arrive(&full[it & 1]);
+    mbar_arrive(&full[it % kTcStages]);
   };
 
   if (warp == 0) {
@@ -439,31 +444,45 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     if (lane == 0) mbar_arrive(kv_full);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
+    constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 64, false, false);
     constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
     const uint64_t k_desc = make_smem_desc_sw128(smem_u32(smem + TcSmem::k), 16, 1024);
     const uint64_t v_desc = make_smem_desc_sw128(smem_u32(smem + TcSmem::v), 16, 1024);
-    bool ok = ntiles == 0 || warp_wait(kv_full, 0, abort_flag);
-    for (int it = 0; it < ntiles && ok; ++it) {
-      const int s = it & 1;
-      if (!warp_wait(&full[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcTile), doa = qa + kTcTile;
-      umma_ss_k128_warp(tm_st, k_desc, make_smem_desc_sw128(qa, 16, 1024), idesc_s);
-      umma_ss_k128_warp(tm_dpt, v_desc, make_smem_desc_sw128(doa, 16, 1024), idesc_s);
-      tc_commit_warp(s_full);
-      if (!warp_wait(p_full, it & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint64_t do_mn = make_smem_desc_sw128(doa, kTcTile / 2, 1024);
-      const uint64_t q_mn = make_smem_desc_sw128(qa, kTcTile / 2, 1024);
+    auto products = [&](int t) {  // dV += P^T dO, dK += dS^T Q of block t
+      const int s = t % kTcStages;
+      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcRowTile), doa = qa + kTcRowTile;
+      const uint64_t do_mn = make_smem_desc_sw128(doa, kTcRowTile / 2, 1024);
+      const uint64_t q_mn = make_smem_desc_sw128(qa, kTcRowTile / 2, 1024);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // rows 32 c .. 32 c + 31 (BF16 pairs in columns 64 (c / 2) + 16 (c % 2))
-        const uint32_t acol = 64 * (c >> 1) + 16 * (c & 1);
-        const uint32_t acc = (it > 0 || c > 0) ? 1u : 0u;
-        umma_ts_k32_warp(tm_dv, tm_st + acol, do_mn + 2 * c * 128, idesc_o, acc);
-        umma_ts_k32_warp(tm_dk, tm_dpt + acol, q_mn + 2 * c * 128, idesc_o, acc);
+      for (int c = 0; c < 2; ++c) {  // rows 32 c .. 32 c + 31: BF16 pairs in columns 32 c .. 32 c + 15
+        const uint32_t acc = (t > 0 || c > 0) ? 1u : 0u;
+        umma_ts_k32_warp(tm_dv, tm_st(t) + 32 * c, do_mn + 2 * c * 128, idesc_o, acc);
+        umma_ts_k32_warp(tm_dk, tm_dpt(t) + 32 * c, q_mn + 2 * c * 128, idesc_o, acc);
       }
       tc_commit_warp(&empty[s]);
+    };
+    bool ok = nblocks == 0 || warp_wait(kv_full, 0, abort_flag);
+    for (int it = 0; it < nblocks && ok; ++it) {
+      const int s = it % kTcStages;
+      if (!warp_wait(&full[s], (it / kTcStages) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // TMEM buffer it & 1 was last read by the products of block it - 2, issued earlier
+      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcRowTile), doa = qa + kTcRowTile;
+      umma_ss_k128_bhalf8k_warp(tm_st(it), k_desc, make_smem_desc_sw128(qa, 16, 1024), idesc_s);
+      umma_ss_k128_bhalf8k_warp(tm_dpt(it), v_desc, make_smem_desc_sw128(doa, 16, 1024), idesc_s);
+      tc_commit_warp(&s_full[it & 1]);
+      if (it >= 1) {
+        if (!warp_wait(&p_full[(it - 1) & 1], ((it - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        products(it - 1);
+      }
+    }
+    if (ok && nblocks >= 1) {
+      const int t = nblocks - 1;
+      if (warp_wait(&p_full[t & 1], (t >> 1) & 1, abort_flag)) {
+        tc_fence_after();
+        products(t);
+      }
     }
     // all MMAs complete before the epilogue reads (and before the CTA frees TMEM)
     tc_commit_warp(done);
@@ -471,30 +490,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     // ------------------------------------------------------------ elementwise + epilogue
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int key_row = 32 * quarter + lane;
-    const int key = k0 + key_row;
+    const int key = k0 + 32 * quarter + lane;
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int it = 0; it < ntiles && it < 2; ++it) {
-      issue_block(it, block_row(it));
-      land_block(it);
-    }
+    for (int it = 0; it < nblocks && it < kTcStages; ++it) issue_block(it, block_row(it));
+    for (int it = 0; it < nblocks && it < kTcStages; ++it) land_block(it);  // (one wait covers all)
     RowReg xn{};
-    for (int it = 0; it < ntiles; ++it) {
-      const int s = it & 1;
-      if (!warp_wait(s_full, it & 1, abort_flag)) { ok = false; break; }
+    for (int it = 0; it < nblocks; ++it) {
+      const int s = it % kTcStages, tb = it & 1;
+      const int refill = it - 1 + kTcStages;  // block for the entry block it - 1 frees
+      if (it >= 1 && refill < nblocks) xn = block_row(refill);  // loads in flight during this block
+      if (!warp_wait(&s_full[tb], (it >> 1) & 1, abort_flag)) { ok = false; break; }
       // (already complete: acquires the row data the other threads wrote)
-      if (!warp_wait(&full[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
-      if (it + 2 < ntiles) xn = block_row(it + 2);  // loads in flight during this block
+      if (!warp_wait(&full[s], (it / kTcStages) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const RowInfo ri = row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows);
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      {
         uint32_t sr[32], dr[32];
-        const uint32_t col = 64 * half + 32 * cc;
-        tmem_ld_x32(tm_st + lane_off + col, sr);
-        tmem_ld_x32(tm_dpt + lane_off + col, dr);
+        tmem_ld_x32(tm_st(it) + lane_off + 32 * half, sr);
+        tmem_ld_x32(tm_dpt(it) + lane_off + 32 * half, dr);
         tmem_ld_wait();
         reg_fence32(sr);
         reg_fence32(dr);
@@ -504,7 +519,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
           float pv[2], dsv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int rr = col + 2 * j + e;  // row of the block
+            const int rr = 32 * half + 2 * j + e;  // row of the block
             const bool legal = key >= ri.lo[rr] && key < ri.hi[rr];
             pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ri.lse[rr]) : 0.0f;
             dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ri.d[rr]);
@@ -512,28 +527,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
           pk[j] = pack_bf16x2(pv[0], pv[1]);
           dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
-        // over this thread's own, already read columns: 64 half + 16 cc .. + 15
-        tmem_st_x16(tm_st + lane_off + 64 * half + 16 * cc, pk);
-        tmem_st_x16(tm_dpt + lane_off + 64 * half + 16 * cc, dk2);
+        // over this thread's own, already read columns: 32 half .. 32 half + 15
+        tmem_st_x16(tm_st(it) + lane_off + 32 * half, pk);
+        tmem_st_x16(tm_dpt(it) + lane_off + 32 * half, dk2);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
-      // block it + 1's copies were issued one block ago: retire them now, while the
-      // dV / dK products of this block run (the S MMAs of block it + 1 follow them)
-      if (it + 1 >= 2 && it + 1 < ntiles) land_block(it + 1);
-      if (it + 2 < ntiles) {
-        // ring entry s is free once the dV / dK products of block it have read it
-        // (they follow p_full, so every thread is done with its row data too)
-        if (!warp_wait(&empty[s], (it >> 1) & 1, abort_flag)) { ok = false; break; }
-        issue_block(it + 2, xn);
+      mbar_arrive(&p_full[tb]);
+      if (it >= 1) {
+        // the block issued one iteration ago lands now; then the entry that block
+        // it - 1 used is refilled (its products were issued before this block's end)
+        if (it - 2 + kTcStages < nblocks && it >= 2) land_block(it - 2 + kTcStages);
+        if (refill < nblocks) {
+          if (!warp_wait(&empty[(it - 1) % kTcStages], ((it - 1) / kTcStages) & 1, abort_flag)) { ok = false; break; }
+          issue_block(refill, xn);
+        }
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort: copies still in flight)
     // epilogue: dK (scaled) and dV of this thread's key, dims 64 half .. 64 half + 63.
-    // tcgen05.ld is warp-collective: every lane loads (the condition is made warp
+    // tcgen05.ld is warp-collective: every lane loads (the condition is warp
     // uniform), only the stores of keys past Skv are skipped.
-    if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
+    if (ok && nblocks > 0) ok = warp_wait(done, 0, abort_flag);
     tc_fence_after();
     const bool store = key < p.Skv;
     const int64_t row = (static_cast<int64_t>(b) * p.Skv + (store ? key : 0)) * p.Hkv + g;
@@ -545,7 +560,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         uint32_t r[32];
-        if (ntiles > 0 && ok) {
+        if (nblocks > 0 && ok) {
           tmem_ld_x32(src + 32 * cc, r);
           tmem_ld_wait();
           reg_fence32(r);

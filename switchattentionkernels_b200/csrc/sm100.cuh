@@ -216,6 +216,30 @@ __device__ __forceinline__ void umma_ss_k128_warp(uint32_t d_tmem, uint64_t a_de
       : "memory");
 }
 
+// As umma_ss_k128_warp with an N = 64 B operand whose two 64-column halves lie
+// 8192 bytes apart (a 64-row swizzled tile); A's halves lie 16384 bytes apart.
+__device__ __forceinline__ void umma_ss_k128_bhalf8k_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                          uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, p1;\n\t.reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n\t"
+      "setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\tadd.s64 a4, %1, 1024;\n\t"
+      "add.s64 a5, %1, 1026;\n\tadd.s64 a6, %1, 1028;\n\tadd.s64 a7, %1, 1030;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\tadd.s64 b4, %2, 512;\n\t"
+      "add.s64 b5, %2, 514;\n\tadd.s64 b6, %2, 516;\n\tadd.s64 b7, %2, 518;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+
 // Two back-to-back TS MMAs over 32 keys (A = P from TMEM, 8 columns per 16 keys;
 // B = V MN-major, 2048 bytes per 16 keys); `accumulate_first` = 0 makes the first
 // step overwrite D.
