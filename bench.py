@@ -64,6 +64,10 @@ def parse_args():
     ap.add_argument("--cp", action="store_true",
                     help="instead of the default line: context-parallel prefill over the N ranks "
                          "(strong scaling; K/V all-gather + kernel per step)")
+    ap.add_argument("--sharded", action="store_true",
+                    help="instead of the default line: config 3's batch split over the N ranks by (batch, KV group) "
+                         "units (strong scaling)")
+    ap.add_argument("--gather", action="store_true", help="with --sharded: all-gather O and LSE to every rank")
     ap.add_argument("--backward", action="store_true",
                     help="instead of the default line: the prefill backward (dQ, dK, dV) of the config-3 workload")
     ap.add_argument("--decode", action="store_true",
@@ -248,6 +252,77 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------- GPU arm
+def run_sharded(args, world, rank, local_rank):
+    """Config 3's batch (B = 4, 32 (batch, KV group) units) split over ``world`` ranks.
+
+    Every rank holds the same inputs; units go to ranks longest-processing-time
+    first on their legal-entry cost (``sharded.plan_units``) and each rank runs
+    the kernel on its units only.  With ``--gather`` every step ends with the
+    NCCL all-gather of O and LSE, so every rank holds the whole result.
+    ``value`` = effective FLOP of the batch / the slowest rank's step time
+    (strong scaling).
+    """
+    import torch.distributed as dist
+    from switchattentionkernels_b200 import build_switch_query_indices_batched
+    from switchattentionkernels_b200.sharded import _host_lists, sharded_switch_gqa_prefill_forward, unit_costs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29650 + os.getpid() % 200))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    w = workloads.make_inputs(CONFIG_ID, device=dev, on_device=True)
+    cfg = w["cfg"]
+    q, k, v, mask, W = w["q"], w["k"], w["v"], w["mask"], w["window"]
+    full, local, counts = build_switch_query_indices_batched(mask.to(dev))
+    fl, ll = _host_lists(full, local, counts, q.shape[0])
+    costs = unit_costs(fl, ll, hkv=k.shape[2], skv=k.shape[1], window=W)
+    flops = workloads.effective_flops(mask.numpy(), W, q.shape[1], q.shape[2])
+
+    def step():
+        return sharded_switch_gqa_prefill_forward(q, k, v, full, local, window_size=W, query_counts=counts,
+                                                  gather=args.gather, validate=False, costs=costs)
+
+    plan = None
+    for _ in range(args.warmup):
+        _, _, plan = step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.mark("begin")
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark("end")
+    dist.barrier()
+    clock_info = clocks.stop()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_max = float(ms.item())
+    dist.destroy_process_group()
+    if rank == 0:
+        peak_burst, _, peak_src = measured_peaks()
+        value = flops / (ms_max * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "effective TFLOP/s, (batch, KV group) units sharded over the GPUs", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "units": len(costs), "units_per_rank": [len(u) for u in plan],
+                       "gather_o_lse": bool(args.gather), "effective_tflop_per_step": flops / 1e12},
+            "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst, "peak_source": peak_src,
+            "gpu_launches": args.steps,  # the prefill kernel, once per step and rank
+            "clocks": clock_info,
+        }), flush=True)
+    return 0
+
+
 def run_backward(args, world, rank, local_rank):
     """Prefill backward of the config-3 workload (``--batch`` sequences per GPU).
 
@@ -487,6 +562,8 @@ def main():
         return run_decode(args, world, rank, local_rank)
     if args.backward and args.impl == "ours":
         return run_backward(args, world, rank, local_rank)
+    if args.sharded and args.impl == "ours":
+        return run_sharded(args, world, rank, local_rank)
     if args.cp and args.impl == "ours":
         rc = run_cp(args, world, rank, local_rank)
         if world > 1:
