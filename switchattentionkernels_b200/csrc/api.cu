@@ -313,7 +313,12 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   p.scale_log2 = scale_log2;
   p.scale = scale_log2 / 1.4426950408889634f;
   for (int br = 0; br < 2; ++br)
-    p.nblk[br] = static_cast<int>((static_cast<int64_t>(p.idx_stride[br]) * p.r + 63) / 64);
+    p.nblk[br] = static_cast<int>((static_cast<int64_t>(p.idx_stride[br]) * p.r + 127) / 128);
+  const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Skv), static_cast<uint64_t>(B)};
+  const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Skv) * Hkv * 256};
+  const uint32_t kb[4] = {64, 1, 64, 1};
+  if (!swa::make_bf16_map_sw128(&p.k_map, k, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+  if (!swa::make_bf16_map_sw128(&p.v_map, v, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // rows that no list routes keep a zero gradient
   cudaError_t e = cudaMemsetAsync(dq, 0, static_cast<size_t>(B) * Sq * Hq * 128 * 2, s);

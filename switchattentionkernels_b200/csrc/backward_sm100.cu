@@ -11,17 +11,15 @@
 // the r heads that share K/V sit in one matrix dimension and dK / dV sum over
 // them inside the matrix products.
 //   bwd_dsum_kernel : D for every (position, head), one warp per row.
-//   bwd_dq_kernel   : one CTA per 64 packed rows (16 per warp); loops over the
-//                     64-key tiles of the rows' union key range: S = Q K^T and
-//                     dP = dO V^T, dS, dQ += dS K.
+//   bwd_dq_tc_kernel : one CTA per 128 packed rows; loops over the 64-key tiles
+//                     of the rows' union key range: S = Q K^T and dP = dO V^T,
+//                     dS, dQ += dS K, on tcgen05 (see its comment below).
 //   bwd_dkv_tc_kernel: one CTA per 128-key tile; loops over the packed rows
 //                     whose key range meets the tile (a slot range per branch,
-//                     found by binary search in the sorted index lists), 128 at
+//                     found by binary search in the sorted index lists), 64 at
 //                     a time, on tcgen05 (see its comment below).
-// The dQ pass runs on mma.sync m16n8k16 (BF16 in, FP32 accumulate; P and dS
-// rounded to BF16 as operands), every operand read from row-major swizzled
-// shared tiles by plain or transposed ldmatrix, K/V tiles double-buffered by
-// cp.async; porting it to tcgen05 like the dK/dV pass is the next step.
+// Both passes take BF16 operands with FP32 accumulation in TMEM; P and dS are
+// rounded to BF16 where they are operands of a product.
 #include "mma_sync.cuh"
 #include "sm100.cuh"
 #include "swattn_internal.h"
@@ -29,10 +27,6 @@
 namespace swa {
 
 namespace {
-
-constexpr int kBwdThreads = 128;
-constexpr int kQRows = 64;   // dQ pass: packed rows per CTA
-constexpr int kTile = 64;    // keys per tile
 
 __device__ __forceinline__ void bwd_row_bounds(const BwdParams& p, int branch, int pos, int& lo, int& hi) {
   if (p.ends != nullptr) {
@@ -99,32 +93,6 @@ __device__ __forceinline__ RowInfo row_info_at(uint8_t* base, int rows) {
   return r;
 }
 
-// Asynchronous gather of the Q and dO rows of a block (positions already in
-// shared memory); absent rows are zero-filled.
-__device__ __forceinline__ void gather_rows_async(const BwdParams& p, int b, int g, int R0, int rows, const int* spos,
-                                                  uint8_t* sq, uint8_t* sdo) {
-  for (int i = threadIdx.x; i < rows * 16; i += kBwdThreads) {
-    const int rr = i >> 4, c = i & 15;
-    const int pos = spos[rr];
-    const bool ok = pos >= 0;
-    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
-    cp_async_16(smem_u32(sq + swz(rows, rr, c)), p.q + row * 128 + 8 * c, ok);
-    cp_async_16(smem_u32(sdo + swz(rows, rr, c)), p.dout + row * 128 + 8 * c, ok);
-  }
-}
-
-// Asynchronous load of keys [k0, k0 + 64) of (b, g) of K and V (zeros past Skv).
-__device__ __forceinline__ void gather_keys_async(const BwdParams& p, int b, int g, int k0, uint8_t* sk, uint8_t* sv) {
-  for (int i = threadIdx.x; i < kTile * 16; i += kBwdThreads) {
-    const int kr = i >> 4, c = i & 15;
-    const int key = k0 + kr;
-    const bool ok = key < p.Skv;
-    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g : 0;
-    cp_async_16(smem_u32(sk + swz(kTile, kr, c)), p.k + row * 128 + 8 * c, ok);
-    cp_async_16(smem_u32(sv + swz(kTile, kr, c)), p.v + row * 128 + 8 * c, ok);
-  }
-}
-
 __global__ void __launch_bounds__(256) bwd_dsum_kernel(const __grid_constant__ BwdParams p) {
   const int64_t rows = static_cast<int64_t>(p.B) * p.Sq * p.Hq;
   const int lane = threadIdx.x & 31;
@@ -137,141 +105,6 @@ __global__ void __launch_bounds__(256) bwd_dsum_kernel(const __grid_constant__ B
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (lane == 0) p.dsum[row] = s;
-  }
-}
-
-struct DqSmem {
-  static constexpr uint32_t q = 0;
-  static constexpr uint32_t dout = q + kQRows * 256;
-  static constexpr uint32_t kv = dout + kQRows * 256;         // 2 x (K tile, V tile)
-  static constexpr uint32_t info = kv + 2 * 2 * kTile * 256;  // lse, D, lo, hi, pos x 64, range
-  static constexpr uint32_t total = info + 5 * kQRows * 4 + 16;
-};
-
-__global__ void __launch_bounds__(kBwdThreads) bwd_dq_kernel(const __grid_constant__ BwdParams p) {
-  const int g = blockIdx.y, b = blockIdx.z;
-  int blk = blockIdx.x, branch = 0;
-  if (blk >= p.nblk[0]) {
-    blk -= p.nblk[0];
-    branch = 1;
-  }
-  const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
-  const int R0 = blk * kQRows;
-  if (R0 >= cnt * p.r) return;
-  extern __shared__ uint8_t bsm_raw[];
-  uint8_t* smem =
-      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const RowInfo ri = row_info_at(smem + DqSmem::info, kQRows);
-  int* range = ri.pos + kQRows;  // union key range of the CTA's rows
-  if (threadIdx.x == 0) {
-    range[0] = 0x7fffffff;
-    range[1] = 0;
-  }
-  if (threadIdx.x < kQRows) ri.put(threadIdx.x, load_row(p, branch, b, g, cnt, R0 + threadIdx.x));
-  __syncthreads();
-  gather_rows_async(p, b, g, R0, kQRows, ri.pos, smem + DqSmem::q, smem + DqSmem::dout);
-  cp_async_commit();
-  if (threadIdx.x < kQRows && ri.hi[threadIdx.x] > ri.lo[threadIdx.x]) {
-    atomicMin(&range[0], ri.lo[threadIdx.x]);
-    atomicMax(&range[1], ri.hi[threadIdx.x]);
-  }
-  __syncthreads();
-  const int lo_u = range[0], hi_u = range[1];
-  const int kfirst = lo_u < hi_u ? (lo_u / kTile) * kTile : hi_u;
-  const int ntiles = lo_u < hi_u ? (hi_u - kfirst + kTile - 1) / kTile : 0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mat = lane >> 3, mr = lane & 7;
-  const int r0 = 16 * warp + (lane >> 2), r1 = r0 + 8;
-  const uint32_t aq = smem_u32(smem + DqSmem::q), ado = smem_u32(smem + DqSmem::dout);
-  const float sl2 = p.scale_log2;
-  const int lo0 = ri.lo[r0], hi0 = ri.hi[r0], lo1 = ri.lo[r1], hi1 = ri.hi[r1];
-  const float l0 = ri.lse[r0], l1 = ri.lse[r1], d0 = ri.d[r0], d1 = ri.d[r1];
-  float dq[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.0f;
-  if (ntiles > 0) {
-    gather_keys_async(p, b, g, kfirst, smem + DqSmem::kv, smem + DqSmem::kv + kTile * 256);
-    cp_async_commit();
-  }
-  for (int t = 0; t < ntiles; ++t) {
-    const int k0 = kfirst + t * kTile;
-    uint8_t* kvb = smem + DqSmem::kv + (t & 1) * 2 * kTile * 256;
-    if (t + 1 < ntiles) {
-      uint8_t* nb = smem + DqSmem::kv + ((t + 1) & 1) * 2 * kTile * 256;
-      gather_keys_async(p, b, g, k0 + kTile, nb, nb + kTile * 256);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t ak = smem_u32(kvb), av = smem_u32(kvb + kTile * 256);
-    float s[8][4], dp[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = dp[n][0] = dp[n][1] = dp[n][2] = dp[n][3] = 0.0f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t qa[4], da[4];
-      const int arow = 16 * warp + (mat & 1) * 8 + mr, ac = 2 * ks + (mat >> 1);
-      ldsm_x4(aq + swz(kQRows, arow, ac), qa[0], qa[1], qa[2], qa[3]);
-      ldsm_x4(ado + swz(kQRows, arow, ac), da[0], da[1], da[2], da[3]);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        const int key = 16 * np + (mat >> 1) * 8 + mr, bc = 2 * ks + (mat & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(ak + swz(kTile, key, bc), b0, b1, b2, b3);
-        mma_bf16(s[2 * np], qa, b0, b1);
-        mma_bf16(s[2 * np + 1], qa, b2, b3);
-        ldsm_x4(av + swz(kTile, key, bc), b0, b1, b2, b3);
-        mma_bf16(dp[2 * np], da, b0, b1);
-        mma_bf16(dp[2 * np + 1], da, b2, b3);
-      }
-    }
-    // dS = P (dP - D) on the rows' legal keys
-    uint32_t dsa[4][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      float ds[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = k0 + 8 * n + 2 * (lane & 3) + (e & 1);
-        const bool top = e < 2;
-        const bool legal = key >= (top ? lo0 : lo1) && key < (top ? hi0 : hi1);
-        const float pv = legal ? ex2_approx(s[n][e] * sl2 - (top ? l0 : l1)) : 0.0f;
-        ds[e] = pv * (dp[n][e] - (top ? d0 : d1));
-      }
-      dsa[n >> 1][(n & 1) * 2] = pack_bf16x2(ds[0], ds[1]);
-      dsa[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
-    }
-    // dQ += dS K (K read transposed: the key dimension is the reduction)
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int nd = 0; nd < 16; nd += 2) {
-        const int key = 16 * kk + (mat & 1) * 8 + mr, bc = nd + (mat >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(ak + swz(kTile, key, bc), b0, b1, b2, b3);
-        mma_bf16(dq[nd], dsa[kk], b0, b1);
-        mma_bf16(dq[nd + 1], dsa[kk], b2, b3);
-      }
-    }
-    __syncthreads();  // this K/V buffer is refilled two tiles later
-  }
-  cp_async_wait<0>();  // (no tile: the row gather is still outstanding)
-  // write dQ (scaled) of the present rows
-  const float sc = p.scale;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int rr = h ? r1 : r0;
-    const int pos = ri.pos[rr];
-    if (pos < 0) continue;
-    const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + (R0 + rr) % p.r;
-#pragma unroll
-    for (int nd = 0; nd < 16; ++nd) {
-      const int col = 8 * nd + 2 * (lane & 3);
-      *reinterpret_cast<uint32_t*>(p.dq + row * 128 + col) =
-          pack_bf16x2(dq[nd][2 * h] * sc, dq[nd][2 * h + 1] * sc);
-    }
   }
 }
 
@@ -597,15 +430,303 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   if (threadIdx.x == 0 && *abort_flag) atomicOr(p.status, kStatusTimeout);
 }
 
+// ---------------------------------------------------------------------------
+// dQ pass on the 5th-generation tensor cores.  One CTA per 128 packed rows of
+// (branch, b, g), 320 threads, over the 64-key tiles of the rows' union key
+// range [lo of the first row, hi of the last):
+//   warp 0     TMA loads of the K and V tiles (two 64-dim halves each, 128B
+//              swizzle) into a 6-entry ring.
+//   warp 1     MMA: per tile t, S = Q K^T and dP = dO V^T into TMEM buffer t & 1
+//              (TS: Q and dO sit in TMEM, the K-major key tile is the B operand,
+//              so only B is read from shared memory -- with N = 64 an SS product
+//              would need more shared-memory bandwidth than the SM has); then,
+//              once dS of tile t - 1 is in TMEM, dQ += dS K (TS, K MN-major),
+//              whose commit frees ring entry t - 1.  The products of tile t + 1
+//              thus run while the elementwise warps work on tile t.
+//   warps 2-9  two threads per row (TMEM lane = row; the two 64-dim halves of
+//              Q / dO, the two 32-key halves of a tile): first the row's Q and dO
+//              into TMEM; per tile P = 2^(S scale_log2 - LSE) on the row's legal
+//              keys and dS = P (dP - D), written as BF16 pairs over the thread's
+//              own, already read dP columns; finally dQ (scaled) of the row.
+// TMEM: Q | dO (64 columns each, BF16 pairs) | S[2] | dP[2] (64 each) | dQ (128).
+// Full-branch blocks run latest rows first: their key ranges, and so their
+// run times, grow with the position.
+constexpr int kDqRows = 128;
+constexpr int kDqKeys = 64;
+constexpr int kDqStages = 6;
+constexpr int kDqThreads = 320;
+constexpr uint32_t kDqKeyTile = kDqKeys * 256;  // 64 keys x 128 dims BF16 (two 8 KB halves)
+
+struct DqTcSmem {
+  static constexpr uint32_t stage = 0;                                   // kDqStages x (K tile, V tile)
+  static constexpr uint32_t bars = stage + kDqStages * 2 * kDqKeyTile;   // rows_full, full[6], empty[6], s_full[2], p_full[2], done
+  static constexpr uint32_t misc = bars + 24 * 8;                        // tmem holder, abort flag, key range
+  static constexpr uint32_t total = misc + 32;
+};
+constexpr uint32_t kDqTcSmemBytes = DqTcSmem::total + 1024;
+
+__global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_constant__ BwdParams p) {
+  const int g = blockIdx.y, b = blockIdx.z;
+  const int nblk0 = p.nblk[0];
+  int blk = blockIdx.x, branch = 0;
+  if (blk >= nblk0) {
+    blk -= nblk0;
+    branch = 1;
+  } else {
+    blk = nblk0 - 1 - blk;
+  }
+  const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+  const int R0 = blk * kDqRows;
+  if (R0 >= cnt * p.r) return;  // (the whole CTA, before any barrier or TMEM use)
+  extern __shared__ uint8_t bsm_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DqTcSmem::bars);
+  uint64_t* rows_full = bars;
+  uint64_t* full = bars + 1;             // [kDqStages]
+  uint64_t* empty = full + kDqStages;    // [kDqStages]
+  uint64_t* s_full = empty + kDqStages;  // [2]
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* done = p_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + DqTcSmem::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + DqTcSmem::misc + 4);
+  int* range = reinterpret_cast<int*>(smem + DqTcSmem::misc + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(rows_full, 256);
+    for (int s = 0; s < kDqStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 256);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    range[0] = 0x7fffffff;
+    range[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // elementwise threads: row 32 quarter + lane of the block, dims / keys half
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const int row = 32 * quarter + lane;
+  RowReg x{-1, 0, 0, 0.0f, 0.0f};
+  uint4 qv[8], dv[8];
+  if (warp >= 2) {
+    x = load_row(p, branch, b, g, cnt, R0 + row);
+    if (half == 0 && x.hi > x.lo) {
+      atomicMin(&range[0], x.lo);
+      atomicMax(&range[1], x.hi);
+    }
+    // this thread's 64 dims of the row's Q and dO (in flight across the barrier)
+    const int64_t grow = (static_cast<int64_t>(b) * p.Sq + max(x.pos, 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
+    const uint4* qs = reinterpret_cast<const uint4*>(p.q + grow * 128 + 64 * half);
+    const uint4* ds = reinterpret_cast<const uint4*>(p.dout + grow * 128 + 64 * half);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      qv[j] = x.pos >= 0 ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
+      dv[j] = x.pos >= 0 ? __ldg(ds + j) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (warp == 0) {
+    __syncwarp();  // tcgen05.alloc is warp-collective: lane 0 comes from the set-up above
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int lo_u = range[0], hi_u = range[1];
+  const int kfirst = lo_u < hi_u ? (lo_u / kDqKeys) * kDqKeys : 0;
+  const int ntiles = lo_u < hi_u ? (hi_u - kfirst + kDqKeys - 1) / kDqKeys : 0;
+  const uint32_t tm_q = tmem, tm_do = tmem + 64, tm_dq = tmem + 384;
+  auto tm_s = [&](int t) { return tmem + 128 + 64 * (t & 1); };
+  auto tm_dp = [&](int t) { return tmem + 256 + 64 * (t & 1); };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ K / V tiles
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&p.k_map);
+      tma_prefetch_desc(&p.v_map);
+      int t = 0;
+      for (; t < ntiles; ++t) {
+        const int s = t % kDqStages;
+        if (!mbar_wait(&empty[s], ((t / kDqStages) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], 2 * kDqKeyTile);
+        uint8_t* dst = smem + DqTcSmem::stage + s * 2 * kDqKeyTile;
+        const int key0 = kfirst + t * kDqKeys;
+        tma_load_4d(dst, &p.k_map, &full[s], 0, g, key0, b);
+        tma_load_4d(dst + kDqKeyTile / 2, &p.k_map, &full[s], 64, g, key0, b);
+        tma_load_4d(dst + kDqKeyTile, &p.v_map, &full[s], 0, g, key0, b);
+        tma_load_4d(dst + kDqKeyTile + kDqKeyTile / 2, &p.v_map, &full[s], 64, g, key0, b);
+      }
+      if (*abort_flag) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int u = max(0, t - kDqStages); u < t; ++u) {
+          volatile int dummy = 0;
+          mbar_wait(&full[u % kDqStages], (u / kDqStages) & 1, &dummy);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 64, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
+    auto product = [&](int t) {  // dQ += dS K of tile t (dS over the dP columns)
+      const int s = t % kDqStages;
+      const uint64_t k_mn = make_smem_desc_sw128(smem_u32(smem + DqTcSmem::stage + s * 2 * kDqKeyTile),
+                                                 kDqKeyTile / 2, 1024);
+#pragma unroll
+      for (int c = 0; c < 2; ++c)  // keys 32 c .. 32 c + 31: BF16 pairs in columns 32 c .. 32 c + 15
+        umma_ts_k32_warp(tm_dq, tm_dp(t) + 32 * c, k_mn + 2 * c * 128, idesc_o, (t > 0 || c > 0) ? 1u : 0u);
+      tc_commit_warp(&empty[s]);
+    };
+    bool ok = ntiles == 0 || warp_wait(rows_full, 0, abort_flag);
+    if (ok) tc_fence_after();
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int s = t % kDqStages;
+      if (!warp_wait(&full[s], (t / kDqStages) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // TMEM buffer t & 1 was last read by the product of tile t - 2, issued earlier
+      const uint32_t ka = smem_u32(smem + DqTcSmem::stage + s * 2 * kDqKeyTile), va = ka + kDqKeyTile;
+      umma_ts_k128_bhalf8k_warp(tm_s(t), tm_q, make_smem_desc_sw128(ka, 16, 1024), idesc_s);
+      umma_ts_k128_bhalf8k_warp(tm_dp(t), tm_do, make_smem_desc_sw128(va, 16, 1024), idesc_s);
+      tc_commit_warp(&s_full[t & 1]);
+      if (t >= 1) {
+        if (!warp_wait(&p_full[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        product(t - 1);
+      }
+    }
+    if (ok && ntiles >= 1) {
+      const int t = ntiles - 1;
+      if (warp_wait(&p_full[t & 1], (t >> 1) & 1, abort_flag)) {
+        tc_fence_after();
+        product(t);
+      }
+    }
+    // all MMAs complete before the epilogue reads (and before the CTA frees TMEM)
+    tc_commit_warp(done);
+  } else {
+    // ------------------------------------------------------------ elementwise + epilogue
+    const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
+    {
+      uint32_t r[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        r[4 * j] = qv[j].x;
+        r[4 * j + 1] = qv[j].y;
+        r[4 * j + 2] = qv[j].z;
+        r[4 * j + 3] = qv[j].w;
+      }
+      tmem_st_x32(tm_q + lane_off + 32 * half, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        r[4 * j] = dv[j].x;
+        r[4 * j + 1] = dv[j].y;
+        r[4 * j + 2] = dv[j].z;
+        r[4 * j + 3] = dv[j].w;
+      }
+      tmem_st_x32(tm_do + lane_off + 32 * half, r);
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    mbar_arrive(rows_full);
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const int tb = t & 1;
+      if (!warp_wait(&s_full[tb], (t >> 1) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[32], dr[32];
+      tmem_ld_x32(tm_s(t) + lane_off + 32 * half, sr);
+      tmem_ld_x32(tm_dp(t) + lane_off + 32 * half, dr);
+      tmem_ld_wait();
+      reg_fence32(sr);
+      reg_fence32(dr);
+      // legal keys of the row among this thread's 32: i in [i_lo, i_hi)
+      const int key0 = kfirst + kDqKeys * t + 32 * half;
+      const int i_lo = x.lo - key0, i_hi = x.hi - key0;
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float dsv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int i = 2 * j + e;
+          const bool legal = i >= i_lo && i < i_hi;
+          const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - x.lse) : 0.0f;
+          dsv[e] = pv * (__uint_as_float(dr[i]) - x.d);
+        }
+        pk[j] = pack_bf16x2(dsv[0], dsv[1]);
+      }
+      // over this thread's own, already read columns: 32 half .. 32 half + 15
+      tmem_st_x16(tm_dp(t) + lane_off + 32 * half, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[tb]);
+    }
+    // epilogue: dQ (scaled) of this thread's row, dims 64 half .. 64 half + 63.
+    // tcgen05.ld is warp-collective: every lane loads (the condition is warp
+    // uniform), only the stores of absent rows are skipped.
+    if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
+    tc_fence_after();
+    const bool store = x.pos >= 0;
+    const int64_t grow = (static_cast<int64_t>(b) * p.Sq + (store ? x.pos : 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
+    __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half;
+    const float sc = p.scale;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t r[32];
+      if (ntiles > 0 && ok) {
+        tmem_ld_x32(tm_dq + lane_off + 64 * half + 32 * cc, r);
+        tmem_ld_wait();
+        reg_fence32(r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (store) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
+          w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
+          w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
+          w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
+          *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
+        }
+      }
+    }
+  }
+  // teardown: the MMA warp's `done` commit covers every MMA it issued
+  if (warp == 1) {
+    volatile int dummy = 0;
+    mbar_wait(done, 0, &dummy);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(p.status, kStatusTimeout);
+}
+
 }  // namespace
 
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint32_t dq_smem = DqSmem::total + 1024;
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dq_smem);
+    cudaError_t e = cudaFuncSetAttribute(bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqTcSmemBytes);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(bwd_dkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
     if (e != cudaSuccess) return e;
@@ -618,7 +739,7 @@ cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t s
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const dim3 gq(params.nblk[0] + params.nblk[1], params.Hkv, params.B);
-  if (gq.x > 0) bwd_dq_kernel<<<gq, kBwdThreads, dq_smem, stream>>>(params);
+  if (gq.x > 0) bwd_dq_tc_kernel<<<gq, kDqThreads, kDqTcSmemBytes, stream>>>(params);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const dim3 gkv((params.Skv + kTcKeys - 1) / kTcKeys, params.Hkv, params.B);

@@ -256,6 +256,33 @@ __device__ __forceinline__ void umma_ts_k32_warp(uint32_t d_tmem, uint32_t a_tme
       : "memory");
 }
 
+// Eight back-to-back TS MMAs over K = 128: A (M x 128, BF16 pairs) from TMEM, 8
+// columns per 16-element step; B a K-major 64-row swizzled tile whose two
+// 64-column halves lie 8192 bytes apart (step kk adds (kk / 4) * 8192 +
+// (kk % 4) * 32 bytes to its start address).  The first step overwrites D.
+__device__ __forceinline__ void umma_ts_k128_bhalf8k_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                          uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, p1;\n\t.reg .b64 b1, b2, b3, b4, b5, b6, b7;\n\t"
+      ".reg .b32 a1, a2, a3, a4, a5, a6, a7;\n\t"
+      "setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\tadd.u32 a4, %1, 32;\n\t"
+      "add.u32 a5, %1, 40;\n\tadd.u32 a6, %1, 48;\n\tadd.u32 a7, %1, 56;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\tadd.s64 b4, %2, 512;\n\t"
+      "add.s64 b5, %2, 514;\n\tadd.s64 b6, %2, 516;\n\tadd.s64 b7, %2, 518;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, p1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm100 version field = 1.
 //   K-major operand : lbo ignored (pass 16), sbo = byte stride between 8-row groups.
 //   MN-major operand: lbo = byte stride between 64-element MN blocks,
@@ -311,6 +338,15 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t* r) {
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       SWA_W8(0), SWA_W8(8)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      SWA_W8(0), SWA_W8(8), SWA_W8(16), SWA_W8(24)
       : "memory");
 }
 

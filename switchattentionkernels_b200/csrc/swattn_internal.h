@@ -75,7 +75,9 @@ struct __align__(64) DecodeParams {
 cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream);
 
 // Prefill backward: dQ, dK, dV of both branches.
-struct BwdParams {
+struct __align__(64) BwdParams {
+  CUtensorMap k_map;         // 4-D {128, Hkv, Skv, B}, box {64, 1, 64, 1}, 128B swizzle (dQ pass)
+  CUtensorMap v_map;
   const __nv_bfloat16 *q, *k, *v, *o, *dout;
   const float* lse;          // [B, Sq, Hq] forward LSE (log2 units)
   float* dsum;               // [B, Sq, Hq] rowsum(dO * O) (workspace)
@@ -87,7 +89,7 @@ struct BwdParams {
   __nv_bfloat16 *dq, *dk, *dv;
   int B, Sq, Skv, Hq, Hkv, r, window;
   float scale_log2, scale;   // softmax scale in log2 units and in natural units
-  int nblk[2];               // 64-row blocks of each branch per (batch, KV group)
+  int nblk[2];               // dQ pass: 128-row blocks of each branch per (batch, KV group)
   int32_t* status;           // kStatusTimeout when a bounded wait gave up
 };
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream);
