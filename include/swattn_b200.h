@@ -109,15 +109,19 @@ int swa_compact_router_ws(const void* router, int dtype, int pair, float thresho
  * (bf16) of the forward's output, from o, its lse (fp32 [B, Sq, Hq], log2
  * units) and dout (bf16, like o).  Index lists: -1 padded [B, stride] rows with
  * counts[2*b] = n_full, counts[2*b+1] = n_local (as swa_compact_mask writes
- * them); metadata as in swa_prefill_forward (nullable).  workspace: at least
- * B * Sq * Hq floats (rowsum(dout * o)) followed by a 16-byte status word whose
- * first int32 receives SWA_STATUS_TIMEOUT if a bounded device wait gave up. */
+ * them); metadata as in swa_prefill_forward (nullable).  workspace: 16-byte
+ * aligned, at least swa_backward_workspace_bytes(B, Hq, full_stride,
+ * local_stride) bytes (the routed rows' Q and dO in packed order with their key
+ * ranges, LSE and rowsum(dout * o): about 532 bytes per routed (position, head)
+ * slot of the lists); its first int32 receives SWA_STATUS_TIMEOUT if a bounded
+ * device wait gave up. */
+size_t swa_backward_workspace_bytes(int B, int Hq, int full_stride, int local_stride);
 int swa_prefill_backward(const void* q, const void* k, const void* v, const void* o, const float* lse,
                          const void* dout, const int32_t* full_idx, const int32_t* local_idx, int full_stride,
                          int local_stride, const int32_t* counts, const int32_t* full_starts,
                          const int32_t* local_starts, const int32_t* causal_ends, void* dq, void* dk, void* dv,
                          int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window, float scale_log2,
-                         float* workspace, size_t workspace_bytes, void* stream);
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Decode step (no counterpart in the reference, which is prefill only): one
  * new query token per sequence against its KV cache, routed per sequence.

@@ -44,6 +44,7 @@ EXPORTED = (
     "swa_decode_workspace_bytes",
     "swa_decode_forward",
     "swa_prefill_backward",
+    "swa_backward_workspace_bytes",
 )
 
 _lock = threading.Lock()
@@ -116,6 +117,8 @@ def _declare(lib) -> None:
         _i, _f,                  # window, scale_log2
         _p, _sz, _p,             # workspace, workspace_bytes, stream
     ]
+    lib.swa_backward_workspace_bytes.restype = _sz
+    lib.swa_backward_workspace_bytes.argtypes = [_i, _i, _i, _i]
     lib.swa_decode_workspace_bytes.restype = _sz
     lib.swa_decode_workspace_bytes.argtypes = [_i, _i, _i, _i]
     lib.swa_decode_forward.restype = _i

@@ -66,11 +66,12 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    ws = torch.empty(B * Sq * Hq + 4, dtype=torch.float32, device=dev)
     fs = ls = ce = None
     if metadata is not None:
         fs, ls, ce = metadata.full_starts, metadata.local_starts, metadata.causal_ends
     lib = _native.load()
+    ws_bytes = lib.swa_backward_workspace_bytes(B, Hq, int(f.shape[1]), int(l.shape[1]))
+    ws = torch.empty((ws_bytes + 15) // 16 * 4, dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         rc = lib.swa_prefill_backward(
             _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(out), _native.ptr(lse), _native.ptr(dout),
@@ -80,7 +81,7 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
             float(scale), _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
     _native.check(rc, "switch_gqa_prefill_backward")
     if os.environ.get("SWA_CHECK_STATUS") == "1":
-        _raise_status(int(ws[B * Sq * Hq:].view(torch.int32)[0].item()))
+        _raise_status(int(ws[0].item()))
     return dq, dk, dv
 
 

@@ -253,12 +253,17 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
   return SWA_OK;
 }
 
+size_t swa_backward_workspace_bytes(int B, int Hq, int full_stride, int local_stride) {
+  if (B <= 0 || Hq <= 0 || full_stride < 0 || local_stride < 0) return 0;
+  return swa::backward_workspace_bytes(B, Hq, full_stride, local_stride);
+}
+
 int swa_prefill_backward(const void* q, const void* k, const void* v, const void* o, const float* lse,
                          const void* dout, const int32_t* full_idx, const int32_t* local_idx, int full_stride,
                          int local_stride, const int32_t* counts, const int32_t* full_starts,
                          const int32_t* local_starts, const int32_t* causal_ends, void* dq, void* dk, void* dv,
                          int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window, float scale_log2,
-                         float* workspace, size_t workspace_bytes, void* stream) {
+                         void* workspace, size_t workspace_bytes, void* stream) {
   if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
   if (B <= 0 || Sq <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
   if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
@@ -276,10 +281,13 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   const bool has_meta = causal_ends != nullptr;
   if (has_meta && (full_starts == nullptr || local_starts == nullptr))
     return fail(SWA_E_INVALID, "metadata needs full_starts, local_starts and causal_ends");
-  if (workspace_bytes < static_cast<size_t>(B) * Sq * Hq * sizeof(float) + 16)
-    return fail(SWA_E_INVALID, "workspace must hold B * Sq * Hq floats and a 16-byte status word");
   if (static_cast<int64_t>(B) * Sq * Hq >= (int64_t(1) << 31) || static_cast<int64_t>(B) * Skv * Hkv >= (int64_t(1) << 31))
     return fail(SWA_E_UNSUPPORTED, "tensor too large for 32-bit row indices");
+  const int fs = full_idx ? full_stride : 0, ls = local_idx ? local_stride : 0;
+  if (static_cast<int64_t>(B) * Hq * (static_cast<int64_t>(fs) + ls) >= (int64_t(1) << 31))
+    return fail(SWA_E_UNSUPPORTED, "index lists too wide for 32-bit packed row indices");
+  if (!aligned16(workspace) || workspace_bytes < swa::backward_workspace_bytes(B, Hq, fs, ls))
+    return fail(SWA_E_INVALID, "workspace must be 16-byte aligned and hold swa_backward_workspace_bytes() bytes");
   int nsm = 0;
   int rc = device_sms(&nsm);
   if (rc != SWA_OK) return rc;
@@ -290,8 +298,6 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   p.o = static_cast<const __nv_bfloat16*>(o);
   p.dout = static_cast<const __nv_bfloat16*>(dout);
   p.lse = lse;
-  p.dsum = workspace;
-  p.status = reinterpret_cast<int32_t*>(workspace + static_cast<size_t>(B) * Sq * Hq);
   p.idx[0] = full_idx;
   p.idx[1] = local_idx;
   p.idx_stride[0] = full_idx ? full_stride : 0;
@@ -314,11 +320,19 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   p.scale = scale_log2 / 1.4426950408889634f;
   for (int br = 0; br < 2; ++br)
     p.nblk[br] = static_cast<int>((static_cast<int64_t>(p.idx_stride[br]) * p.r + 127) / 128);
+  swa::bind_backward_workspace(p, workspace);
   const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Skv), static_cast<uint64_t>(B)};
   const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Skv) * Hkv * 256};
   const uint32_t kb[4] = {64, 1, 64, 1};
   if (!swa::make_bf16_map_sw128(&p.k_map, k, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
   if (!swa::make_bf16_map_sw128(&p.v_map, v, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  const uint64_t prow = static_cast<uint64_t>(p.pk_rows > 0 ? p.pk_rows : 1);
+  const uint64_t pd[2] = {128, prow};
+  const uint64_t ps[1] = {256};
+  const uint32_t pb[2] = {64, 64};
+  if (!swa::make_bf16_map_sw128(&p.qp_map, p.qp, 2, pd, ps, pb)) return fail(SWA_E_TMA, "packed q tensor map");
+  if (!swa::make_bf16_map_sw128(&p.dop_map, p.dop, 2, pd, ps, pb)) return fail(SWA_E_TMA, "packed dout tensor map");
+  if (!swa::make_i32_map_2d(&p.rec_map, p.rec, 4, prow, 16, 4, 64)) return fail(SWA_E_TMA, "row record tensor map");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // rows that no list routes keep a zero gradient
   cudaError_t e = cudaMemsetAsync(dq, 0, static_cast<size_t>(B) * Sq * Hq * 128 * 2, s);

@@ -10,17 +10,18 @@
 // g) is routed slot R / r of the branch's list and query head g r + R % r, so
 // the r heads that share K/V sit in one matrix dimension and dK / dV sum over
 // them inside the matrix products.
-//   bwd_dsum_kernel : D for every (position, head), one warp per row.
+//   bwd_pack_kernel  : one warp per packed row: Q and dO copied into packed
+//                      order, the row's record {lo, hi, LSE, D} and position,
+//                      so both passes read contiguous rows without index chains.
 //   bwd_dq_tc_kernel : one CTA per 128 packed rows; loops over the 64-key tiles
-//                     of the rows' union key range: S = Q K^T and dP = dO V^T,
-//                     dS, dQ += dS K, on tcgen05 (see its comment below).
+//                      of the rows' union key range: S = Q K^T and dP = dO V^T,
+//                      dS, dQ += dS K, on tcgen05 (see its comment below).
 //   bwd_dkv_tc_kernel: one CTA per 128-key tile; loops over the packed rows
-//                     whose key range meets the tile (a slot range per branch,
-//                     found by binary search in the sorted index lists), 64 at
-//                     a time, on tcgen05 (see its comment below).
+//                      whose key range meets the tile (a slot range per branch,
+//                      found by binary search in the sorted index lists), 64 at
+//                      a time, on tcgen05 (see its comment below).
 // Both passes take BF16 operands with FP32 accumulation in TMEM; P and dS are
 // rounded to BF16 where they are operands of a product.
-#include "mma_sync.cuh"
 #include "sm100.cuh"
 #include "swattn_internal.h"
 
@@ -44,101 +45,103 @@ __device__ __forceinline__ float2 bf2_to_f2(uint32_t u) {
   return __bfloat1622float2(h);
 }
 
-// Per-row data of packed row R of (branch, b, g): position (-1 when absent),
-// legal key range (empty for absent rows and rows without legal keys), LSE, D.
-struct RowReg {
-  int pos, lo, hi;
-  float lse, d;
-};
-
-__device__ __forceinline__ RowReg load_row(const BwdParams& p, int branch, int b, int g, int cnt, int R) {
-  RowReg x{-1, 0, 0, 0.0f, 0.0f};
-  const int slot = R / p.r;
-  if (slot < cnt) {
-    const int pos = p.idx[branch][static_cast<int64_t>(b) * p.idx_stride[branch] + slot];
-    if (pos >= 0 && pos < p.Sq) {
-      const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
-      x.pos = pos;
-      bwd_row_bounds(p, branch, pos, x.lo, x.hi);
-      x.lse = p.lse[row];
-      x.d = p.dsum[row];
-      if (!(x.lse > -INFINITY)) x.hi = x.lo;  // a row without legal keys has no gradient
-    }
-  }
-  return x;
+// First packed row of (branch, b, g).
+__device__ __forceinline__ int64_t packed_base(const BwdParams& p, int branch, int b, int g) {
+  return (branch ? p.pk_n0 : 0) + (static_cast<int64_t>(b) * p.Hkv + g) * p.idx_stride[branch] * p.r;
 }
 
-struct RowInfo {  // shared-memory arrays of a block of packed rows
-  float* lse;
-  float* d;
-  int* lo;
-  int* hi;
-  int* pos;
-  __device__ __forceinline__ void put(int i, const RowReg& x) const {
-    pos[i] = x.pos;
-    lo[i] = x.lo;
-    hi[i] = x.hi;
-    lse[i] = x.lse;
-    d[i] = x.d;
-  }
-};
-
-__device__ __forceinline__ RowInfo row_info_at(uint8_t* base, int rows) {
-  RowInfo r;
-  r.lse = reinterpret_cast<float*>(base);
-  r.d = r.lse + rows;
-  r.lo = reinterpret_cast<int*>(r.d + rows);
-  r.hi = r.lo + rows;
-  r.pos = r.hi + rows;
-  return r;
-}
-
-__global__ void __launch_bounds__(256) bwd_dsum_kernel(const __grid_constant__ BwdParams p) {
-  const int64_t rows = static_cast<int64_t>(p.B) * p.Sq * p.Hq;
+__global__ void __launch_bounds__(256) bwd_pack_kernel(const __grid_constant__ BwdParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
-    const uint2 a = *reinterpret_cast<const uint2*>(p.dout + row * 128 + 4 * lane);
-    const uint2 o = *reinterpret_cast<const uint2*>(p.o + row * 128 + 4 * lane);
-    const float2 a0 = bf2_to_f2(a.x), a1 = bf2_to_f2(a.y), o0 = bf2_to_f2(o.x), o1 = bf2_to_f2(o.y);
-    float s = a0.x * o0.x + a0.y * o0.y + a1.x * o1.x + a1.y * o1.y;
+  for (int64_t pr = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; pr < p.pk_rows;
+       pr += warps) {
+    const int branch = pr < p.pk_n0 ? 0 : 1;
+    const int64_t local = branch ? pr - p.pk_n0 : pr;
+    const int64_t per = static_cast<int64_t>(p.idx_stride[branch]) * p.r;
+    const int64_t bg = local / per;
+    const int R = static_cast<int>(local - bg * per);
+    const int g = static_cast<int>(bg % p.Hkv), b = static_cast<int>(bg / p.Hkv);
+    const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+    const int slot = R / p.r;
+    int pos = -1;
+    if (slot < cnt) {
+      pos = p.idx[branch][static_cast<int64_t>(b) * p.idx_stride[branch] + slot];
+      if (pos < 0 || pos >= p.Sq) pos = -1;
+    }
+    uint2 qv = make_uint2(0, 0), dv = make_uint2(0, 0);
+    int4 rec = make_int4(0, 0, 0, 0);
+    if (pos >= 0) {  // (warp uniform)
+      const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
+      qv = *reinterpret_cast<const uint2*>(p.q + row * 128 + 4 * lane);
+      dv = *reinterpret_cast<const uint2*>(p.dout + row * 128 + 4 * lane);
+      const uint2 o = *reinterpret_cast<const uint2*>(p.o + row * 128 + 4 * lane);
+      const float2 a0 = bf2_to_f2(dv.x), a1 = bf2_to_f2(dv.y), o0 = bf2_to_f2(o.x), o1 = bf2_to_f2(o.y);
+      float d = a0.x * o0.x + a0.y * o0.y + a1.x * o1.x + a1.y * o1.y;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) p.dsum[row] = s;
+      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      int lo, hi;
+      bwd_row_bounds(p, branch, pos, lo, hi);
+      const float lse = p.lse[row];
+      if (!(lse > -INFINITY)) hi = lo;  // a row without legal keys has no gradient
+      rec = make_int4(lo, max(hi, lo), __float_as_int(lse), __float_as_int(d));
+    }
+    *reinterpret_cast<uint2*>(p.qp + pr * 128 + 4 * lane) = qv;
+    *reinterpret_cast<uint2*>(p.dop + pr * 128 + 4 * lane) = dv;
+    if (lane == 0) {
+      p.rec[pr] = rec;
+      p.rpos[pr] = pos;
+    }
   }
 }
 
-// First slot in [0, cnt) whose row satisfies pred (pred is monotone: false...true).
+// First slot in [0, cnt) whose row satisfies pred (monotone: false...true), or
+// cnt; the 32 lanes of a warp probe 32 points per round, so a list of 32^k slots
+// takes k rounds of one load each.  Warp-collective; every lane gets the result.
 template <typename Pred>
-__device__ __forceinline__ int first_slot(int cnt, Pred pred) {
+__device__ __forceinline__ int first_slot_warp(int cnt, Pred pred) {
+  const int lane = threadIdx.x & 31;
   int lo = 0, hi = cnt;
   while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (pred(mid))
-      hi = mid;
-    else
-      lo = mid + 1;
+    const int n = hi - lo;
+    const int s = lo + static_cast<int>((static_cast<int64_t>(n) * lane) >> 5);
+    const uint32_t m = __ballot_sync(0xffffffffu, pred(s));
+    if (m == 0u) {
+      lo = __shfl_sync(0xffffffffu, s, 31) + 1;
+    } else {
+      const int f = __ffs(m) - 1;
+      const int sf = __shfl_sync(0xffffffffu, s, f);
+      const int sp = __shfl_sync(0xffffffffu, s, f > 0 ? f - 1 : 0);
+      hi = sf;
+      lo = f > 0 ? sp + 1 : hi;
+    }
   }
   return lo;
+}
+
+// A bounded wait whose outcome is the same in every lane of the warp (the
+// warp-collective tcgen05 instructions after it need the whole warp).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
 }
 
 // ---------------------------------------------------------------------------
 // dK / dV pass on the 5th-generation tensor cores.  One CTA per 128-key tile of
 // (b, g), 320 threads, over blocks of 64 packed rows:
-//   warp 0     K and V tiles of the CTA (cp.async into 128B-swizzled tiles, the
-//              layout the MMA descriptors read).
+//   warp 0     TMA: the CTA's K and V tiles once, then per block the rows' Q and
+//              dO tiles and records (consecutive packed rows: one box each) into
+//              a 4-entry ring.
 //   warp 1     MMA: per block t, S^T = K Q^T and dP^T = V dO^T (SS, N = 64, both
 //              K-major) into TMEM buffer t & 1; then, once P^T / dS^T of block
 //              t - 1 are in TMEM, dV += P^T dO and dK += dS^T Q (TS, dO / Q
-//              MN-major).  The products of block t + 1 thus run while the
-//              elementwise warps work on block t.
+//              MN-major), whose commit frees ring entry t - 1.  The products of
+//              block t + 1 thus run while the elementwise warps work on block t.
 //   warps 2-9  elementwise: two threads per key (TMEM lane = key), 32 rows each:
 //              P^T = 2^(S^T scale_log2 - LSE_row) on the legal entries,
 //              dS^T = P^T (dP^T - D_row), written as BF16 pairs over the thread's
-//              own, already read S^T / dP^T columns.  They also fill a 4-entry
-//              ring with the blocks' Q / dO rows and each row's LSE, D and key
-//              bounds (a single producer warp sharing schedulers with these warps
-//              could not keep up), then write dK / dV.
+//              own, already read S^T / dP^T columns; then dK / dV.
+// A block starts at a slot-range row of its branch and may run past the range's
+// end into later rows (of this or the next (b, g)): those rows are masked by
+// their index in the block, whatever their records say.
 // TMEM: S^T[2] | dP^T[2] (64 columns each) | dV | dK.
 constexpr int kTcKeys = 128;
 constexpr int kTcRows = 64;
@@ -146,24 +149,19 @@ constexpr int kTcStages = 4;
 constexpr int kTcThreads = 320;
 constexpr uint32_t kTcKvTile = 128 * 256;   // 128 keys x 128 dims BF16 (two 16 KB halves)
 constexpr uint32_t kTcRowTile = 64 * 256;   // 64 rows x 128 dims BF16 (two 8 KB halves)
+constexpr uint32_t kTcRecBytes = kTcRows * 16;
 
 struct TcSmem {
   static constexpr uint32_t k = 0;
   static constexpr uint32_t v = k + kTcKvTile;
-  static constexpr uint32_t stage = v + kTcKvTile;                   // kTcStages x (Q, dO)
-  static constexpr uint32_t info = stage + kTcStages * 2 * kTcRowTile;
-  static constexpr uint32_t info_bytes = 5 * kTcRows * 4;
-  static constexpr uint32_t bars = info + kTcStages * info_bytes;   // kv, full[4], empty[4], s_full[2], p_full[2], done
-  static constexpr uint32_t misc = bars + 16 * 8;                    // tmem holder, abort flag, slot ranges
+  static constexpr uint32_t stage = v + kTcKvTile;                        // kTcStages x (Q, dO, records)
+  static constexpr uint32_t stage_bytes = 2 * kTcRowTile + kTcRecBytes;   // 33 KB (1024-byte multiple)
+  static constexpr uint32_t bars = stage + kTcStages * stage_bytes;      // kv, full[4], empty[4], s_full[2], p_full[2], done
+  static constexpr uint32_t misc = bars + 16 * 8;                         // tmem holder, abort flag, slot ranges
   static constexpr uint32_t total = misc + 64;
 };
+static_assert(TcSmem::stage_bytes % 1024 == 0, "ring entries keep the 1024-byte alignment of the swizzled tiles");
 constexpr uint32_t kTcSmemBytes = TcSmem::total + 1024;
-
-// A bounded wait whose outcome is the same in every lane of the warp (the
-// warp-collective tcgen05 instructions after it need the whole warp).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
-}
 
 __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_constant__ BwdParams p) {
   const int k0 = blockIdx.x * kTcKeys, g = blockIdx.y, b = blockIdx.z;
@@ -179,13 +177,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   uint64_t* done = p_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + TcSmem::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::misc + 4);
-  int* ranges = reinterpret_cast<int*>(smem + TcSmem::misc + 8);  // s_lo[2], s_hi[2], blocks[2]
+  int* ranges = reinterpret_cast<int*>(smem + TcSmem::misc + 8);  // first slot [2], end slot [2] per branch
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full[s], 256);  // every elementwise thread, once its copies landed
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
@@ -195,21 +193,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
+  }
+  if (warp < 4) {
     // rows of each branch whose key range [lo, hi) meets [k0, k0 + 128): a slot range,
-    // both bounds being non-decreasing along the increasing routed positions
-    for (int branch = 0; branch < 2; ++branch) {
-      const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
-      const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
-      auto bounds = [&](int slot, int& lo, int& hi) {
-        const int pos = min(max(idx[slot], 0), p.Sq - 1);
-        bwd_row_bounds(p, branch, pos, lo, hi);
-      };
-      const int s_lo = first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return hi > k0; });
-      const int s_hi = max(s_lo, first_slot(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return lo >= k0 + kTcKeys; }));
-      ranges[branch] = s_lo;
-      ranges[2 + branch] = s_hi;
-      ranges[4 + branch] = ((s_hi - s_lo) * p.r + kTcRows - 1) / kTcRows;
-    }
+    // both bounds being non-decreasing along the increasing routed positions.
+    // Warp w finds bound w & 1 of branch w >> 1.
+    __syncwarp();
+    const int branch = warp >> 1;
+    const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
+    const int32_t* idx = p.idx[branch] + static_cast<int64_t>(b) * p.idx_stride[branch];
+    auto bounds = [&](int slot, int& lo, int& hi) {
+      const int pos = min(max(idx[min(slot, cnt - 1)], 0), p.Sq - 1);
+      bwd_row_bounds(p, branch, pos, lo, hi);
+    };
+    const int found = (warp & 1) == 0
+        ? first_slot_warp(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return hi > k0; })
+        : first_slot_warp(cnt, [&](int s) { int lo, hi; bounds(s, lo, hi); return lo >= k0 + kTcKeys; });
+    if (lane == 0) ranges[2 * (warp & 1) + branch] = found;
   }
   if (warp == 0) {
     __syncwarp();  // tcgen05.alloc is warp-collective: lane 0 comes from the set-up above
@@ -220,61 +220,66 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int nblocks = ranges[4] + ranges[5];
+  // slot ranges, re-read from shared memory where needed (registers are scarce)
+  auto branch_blocks = [&](int br) {
+    return ((max(ranges[br], ranges[2 + br]) - ranges[br]) * p.r + kTcRows - 1) / kTcRows;
+  };
+  const int nblocks = branch_blocks(0) + branch_blocks(1);
   const uint32_t tm_dv = tmem + 256, tm_dk = tmem + 384;
   auto tm_st = [&](int t) { return tmem + 64 * (t & 1); };
   auto tm_dpt = [&](int t) { return tmem + 128 + 64 * (t & 1); };
-
-  // Row blocks (rows of branch 0, then of branch 1) go through a 4-entry ring,
-  // filled by the 256 elementwise threads: threads 4 j .. 4 j + 3 take row j of a
-  // block (its position, bounds, LSE and D, and 4 of its 16 chunks of Q and dO
-  // each); every thread arrives on full[entry] once its copies landed.  No
-  // barrier among the threads, so a thread that left on a timed-out wait cannot
-  // hold the others.
-  const int et = threadIdx.x - 64;  // 0..255 among the elementwise threads
-  auto block_row = [&](int it) -> RowReg {
-    const int branch = it < ranges[4] ? 0 : 1;
-    const int t = branch ? it - ranges[4] : it;
-    const int R0 = ranges[branch] * p.r + t * kTcRows;
-    return load_row(p, branch, b, g, ranges[2 + branch], R0 + (et >> 2));
-  };
-  auto issue_block = [&](int it, const RowReg& x) {
-    const int branch = it < ranges[4] ? 0 : 1;
-    const int t = branch ? it - ranges[4] : it;
-    const int R0 = ranges[branch] * p.r + t * kTcRows;
-    const int s = it % kTcStages;
-    const int rr = et >> 2, c0 = (et & 3) * 4;
-    if (c0 == 0) row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows).put(rr, x);
-    const bool ok = x.pos >= 0;
-    const int64_t row = ok ? (static_cast<int64_t>(b) * p.Sq + x.pos) * p.Hq + g * p.r + (R0 + rr) % p.r : 0;
-    uint8_t* sq = smem + TcSmem::stage + s * 2 * kTcRowTile;
-    uint8_t* sdo = sq + kTcRowTile;
-#pragma unroll
-    for (int c = c0; c < c0 + 4; ++c) {
-      cp_async_16(smem_u32(sq + swz(kTcRows, rr, c)), p.q + row * 128 + 8 * c, ok);
-      cp_async_16(smem_u32(sdo + swz(kTcRows, rr, c)), p.dout + row * 128 + 8 * c, ok);
-    }
-  };
-  auto land_block = [&](int it) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    fence_proxy_async_smem();
-    mbar_arrive(&full[it % kTcStages]);
+  // block it: rows [R0, R0 + 64) of its branch, the first `valid` of them in the slot range
+  auto block_rows = [&](int it, int& branch, int& R0, int& valid) {
+    const int nb0 = branch_blocks(0);
+    branch = it < nb0 ? 0 : 1;
+    const int t = branch ? it - nb0 : it;
+    const int s_lo = ranges[branch];
+    R0 = s_lo * p.r + t * kTcRows;
+    valid = min(kTcRows, max(s_lo, ranges[2 + branch]) * p.r - R0);
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ K / V tiles
-    for (int i = lane; i < kTcKeys * 16; i += 32) {
-      const int kr = i >> 4, c = i & 15;
-      const int key = k0 + kr;
-      const bool ok = key < p.Skv;
-      const int64_t row = ok ? (static_cast<int64_t>(b) * p.Skv + key) * p.Hkv + g : 0;
-      cp_async_16(smem_u32(smem + TcSmem::k + swz(kTcKeys, kr, c)), p.k + row * 128 + 8 * c, ok);
-      cp_async_16(smem_u32(smem + TcSmem::v + swz(kTcKeys, kr, c)), p.v + row * 128 + 8 * c, ok);
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && nblocks > 0) {
+      tma_prefetch_desc(&p.k_map);
+      tma_prefetch_desc(&p.v_map);
+      tma_prefetch_desc(&p.qp_map);
+      tma_prefetch_desc(&p.dop_map);
+      tma_prefetch_desc(&p.rec_map);
+      // the K and V tiles: per 64-dim half, keys k0 .. k0 + 63 and k0 + 64 .. k0 + 127
+      // (zeros past Skv)
+      mbar_arrive_expect_tx(kv_full, 2 * kTcKvTile);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint32_t off = h * (kTcKvTile / 2) + kk * (kTcKvTile / 4);
+          tma_load_4d(smem + TcSmem::k + off, &p.k_map, kv_full, 64 * h, g, k0 + 64 * kk, b);
+          tma_load_4d(smem + TcSmem::v + off, &p.v_map, kv_full, 64 * h, g, k0 + 64 * kk, b);
+        }
+      }
+      int it = 0;
+      for (; it < nblocks; ++it) {
+        const int s = it % kTcStages;
+        if (!mbar_wait(&empty[s], ((it / kTcStages) & 1) ^ 1, abort_flag)) break;
+        int branch, R0, valid;
+        block_rows(it, branch, R0, valid);
+        const int pr0 = static_cast<int>(packed_base(p, branch, b, g) + R0);
+        uint8_t* st = smem + TcSmem::stage + s * TcSmem::stage_bytes;
+        mbar_arrive_expect_tx(&full[s], TcSmem::stage_bytes);
+        tma_load_2d(st, &p.qp_map, &full[s], 0, pr0);
+        tma_load_2d(st + kTcRowTile / 2, &p.qp_map, &full[s], 64, pr0);
+        tma_load_2d(st + kTcRowTile, &p.dop_map, &full[s], 0, pr0);
+        tma_load_2d(st + kTcRowTile + kTcRowTile / 2, &p.dop_map, &full[s], 64, pr0);
+        tma_load_2d(st + 2 * kTcRowTile, &p.rec_map, &full[s], 0, pr0);
+      }
+      if (*abort_flag) {
+        // let the loads already issued land before the CTA's shared memory is released
+        volatile int dummy = 0;
+        mbar_wait(kv_full, 0, &dummy);
+        for (int u = max(0, it - kTcStages); u < it; ++u) mbar_wait(&full[u % kTcStages], (u / kTcStages) & 1, &dummy);
+      }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(kv_full);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 64, false, false);
@@ -283,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     const uint64_t v_desc = make_smem_desc_sw128(smem_u32(smem + TcSmem::v), 16, 1024);
     auto products = [&](int t) {  // dV += P^T dO, dK += dS^T Q of block t
       const int s = t % kTcStages;
-      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcRowTile), doa = qa + kTcRowTile;
+      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * TcSmem::stage_bytes), doa = qa + kTcRowTile;
       const uint64_t do_mn = make_smem_desc_sw128(doa, kTcRowTile / 2, 1024);
       const uint64_t q_mn = make_smem_desc_sw128(qa, kTcRowTile / 2, 1024);
 #pragma unroll
@@ -300,7 +305,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       if (!warp_wait(&full[s], (it / kTcStages) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       // TMEM buffer it & 1 was last read by the products of block it - 2, issued earlier
-      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * 2 * kTcRowTile), doa = qa + kTcRowTile;
+      const uint32_t qa = smem_u32(smem + TcSmem::stage + s * TcSmem::stage_bytes), doa = qa + kTcRowTile;
       umma_ss_k128_bhalf8k_warp(tm_st(it), k_desc, make_smem_desc_sw128(qa, 16, 1024), idesc_s);
       umma_ss_k128_bhalf8k_warp(tm_dpt(it), v_desc, make_smem_desc_sw128(doa, 16, 1024), idesc_s);
       tc_commit_warp(&s_full[it & 1]);
@@ -327,57 +332,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int it = 0; it < nblocks && it < kTcStages; ++it) issue_block(it, block_row(it));
-    for (int it = 0; it < nblocks && it < kTcStages; ++it) land_block(it);  // (one wait covers all)
-    RowReg xn{};
     for (int it = 0; it < nblocks; ++it) {
       const int s = it % kTcStages, tb = it & 1;
-      const int refill = it - 1 + kTcStages;  // block for the entry block it - 1 frees
-      if (it >= 1 && refill < nblocks) xn = block_row(refill);  // loads in flight during this block
+      int branch, R0, valid;
+      block_rows(it, branch, R0, valid);
       if (!warp_wait(&s_full[tb], (it >> 1) & 1, abort_flag)) { ok = false; break; }
-      // (already complete: acquires the row data the other threads wrote)
+      // (already complete: makes the records the TMA wrote visible to this thread)
       if (!warp_wait(&full[s], (it / kTcStages) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const RowInfo ri = row_info_at(smem + TcSmem::info + s * TcSmem::info_bytes, kTcRows);
-      {
-        uint32_t sr[32], dr[32];
-        tmem_ld_x32(tm_st(it) + lane_off + 32 * half, sr);
-        tmem_ld_x32(tm_dpt(it) + lane_off + 32 * half, dr);
-        tmem_ld_wait();
-        reg_fence32(sr);
-        reg_fence32(dr);
-        uint32_t pk[16], dk2[16];
+      const int4* rec = reinterpret_cast<const int4*>(smem + TcSmem::stage + s * TcSmem::stage_bytes + 2 * kTcRowTile);
+      uint32_t sr[32], dr[32];
+      tmem_ld_x32(tm_st(it) + lane_off + 32 * half, sr);
+      tmem_ld_x32(tm_dpt(it) + lane_off + 32 * half, dr);
+      tmem_ld_wait();
+      reg_fence32(sr);
+      reg_fence32(dr);
+      uint32_t pk[16], dk2[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float pv[2], dsv[2];
+      for (int j = 0; j < 16; ++j) {
+        // four chunks of 8 rows: keeps the compiler from holding all 32 records
+        // (128 registers) at once
+        if ((j & 3) == 0) asm volatile("" ::: "memory");
+        float pv[2], dsv[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int rr = 32 * half + 2 * j + e;  // row of the block
-            const bool legal = key >= ri.lo[rr] && key < ri.hi[rr];
-            pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ri.lse[rr]) : 0.0f;
-            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ri.d[rr]);
-          }
-          pk[j] = pack_bf16x2(pv[0], pv[1]);
-          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
+        for (int e = 0; e < 2; ++e) {
+          const int rr = 32 * half + 2 * j + e;  // row of the block
+          const int4 rc = rec[rr];               // {lo, hi, LSE, D}
+          const bool legal = rr < valid && key >= rc.x && key < rc.y;
+          pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - __int_as_float(rc.z)) : 0.0f;
+          dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - __int_as_float(rc.w));
         }
-        // over this thread's own, already read columns: 32 half .. 32 half + 15
-        tmem_st_x16(tm_st(it) + lane_off + 32 * half, pk);
-        tmem_st_x16(tm_dpt(it) + lane_off + 32 * half, dk2);
+        pk[j] = pack_bf16x2(pv[0], pv[1]);
+        dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
       }
+      // over this thread's own, already read columns: 32 half .. 32 half + 15
+      tmem_st_x16(tm_st(it) + lane_off + 32 * half, pk);
+      tmem_st_x16(tm_dpt(it) + lane_off + 32 * half, dk2);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[tb]);
-      if (it >= 1) {
-        // the block issued one iteration ago lands now; then the entry that block
-        // it - 1 used is refilled (its products were issued before this block's end)
-        if (it - 2 + kTcStages < nblocks && it >= 2) land_block(it - 2 + kTcStages);
-        if (refill < nblocks) {
-          if (!warp_wait(&empty[(it - 1) % kTcStages], ((it - 1) / kTcStages) & 1, abort_flag)) { ok = false; break; }
-          issue_block(refill, xn);
-        }
-      }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");  // (after an abort: copies still in flight)
     // epilogue: dK (scaled) and dV of this thread's key, dims 64 half .. 64 half + 63.
     // tcgen05.ld is warp-collective: every lane loads (the condition is warp
     // uniform), only the stores of keys past Skv are skipped.
@@ -420,7 +414,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     volatile int dummy = 0;
     mbar_wait(done, 0, &dummy);
   }
-  if (warp == 0) asm volatile("cp.async.wait_all;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -515,22 +508,33 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
   const int quarter = warp & 3;
   const int half = (warp - 2) >> 2;
   const int row = 32 * quarter + lane;
-  RowReg x{-1, 0, 0, 0.0f, 0.0f};
+  int pos = -1, klo = 0, khi = 0;
+  float lse = 0.0f, dsum = 0.0f;
   uint4 qv[8], dv[8];
   if (warp >= 2) {
-    x = load_row(p, branch, b, g, cnt, R0 + row);
-    if (half == 0 && x.hi > x.lo) {
-      atomicMin(&range[0], x.lo);
-      atomicMax(&range[1], x.hi);
+    // rows past the routed count are absent (and may lie past this (b, g)'s packed rows)
+    const bool present = R0 + row < cnt * p.r;
+    const int64_t pr = packed_base(p, branch, b, g) + (present ? R0 + row : 0);
+    int4 rec = make_int4(0, 0, 0, 0);
+    if (present) {
+      rec = p.rec[pr];
+      pos = p.rpos[pr];
+    }
+    klo = rec.x;
+    khi = rec.y;
+    lse = __int_as_float(rec.z);
+    dsum = __int_as_float(rec.w);
+    if (half == 0 && khi > klo) {
+      atomicMin(&range[0], klo);
+      atomicMax(&range[1], khi);
     }
     // this thread's 64 dims of the row's Q and dO (in flight across the barrier)
-    const int64_t grow = (static_cast<int64_t>(b) * p.Sq + max(x.pos, 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
-    const uint4* qs = reinterpret_cast<const uint4*>(p.q + grow * 128 + 64 * half);
-    const uint4* ds = reinterpret_cast<const uint4*>(p.dout + grow * 128 + 64 * half);
+    const uint4* qs = reinterpret_cast<const uint4*>(p.qp + pr * 128 + 64 * half);
+    const uint4* ds = reinterpret_cast<const uint4*>(p.dop + pr * 128 + 64 * half);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      qv[j] = x.pos >= 0 ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
-      dv[j] = x.pos >= 0 ? __ldg(ds + j) : make_uint4(0, 0, 0, 0);
+      qv[j] = present ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
+      dv[j] = present ? __ldg(ds + j) : make_uint4(0, 0, 0, 0);
     }
   }
   if (warp == 0) {
@@ -652,7 +656,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
       reg_fence32(dr);
       // legal keys of the row among this thread's 32: i in [i_lo, i_hi)
       const int key0 = kfirst + kDqKeys * t + 32 * half;
-      const int i_lo = x.lo - key0, i_hi = x.hi - key0;
+      const int i_lo = klo - key0, i_hi = khi - key0;
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -661,8 +665,8 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
         for (int e = 0; e < 2; ++e) {
           const int i = 2 * j + e;
           const bool legal = i >= i_lo && i < i_hi;
-          const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - x.lse) : 0.0f;
-          dsv[e] = pv * (__uint_as_float(dr[i]) - x.d);
+          const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) : 0.0f;
+          dsv[e] = pv * (__uint_as_float(dr[i]) - dsum);
         }
         pk[j] = pack_bf16x2(dsv[0], dsv[1]);
       }
@@ -677,8 +681,8 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
     // uniform), only the stores of absent rows are skipped.
     if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
     tc_fence_after();
-    const bool store = x.pos >= 0;
-    const int64_t grow = (static_cast<int64_t>(b) * p.Sq + (store ? x.pos : 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
+    const bool store = pos >= 0;
+    const int64_t grow = (static_cast<int64_t>(b) * p.Sq + (store ? pos : 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
     __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half;
     const float sc = p.scale;
 #pragma unroll
@@ -721,6 +725,35 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
 
 }  // namespace
 
+namespace {
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+size_t packed_rows(int B, int Hq, int full_stride, int local_stride) {
+  const size_t rows = static_cast<size_t>(B) * Hq * (static_cast<size_t>(full_stride) + local_stride);
+  return rows > 0 ? rows : 1;
+}
+}  // namespace
+
+size_t backward_workspace_bytes(int B, int Hq, int full_stride, int local_stride) {
+  const size_t rows = packed_rows(B, Hq, full_stride, local_stride);
+  return 256 + align256(rows * 16) + align256(rows * 4) + 2 * align256(rows * 256);
+}
+
+void bind_backward_workspace(BwdParams& p, void* workspace) {
+  const size_t rows = packed_rows(p.B, p.Hq, p.idx_stride[0], p.idx_stride[1]);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  p.status = reinterpret_cast<int32_t*>(w);
+  w += 256;
+  p.rec = reinterpret_cast<int4*>(w);
+  w += align256(rows * 16);
+  p.rpos = reinterpret_cast<int32_t*>(w);
+  w += align256(rows * 4);
+  p.qp = reinterpret_cast<__nv_bfloat16*>(w);
+  w += align256(rows * 256);
+  p.dop = reinterpret_cast<__nv_bfloat16*>(w);
+  p.pk_n0 = static_cast<int64_t>(p.B) * p.Hq * p.idx_stride[0];
+  p.pk_rows = p.pk_n0 + static_cast<int64_t>(p.B) * p.Hq * p.idx_stride[1];
+}
+
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
@@ -732,10 +765,11 @@ cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t s
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int64_t rows = static_cast<int64_t>(params.B) * params.Sq * params.Hq;
-  const int64_t want = (rows + 7) / 8;
-  const int dsum_blocks = static_cast<int>(want < 16LL * num_sms ? want : 16LL * num_sms);
-  bwd_dsum_kernel<<<dsum_blocks, 256, 0, stream>>>(params);
+  if (params.pk_rows > 0) {
+    const int64_t want = (params.pk_rows + 7) / 8;
+    const int pack_blocks = static_cast<int>(want < 16LL * num_sms ? want : 16LL * num_sms);
+    bwd_pack_kernel<<<pack_blocks, 256, 0, stream>>>(params);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const dim3 gq(params.nblk[0] + params.nblk[1], params.Hkv, params.B);

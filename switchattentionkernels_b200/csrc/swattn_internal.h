@@ -75,23 +75,45 @@ struct __align__(64) DecodeParams {
 cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream);
 
 // Prefill backward: dQ, dK, dV of both branches.
+//
+// Packed rows: the routed rows of (branch, b, g) in packed order (row R = slot
+// R / r of the branch's list, query head g r + R % r), R < idx_stride[branch] * r,
+// branch 0's regions first: packed index = (branch ? pk_n0 : 0)
+// + (b * Hkv + g) * idx_stride[branch] * r + R.  The pack pass writes, per packed
+// row, Q and dO (BF16, 128 dims; zeros for absent rows), the record {lo, hi,
+// LSE bits, D bits} (legal key range, empty when the row is absent or has no
+// legal key; D = rowsum(dO * O)) and the position (-1 when absent).
 struct __align__(64) BwdParams {
-  CUtensorMap k_map;         // 4-D {128, Hkv, Skv, B}, box {64, 1, 64, 1}, 128B swizzle (dQ pass)
+  CUtensorMap k_map;         // 4-D {128, Hkv, Skv, B}, box {64, 1, 64, 1}, 128B swizzle
   CUtensorMap v_map;
+  CUtensorMap qp_map;        // 2-D {128, packed rows}, box {64, 64}, 128B swizzle
+  CUtensorMap dop_map;
+  CUtensorMap rec_map;       // 2-D int32 {4, packed rows}, box {4, 64}, no swizzle
   const __nv_bfloat16 *q, *k, *v, *o, *dout;
   const float* lse;          // [B, Sq, Hq] forward LSE (log2 units)
-  float* dsum;               // [B, Sq, Hq] rowsum(dO * O) (workspace)
   const int32_t* idx[2];     // [B, stride] routed positions of each branch, -1 padded
   int idx_stride[2];
   const int32_t* counts;     // [B, 2] (n_full, n_local)
   const int32_t* starts[2];  // metadata (nullable)
   const int32_t* ends;
   __nv_bfloat16 *dq, *dk, *dv;
+  // workspace: packed rows
+  int4* rec;
+  int32_t* rpos;
+  __nv_bfloat16 *qp, *dop;
+  int64_t pk_n0;             // packed rows of branch 0
+  int64_t pk_rows;           // packed rows of both branches
   int B, Sq, Skv, Hq, Hkv, r, window;
   float scale_log2, scale;   // softmax scale in log2 units and in natural units
   int nblk[2];               // dQ pass: 128-row blocks of each branch per (batch, KV group)
   int32_t* status;           // kStatusTimeout when a bounded wait gave up
 };
+// Workspace bytes of the backward: status word, then the packed rows (records,
+// positions, Q, dO), each section 256-byte aligned.
+size_t backward_workspace_bytes(int B, int Hq, int full_stride, int local_stride);
+// Points the packed-row fields and the status word of `p` (B, Hq, idx_stride
+// set) into a workspace of backward_workspace_bytes().
+void bind_backward_workspace(BwdParams& p, void* workspace);
 cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t stream);
 uint32_t decode_smem_bytes();
 

@@ -48,4 +48,20 @@ inline bool make_bf16_map_sw128(CUtensorMap* map, const void* base, int rank, co
   return r == CUDA_SUCCESS;
 }
 
+// 2-D int32 tensor map without swizzle (rows of dims[0] elements, row stride
+// `row_bytes`), e.g. 16-byte records copied into shared memory as they lie.
+inline bool make_i32_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes,
+                            uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (fn == nullptr) return false;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {row_bytes};
+  cuuint32_t bdim[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<void*>(base), gdim, gstride, bdim, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace swa
