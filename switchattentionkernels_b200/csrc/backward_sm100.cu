@@ -10,7 +10,7 @@
 // g) is routed slot R / r of the branch's list and query head g r + R % r, so
 // the r heads that share K/V sit in one matrix dimension and dK / dV sum over
 // them inside the matrix products.
-//   bwd_pack_kernel  : one warp per packed row: Q and dO copied into packed
+//   bwd_pack_kernel  : half a warp per packed row: Q and dO copied into packed
 //                      order, the row's record {lo, hi, LSE, D} and position,
 //                      so both passes read contiguous rows without index chains.
 //   bwd_dq_tc_kernel : one CTA per 128 packed rows; loops over the 64-key tiles
@@ -50,17 +50,20 @@ __device__ __forceinline__ int64_t packed_base(const BwdParams& p, int branch, i
   return (branch ? p.pk_n0 : 0) + (static_cast<int64_t>(b) * p.Hkv + g) * p.idx_stride[branch] * p.r;
 }
 
+// Half a warp per packed row (16 bytes per lane); 32-bit index arithmetic (the
+// host bounds the packed rows below 2^31).
 __global__ void __launch_bounds__(256) bwd_pack_kernel(const __grid_constant__ BwdParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t pr = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; pr < p.pk_rows;
-       pr += warps) {
-    const int branch = pr < p.pk_n0 ? 0 : 1;
-    const int64_t local = branch ? pr - p.pk_n0 : pr;
-    const int64_t per = static_cast<int64_t>(p.idx_stride[branch]) * p.r;
-    const int64_t bg = local / per;
-    const int R = static_cast<int>(local - bg * per);
-    const int g = static_cast<int>(bg % p.Hkv), b = static_cast<int>(bg / p.Hkv);
+  const int hl = threadIdx.x & 15;
+  const uint32_t hmask = 0xffffu << (threadIdx.x & 16);
+  const int n0 = static_cast<int>(p.pk_n0), nrows = static_cast<int>(p.pk_rows);
+  const int stride = gridDim.x * (blockDim.x >> 4);
+  for (int pr = (blockIdx.x * blockDim.x + threadIdx.x) >> 4; pr < nrows; pr += stride) {
+    const int branch = pr < n0 ? 0 : 1;
+    const int local = branch ? pr - n0 : pr;
+    const int per = p.idx_stride[branch] * p.r;
+    const int bg = local / per;
+    const int R = local - bg * per;
+    const int g = bg % p.Hkv, b = bg / p.Hkv;
     const int cnt = min(p.counts[2 * b + branch], p.idx_stride[branch]);
     const int slot = R / p.r;
     int pos = -1;
@@ -68,26 +71,31 @@ __global__ void __launch_bounds__(256) bwd_pack_kernel(const __grid_constant__ B
       pos = p.idx[branch][static_cast<int64_t>(b) * p.idx_stride[branch] + slot];
       if (pos < 0 || pos >= p.Sq) pos = -1;
     }
-    uint2 qv = make_uint2(0, 0), dv = make_uint2(0, 0);
+    uint4 qv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0);
     int4 rec = make_int4(0, 0, 0, 0);
-    if (pos >= 0) {  // (warp uniform)
+    if (pos >= 0) {  // (uniform in the half-warp)
       const int64_t row = (static_cast<int64_t>(b) * p.Sq + pos) * p.Hq + g * p.r + R % p.r;
-      qv = *reinterpret_cast<const uint2*>(p.q + row * 128 + 4 * lane);
-      dv = *reinterpret_cast<const uint2*>(p.dout + row * 128 + 4 * lane);
-      const uint2 o = *reinterpret_cast<const uint2*>(p.o + row * 128 + 4 * lane);
-      const float2 a0 = bf2_to_f2(dv.x), a1 = bf2_to_f2(dv.y), o0 = bf2_to_f2(o.x), o1 = bf2_to_f2(o.y);
-      float d = a0.x * o0.x + a0.y * o0.y + a1.x * o1.x + a1.y * o1.y;
+      qv = *reinterpret_cast<const uint4*>(p.q + row * 128 + 8 * hl);
+      dv = *reinterpret_cast<const uint4*>(p.dout + row * 128 + 8 * hl);
+      const uint4 o = *reinterpret_cast<const uint4*>(p.o + row * 128 + 8 * hl);
+      float d = 0.0f;
+      const uint32_t da[4] = {dv.x, dv.y, dv.z, dv.w}, oa[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = bf2_to_f2(da[i]), c = bf2_to_f2(oa[i]);
+        d += a.x * c.x + a.y * c.y;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(hmask, d, off);
       int lo, hi;
       bwd_row_bounds(p, branch, pos, lo, hi);
       const float lse = p.lse[row];
       if (!(lse > -INFINITY)) hi = lo;  // a row without legal keys has no gradient
       rec = make_int4(lo, max(hi, lo), __float_as_int(lse), __float_as_int(d));
     }
-    *reinterpret_cast<uint2*>(p.qp + pr * 128 + 4 * lane) = qv;
-    *reinterpret_cast<uint2*>(p.dop + pr * 128 + 4 * lane) = dv;
-    if (lane == 0) {
+    *reinterpret_cast<uint4*>(p.qp + static_cast<int64_t>(pr) * 128 + 8 * hl) = qv;
+    *reinterpret_cast<uint4*>(p.dop + static_cast<int64_t>(pr) * 128 + 8 * hl) = dv;
+    if (hl == 0) {
       p.rec[pr] = rec;
       p.rpos[pr] = pos;
     }
@@ -766,8 +774,8 @@ cudaError_t launch_backward(const BwdParams& params, int num_sms, cudaStream_t s
     attr_set[dev] = true;
   }
   if (params.pk_rows > 0) {
-    const int64_t want = (params.pk_rows + 7) / 8;
-    const int pack_blocks = static_cast<int>(want < 16LL * num_sms ? want : 16LL * num_sms);
+    const int64_t want = (params.pk_rows + 15) / 16;  // 16 rows per 256-thread block
+    const int pack_blocks = static_cast<int>(want < 64LL * num_sms ? want : 64LL * num_sms);
     bwd_pack_kernel<<<pack_blocks, 256, 0, stream>>>(params);
   }
   cudaError_t e = cudaGetLastError();
