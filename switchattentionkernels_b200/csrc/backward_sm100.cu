@@ -349,6 +349,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       if (!warp_wait(&full[s], (it / kTcStages) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const int4* rec = reinterpret_cast<const int4*>(smem + TcSmem::stage + s * TcSmem::stage_bytes + 2 * kTcRowTile);
+      // every entry of the warp legal (its 32 keys inside each of its 32 rows' ranges,
+      // all rows in the block's slot range): no masking.  Lane j checks row j.
+      const int4 mine = rec[32 * half + lane];
+      const int kmin = k0 + 32 * quarter;
+      const bool all_legal =
+          __all_sync(0xffffffffu, 32 * half + lane < valid && mine.x <= kmin && mine.y >= kmin + 32);
       uint32_t sr[32], dr[32];
       tmem_ld_x32(tm_st(it) + lane_off + 32 * half, sr);
       tmem_ld_x32(tm_dpt(it) + lane_off + 32 * half, dr);
@@ -356,22 +362,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       reg_fence32(sr);
       reg_fence32(dr);
       uint32_t pk[16], dk2[16];
+      if (all_legal) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        // four chunks of 8 rows: keeps the compiler from holding all 32 records
-        // (128 registers) at once
-        if ((j & 3) == 0) asm volatile("" ::: "memory");
-        float pv[2], dsv[2];
+        for (int j = 0; j < 16; ++j) {
+          float pv[2], dsv[2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int rr = 32 * half + 2 * j + e;  // row of the block
-          const int4 rc = rec[rr];               // {lo, hi, LSE, D}
-          const bool legal = rr < valid && key >= rc.x && key < rc.y;
-          pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - __int_as_float(rc.z)) : 0.0f;
-          dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - __int_as_float(rc.w));
+          for (int e = 0; e < 2; ++e) {
+            const float2 ld = *reinterpret_cast<const float2*>(&rec[32 * half + 2 * j + e].z);  // {LSE, D}
+            pv[e] = ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ld.x);
+            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ld.y);
+          }
+          pk[j] = pack_bf16x2(pv[0], pv[1]);
+          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
-        pk[j] = pack_bf16x2(pv[0], pv[1]);
-        dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // four chunks of 8 rows: keeps the compiler from holding all 32 records
+          // (128 registers) at once
+          if ((j & 3) == 0) asm volatile("" ::: "memory");
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int rr = 32 * half + 2 * j + e;  // row of the block
+            const int4 rc = rec[rr];               // {lo, hi, LSE, D}
+            const bool legal = rr < valid && key >= rc.x && key < rc.y;
+            pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - __int_as_float(rc.z)) : 0.0f;
+            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - __int_as_float(rc.w));
+          }
+          pk[j] = pack_bf16x2(pv[0], pv[1]);
+          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
+        }
       }
       // over this thread's own, already read columns: 32 half .. 32 half + 15
       tmem_st_x16(tm_st(it) + lane_off + 32 * half, pk);
@@ -666,17 +687,30 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
       const int key0 = kfirst + kDqKeys * t + 32 * half;
       const int i_lo = klo - key0, i_hi = khi - key0;
       uint32_t pk[16];
+      if (__all_sync(0xffffffffu, i_lo <= 0 && i_hi >= 32)) {  // every entry of the warp legal
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float dsv[2];
+        for (int j = 0; j < 16; ++j) {
+          float dsv[2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int i = 2 * j + e;
-          const bool legal = i >= i_lo && i < i_hi;
-          const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) : 0.0f;
-          dsv[e] = pv * (__uint_as_float(dr[i]) - dsum);
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * j + e;
+            dsv[e] = ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) * (__uint_as_float(dr[i]) - dsum);
+          }
+          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
-        pk[j] = pack_bf16x2(dsv[0], dsv[1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * j + e;
+            const bool legal = i >= i_lo && i < i_hi;
+            const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) : 0.0f;
+            dsv[e] = pv * (__uint_as_float(dr[i]) - dsum);
+          }
+          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
+        }
       }
       // over this thread's own, already read columns: 32 half .. 32 half + 15
       tmem_st_x16(tm_dp(t) + lane_off + 32 * half, pk);
