@@ -143,10 +143,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 //              t - 1 are in TMEM, dV += P^T dO and dK += dS^T Q (TS, dO / Q
 //              MN-major), whose commit frees ring entry t - 1.  The products of
 //              block t + 1 thus run while the elementwise warps work on block t.
-//   warps 2-9  elementwise: two threads per key (TMEM lane = key), 32 rows each:
-//              P^T = 2^(S^T scale_log2 - LSE_row) on the legal entries,
-//              dS^T = P^T (dP^T - D_row), written as BF16 pairs over the thread's
-//              own, already read S^T / dP^T columns; then dK / dV.
+//   warps 2-17 elementwise, two groups of eight taking alternate blocks (group
+//              g the blocks t with t & 1 == g, i.e. TMEM buffer g), so one
+//              group's TMEM round trips and waits overlap the other's arithmetic.
+//              In a group, two threads per key (TMEM lane = key), 32 rows each, in
+//              two 16-row chunks: P^T = 2^(S^T scale_log2 - LSE_row) on the legal
+//              entries, dS^T = P^T (dP^T - D_row), written as BF16 pairs over the
+//              thread's own, already read S^T / dP^T columns.  Group 0 then
+//              writes dK, group 1 dV.
 // A block starts at a slot-range row of its branch and may run past the range's
 // end into later rows (of this or the next (b, g)): those rows are masked by
 // their index in the block, whatever their records say.
@@ -154,7 +158,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 constexpr int kTcKeys = 128;
 constexpr int kTcRows = 64;
 constexpr int kTcStages = 4;
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 576;
 constexpr uint32_t kTcKvTile = 128 * 256;   // 128 keys x 128 dims BF16 (two 16 KB halves)
 constexpr uint32_t kTcRowTile = 64 * 256;   // 64 rows x 128 dims BF16 (two 8 KB halves)
 constexpr uint32_t kTcRecBytes = kTcRows * 16;
@@ -334,13 +338,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
     tc_commit_warp(done);
   } else {
     // ------------------------------------------------------------ elementwise + epilogue
+    const int ew = warp - 2;
+    const int grp = ew >> 3;           // blocks t with (t & 1) == grp
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (ew >> 2) & 1;    // rows 32 half .. 32 half + 31 of a block
     const int key = k0 + 32 * quarter + lane;
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int it = 0; it < nblocks; ++it) {
+    for (int it = grp; it < nblocks; it += 2) {
       const int s = it % kTcStages, tb = it & 1;
       int branch, R0, valid;
       block_rows(it, branch, R0, valid);
@@ -355,85 +361,83 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
       const int kmin = k0 + 32 * quarter;
       const bool all_legal =
           __all_sync(0xffffffffu, 32 * half + lane < valid && mine.x <= kmin && mine.y >= kmin + 32);
-      uint32_t sr[32], dr[32];
-      tmem_ld_x32(tm_st(it) + lane_off + 32 * half, sr);
-      tmem_ld_x32(tm_dpt(it) + lane_off + 32 * half, dr);
-      tmem_ld_wait();
-      reg_fence32(sr);
-      reg_fence32(dr);
-      uint32_t pk[16], dk2[16];
-      if (all_legal) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float pv[2], dsv[2];
+      for (int c = 0; c < 2; ++c) {  // rows 32 half + 16 c .. + 15: read columns 16 c .., write 8 c ..
+        uint32_t sr[16], dr[16];
+        tmem_ld_x16(tm_st(it) + lane_off + 32 * half + 16 * c, sr);
+        tmem_ld_x16(tm_dpt(it) + lane_off + 32 * half + 16 * c, dr);
+        tmem_ld_wait();
+        reg_fence16(sr);
+        reg_fence16(dr);
+        uint32_t pk[8], dk2[8];
+        if (all_legal) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float2 ld = *reinterpret_cast<const float2*>(&rec[32 * half + 2 * j + e].z);  // {LSE, D}
-            pv[e] = ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ld.x);
-            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ld.y);
+          for (int j = 0; j < 8; ++j) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float2 ld = *reinterpret_cast<const float2*>(&rec[32 * half + 16 * c + 2 * j + e].z);  // {LSE, D}
+              pv[e] = ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ld.x);
+              dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ld.y);
+            }
+            pk[j] = pack_bf16x2(pv[0], pv[1]);
+            dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
           }
-          pk[j] = pack_bf16x2(pv[0], pv[1]);
-          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // four chunks of 8 rows: keeps the compiler from holding all 32 records
-          // (128 registers) at once
-          if ((j & 3) == 0) asm volatile("" ::: "memory");
-          float pv[2], dsv[2];
+          for (int j = 0; j < 8; ++j) {
+            float pv[2], dsv[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int rr = 32 * half + 2 * j + e;  // row of the block
-            const int4 rc = rec[rr];               // {lo, hi, LSE, D}
-            const bool legal = rr < valid && key >= rc.x && key < rc.y;
-            pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - __int_as_float(rc.z)) : 0.0f;
-            dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - __int_as_float(rc.w));
+            for (int e = 0; e < 2; ++e) {
+              const int rr = 32 * half + 16 * c + 2 * j + e;  // row of the block
+              const int4 rc = rec[rr];                        // {lo, hi, LSE, D}
+              const bool legal = rr < valid && key >= rc.x && key < rc.y;
+              pv[e] = legal ? ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - __int_as_float(rc.z)) : 0.0f;
+              dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - __int_as_float(rc.w));
+            }
+            pk[j] = pack_bf16x2(pv[0], pv[1]);
+            dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
           }
-          pk[j] = pack_bf16x2(pv[0], pv[1]);
-          dk2[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
+        // rows 32 half .. 32 half + 31 end up as BF16 pairs in columns 32 half .. 32 half + 15
+        // (chunk c over columns 32 half + 8 c .., all read before)
+        tmem_st_x8(tm_st(it) + lane_off + 32 * half + 8 * c, pk);
+        tmem_st_x8(tm_dpt(it) + lane_off + 32 * half + 8 * c, dk2);
       }
-      // over this thread's own, already read columns: 32 half .. 32 half + 15
-      tmem_st_x16(tm_st(it) + lane_off + 32 * half, pk);
-      tmem_st_x16(tm_dpt(it) + lane_off + 32 * half, dk2);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[tb]);
     }
-    // epilogue: dK (scaled) and dV of this thread's key, dims 64 half .. 64 half + 63.
-    // tcgen05.ld is warp-collective: every lane loads (the condition is warp
-    // uniform), only the stores of keys past Skv are skipped.
+    // epilogue: group 0 dK (scaled), group 1 dV, of this thread's key, dims 64 half ..
+    // 64 half + 63.  tcgen05.ld is warp-collective: every lane loads (the condition is
+    // warp uniform), only the stores of keys past Skv are skipped.
     if (ok && nblocks > 0) ok = warp_wait(done, 0, abort_flag);
     tc_fence_after();
     const bool store = key < p.Skv;
     const int64_t row = (static_cast<int64_t>(b) * p.Skv + (store ? key : 0)) * p.Hkv + g;
+    __nv_bfloat16* dst = (grp == 0 ? p.dk : p.dv) + row * 128 + 64 * half;
+    const float sc = grp == 0 ? p.scale : 1.0f;
+    const uint32_t src = (grp == 0 ? tm_dk : tm_dv) + lane_off + 64 * half;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      __nv_bfloat16* dst = (t == 0 ? p.dk : p.dv) + row * 128 + 64 * half;
-      const float sc = t == 0 ? p.scale : 1.0f;
-      const uint32_t src = (t == 0 ? tm_dk : tm_dv) + lane_off + 64 * half;
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t r[32];
+      if (nblocks > 0 && ok) {
+        tmem_ld_x32(src + 32 * cc, r);
+        tmem_ld_wait();
+        reg_fence32(r);
+      } else {
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        if (nblocks > 0 && ok) {
-          tmem_ld_x32(src + 32 * cc, r);
-          tmem_ld_wait();
-          reg_fence32(r);
-        } else {
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (store) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
-        }
-        if (store) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
-            w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
-            w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
-            w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
-            *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
-          }
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
+          w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
+          w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
+          w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
+          *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
         }
       }
     }
@@ -465,18 +469,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
 //              once dS of tile t - 1 is in TMEM, dQ += dS K (TS, K MN-major),
 //              whose commit frees ring entry t - 1.  The products of tile t + 1
 //              thus run while the elementwise warps work on tile t.
-//   warps 2-9  two threads per row (TMEM lane = row; the two 64-dim halves of
-//              Q / dO, the two 32-key halves of a tile): first the row's Q and dO
-//              into TMEM; per tile P = 2^(S scale_log2 - LSE) on the row's legal
-//              keys and dS = P (dP - D), written as BF16 pairs over the thread's
-//              own, already read dP columns; finally dQ (scaled) of the row.
+//   warps 2-17 elementwise, two groups of eight taking alternate tiles (group g
+//              the tiles t with t & 1 == g, i.e. TMEM buffer g), so one group's
+//              TMEM round trips and waits overlap the other's arithmetic.  In a
+//              group, two threads per row (TMEM lane = row; a 64-dim half of Q or
+//              dO, a 32-key half of a tile, in two 16-key chunks): first group 0
+//              puts the rows' Q and group 1 their dO into TMEM; per tile
+//              P = 2^(S scale_log2 - LSE) on the row's legal keys and
+//              dS = P (dP - D), written as BF16 pairs over the thread's own,
+//              already read dP columns; finally 32 dims of dQ (scaled) each.
 // TMEM: Q | dO (64 columns each, BF16 pairs) | S[2] | dP[2] (64 each) | dQ (128).
 // Full-branch blocks run latest rows first: their key ranges, and so their
 // run times, grow with the position.
 constexpr int kDqRows = 128;
 constexpr int kDqKeys = 64;
 constexpr int kDqStages = 6;
-constexpr int kDqThreads = 320;
+constexpr int kDqThreads = 576;
 constexpr uint32_t kDqKeyTile = kDqKeys * 256;  // 64 keys x 128 dims BF16 (two 8 KB halves)
 
 struct DqTcSmem {
@@ -516,7 +524,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(rows_full, 256);
+    mbar_init(rows_full, 512);
     for (int s = 0; s < kDqStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -533,13 +541,15 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
   }
   __syncthreads();
 
-  // elementwise threads: row 32 quarter + lane of the block, dims / keys half
+  // elementwise threads: group, row 32 quarter + lane of the block, dims / keys half
+  const int ew = warp - 2;
+  const int grp = ew >> 3;
   const int quarter = warp & 3;
-  const int half = (warp - 2) >> 2;
+  const int half = (ew >> 2) & 1;
   const int row = 32 * quarter + lane;
   int pos = -1, klo = 0, khi = 0;
   float lse = 0.0f, dsum = 0.0f;
-  uint4 qv[8], dv[8];
+  uint4 qv[8];
   if (warp >= 2) {
     // rows past the routed count are absent (and may lie past this (b, g)'s packed rows)
     const bool present = R0 + row < cnt * p.r;
@@ -553,18 +563,15 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
     khi = rec.y;
     lse = __int_as_float(rec.z);
     dsum = __int_as_float(rec.w);
-    if (half == 0 && khi > klo) {
+    if (grp == 0 && half == 0 && khi > klo) {
       atomicMin(&range[0], klo);
       atomicMax(&range[1], khi);
     }
-    // this thread's 64 dims of the row's Q and dO (in flight across the barrier)
-    const uint4* qs = reinterpret_cast<const uint4*>(p.qp + pr * 128 + 64 * half);
-    const uint4* ds = reinterpret_cast<const uint4*>(p.dop + pr * 128 + 64 * half);
+    // this thread's 64 dims of the row's Q (group 0) or dO (group 1), in flight
+    // across the barrier
+    const uint4* qs = reinterpret_cast<const uint4*>((grp == 0 ? p.qp : p.dop) + pr * 128 + 64 * half);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      qv[j] = present ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
-      dv[j] = present ? __ldg(ds + j) : make_uint4(0, 0, 0, 0);
-    }
+    for (int j = 0; j < 8; ++j) qv[j] = present ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
   }
   if (warp == 0) {
     __syncwarp();  // tcgen05.alloc is warp-collective: lane 0 comes from the set-up above
@@ -658,96 +665,89 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
         r[4 * j + 2] = qv[j].z;
         r[4 * j + 3] = qv[j].w;
       }
-      tmem_st_x32(tm_q + lane_off + 32 * half, r);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        r[4 * j] = dv[j].x;
-        r[4 * j + 1] = dv[j].y;
-        r[4 * j + 2] = dv[j].z;
-        r[4 * j + 3] = dv[j].w;
-      }
-      tmem_st_x32(tm_do + lane_off + 32 * half, r);
+      tmem_st_x32((grp == 0 ? tm_q : tm_do) + lane_off + 32 * half, r);
       tmem_st_wait();
     }
     tc_fence_before();
     mbar_arrive(rows_full);
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int t = 0; t < ntiles; ++t) {
+    for (int t = grp; t < ntiles; t += 2) {
       const int tb = t & 1;
       if (!warp_wait(&s_full[tb], (t >> 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[32], dr[32];
-      tmem_ld_x32(tm_s(t) + lane_off + 32 * half, sr);
-      tmem_ld_x32(tm_dp(t) + lane_off + 32 * half, dr);
-      tmem_ld_wait();
-      reg_fence32(sr);
-      reg_fence32(dr);
       // legal keys of the row among this thread's 32: i in [i_lo, i_hi)
       const int key0 = kfirst + kDqKeys * t + 32 * half;
       const int i_lo = klo - key0, i_hi = khi - key0;
-      uint32_t pk[16];
-      if (__all_sync(0xffffffffu, i_lo <= 0 && i_hi >= 32)) {  // every entry of the warp legal
+      const bool all_legal = __all_sync(0xffffffffu, i_lo <= 0 && i_hi >= 32);  // every entry of the warp
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float dsv[2];
+      for (int c = 0; c < 2; ++c) {  // keys 32 half + 16 c .. + 15: read columns 16 c .., write 8 c ..
+        uint32_t sr[16], dr[16];
+        tmem_ld_x16(tm_s(t) + lane_off + 32 * half + 16 * c, sr);
+        tmem_ld_x16(tm_dp(t) + lane_off + 32 * half + 16 * c, dr);
+        tmem_ld_wait();
+        reg_fence16(sr);
+        reg_fence16(dr);
+        uint32_t pk[8];
+        if (all_legal) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int i = 2 * j + e;
-            dsv[e] = ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) * (__uint_as_float(dr[i]) - dsum);
+          for (int j = 0; j < 8; ++j) {
+            float dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int i = 2 * j + e;
+              dsv[e] = ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) * (__uint_as_float(dr[i]) - dsum);
+            }
+            pk[j] = pack_bf16x2(dsv[0], dsv[1]);
           }
-          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float dsv[2];
+          for (int j = 0; j < 8; ++j) {
+            float dsv[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int i = 2 * j + e;
-            const bool legal = i >= i_lo && i < i_hi;
-            const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) : 0.0f;
-            dsv[e] = pv * (__uint_as_float(dr[i]) - dsum);
+            for (int e = 0; e < 2; ++e) {
+              const int i = 16 * c + 2 * j + e;
+              const bool legal = i >= i_lo && i < i_hi;
+              const float pv = legal ? ex2_approx(__uint_as_float(sr[i - 16 * c]) * sl2 - lse) : 0.0f;
+              dsv[e] = pv * (__uint_as_float(dr[i - 16 * c]) - dsum);
+            }
+            pk[j] = pack_bf16x2(dsv[0], dsv[1]);
           }
-          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
+        // keys 32 half .. 32 half + 31 end up as BF16 pairs in columns 32 half .. 32 half + 15
+        tmem_st_x8(tm_dp(t) + lane_off + 32 * half + 8 * c, pk);
       }
-      // over this thread's own, already read columns: 32 half .. 32 half + 15
-      tmem_st_x16(tm_dp(t) + lane_off + 32 * half, pk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[tb]);
     }
-    // epilogue: dQ (scaled) of this thread's row, dims 64 half .. 64 half + 63.
+    // epilogue: dQ (scaled) of this thread's row, dims 64 half + 32 grp .. + 31.
     // tcgen05.ld is warp-collective: every lane loads (the condition is warp
     // uniform), only the stores of absent rows are skipped.
     if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
     tc_fence_after();
     const bool store = pos >= 0;
     const int64_t grow = (static_cast<int64_t>(b) * p.Sq + (store ? pos : 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
-    __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half;
+    __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half + 32 * grp;
     const float sc = p.scale;
+    uint32_t r[32];
+    if (ntiles > 0 && ok) {
+      tmem_ld_x32(tm_dq + lane_off + 64 * half + 32 * grp, r);
+      tmem_ld_wait();
+      reg_fence32(r);
+    } else {
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      uint32_t r[32];
-      if (ntiles > 0 && ok) {
-        tmem_ld_x32(tm_dq + lane_off + 64 * half + 32 * cc, r);
-        tmem_ld_wait();
-        reg_fence32(r);
-      } else {
+      for (int j = 0; j < 32; ++j) r[j] = 0u;
+    }
+    if (store) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
-      }
-      if (store) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
-          w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
-          w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
-          w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
-          *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
-        }
+      for (int j = 0; j < 4; ++j) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
+        w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
+        w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
+        w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
+        *reinterpret_cast<uint4*>(dst + 8 * j) = w;
       }
     }
   }
