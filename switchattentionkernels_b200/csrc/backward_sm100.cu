@@ -469,22 +469,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
 //              once dS of tile t - 1 is in TMEM, dQ += dS K (TS, K MN-major),
 //              whose commit frees ring entry t - 1.  The products of tile t + 1
 //              thus run while the elementwise warps work on tile t.
-//   warps 2-17 elementwise, two groups of eight taking alternate tiles (group g
-//              the tiles t with t & 1 == g, i.e. TMEM buffer g), so one group's
-//              TMEM round trips and waits overlap the other's arithmetic.  In a
-//              group, two threads per row (TMEM lane = row; a 64-dim half of Q or
-//              dO, a 32-key half of a tile, in two 16-key chunks): first group 0
-//              puts the rows' Q and group 1 their dO into TMEM; per tile
-//              P = 2^(S scale_log2 - LSE) on the row's legal keys and
-//              dS = P (dP - D), written as BF16 pairs over the thread's own,
-//              already read dP columns; finally 32 dims of dQ (scaled) each.
+//   warps 2-9  two threads per row (TMEM lane = row; the two 64-dim halves of
+//              Q / dO, the two 32-key halves of a tile): first the row's Q and dO
+//              into TMEM; per tile P = 2^(S scale_log2 - LSE) on the row's legal
+//              keys and dS = P (dP - D), written as BF16 pairs over the thread's
+//              own, already read dP columns; finally dQ (scaled) of the row.
 // TMEM: Q | dO (64 columns each, BF16 pairs) | S[2] | dP[2] (64 each) | dQ (128).
 // Full-branch blocks run latest rows first: their key ranges, and so their
 // run times, grow with the position.
 constexpr int kDqRows = 128;
 constexpr int kDqKeys = 64;
 constexpr int kDqStages = 6;
-constexpr int kDqThreads = 576;
+constexpr int kDqThreads = 320;
 constexpr uint32_t kDqKeyTile = kDqKeys * 256;  // 64 keys x 128 dims BF16 (two 8 KB halves)
 
 struct DqTcSmem {
@@ -524,7 +520,7 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(rows_full, 512);
+    mbar_init(rows_full, 256);
     for (int s = 0; s < kDqStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -541,15 +537,13 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
   }
   __syncthreads();
 
-  // elementwise threads: group, row 32 quarter + lane of the block, dims / keys half
-  const int ew = warp - 2;
-  const int grp = ew >> 3;
+  // elementwise threads: row 32 quarter + lane of the block, dims / keys half
   const int quarter = warp & 3;
-  const int half = (ew >> 2) & 1;
+  const int half = (warp - 2) >> 2;
   const int row = 32 * quarter + lane;
   int pos = -1, klo = 0, khi = 0;
   float lse = 0.0f, dsum = 0.0f;
-  uint4 qv[8];
+  uint4 qv[8], dv[8];
   if (warp >= 2) {
     // rows past the routed count are absent (and may lie past this (b, g)'s packed rows)
     const bool present = R0 + row < cnt * p.r;
@@ -563,15 +557,18 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
     khi = rec.y;
     lse = __int_as_float(rec.z);
     dsum = __int_as_float(rec.w);
-    if (grp == 0 && half == 0 && khi > klo) {
+    if (half == 0 && khi > klo) {
       atomicMin(&range[0], klo);
       atomicMax(&range[1], khi);
     }
-    // this thread's 64 dims of the row's Q (group 0) or dO (group 1), in flight
-    // across the barrier
-    const uint4* qs = reinterpret_cast<const uint4*>((grp == 0 ? p.qp : p.dop) + pr * 128 + 64 * half);
+    // this thread's 64 dims of the row's Q and dO (in flight across the barrier)
+    const uint4* qs = reinterpret_cast<const uint4*>(p.qp + pr * 128 + 64 * half);
+    const uint4* ds = reinterpret_cast<const uint4*>(p.dop + pr * 128 + 64 * half);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) qv[j] = present ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < 8; ++j) {
+      qv[j] = present ? __ldg(qs + j) : make_uint4(0, 0, 0, 0);
+      dv[j] = present ? __ldg(ds + j) : make_uint4(0, 0, 0, 0);
+    }
   }
   if (warp == 0) {
     __syncwarp();  // tcgen05.alloc is warp-collective: lane 0 comes from the set-up above
@@ -665,89 +662,96 @@ __global__ void __launch_bounds__(kDqThreads, 1) bwd_dq_tc_kernel(const __grid_c
         r[4 * j + 2] = qv[j].z;
         r[4 * j + 3] = qv[j].w;
       }
-      tmem_st_x32((grp == 0 ? tm_q : tm_do) + lane_off + 32 * half, r);
+      tmem_st_x32(tm_q + lane_off + 32 * half, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        r[4 * j] = dv[j].x;
+        r[4 * j + 1] = dv[j].y;
+        r[4 * j + 2] = dv[j].z;
+        r[4 * j + 3] = dv[j].w;
+      }
+      tmem_st_x32(tm_do + lane_off + 32 * half, r);
       tmem_st_wait();
     }
     tc_fence_before();
     mbar_arrive(rows_full);
     const float sl2 = p.scale_log2;
     bool ok = true;
-    for (int t = grp; t < ntiles; t += 2) {
+    for (int t = 0; t < ntiles; ++t) {
       const int tb = t & 1;
       if (!warp_wait(&s_full[tb], (t >> 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
+      uint32_t sr[32], dr[32];
+      tmem_ld_x32(tm_s(t) + lane_off + 32 * half, sr);
+      tmem_ld_x32(tm_dp(t) + lane_off + 32 * half, dr);
+      tmem_ld_wait();
+      reg_fence32(sr);
+      reg_fence32(dr);
       // legal keys of the row among this thread's 32: i in [i_lo, i_hi)
       const int key0 = kfirst + kDqKeys * t + 32 * half;
       const int i_lo = klo - key0, i_hi = khi - key0;
-      const bool all_legal = __all_sync(0xffffffffu, i_lo <= 0 && i_hi >= 32);  // every entry of the warp
+      uint32_t pk[16];
+      if (__all_sync(0xffffffffu, i_lo <= 0 && i_hi >= 32)) {  // every entry of the warp legal
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // keys 32 half + 16 c .. + 15: read columns 16 c .., write 8 c ..
-        uint32_t sr[16], dr[16];
-        tmem_ld_x16(tm_s(t) + lane_off + 32 * half + 16 * c, sr);
-        tmem_ld_x16(tm_dp(t) + lane_off + 32 * half + 16 * c, dr);
-        tmem_ld_wait();
-        reg_fence16(sr);
-        reg_fence16(dr);
-        uint32_t pk[8];
-        if (all_legal) {
+        for (int j = 0; j < 16; ++j) {
+          float dsv[2];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float dsv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int i = 2 * j + e;
-              dsv[e] = ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) * (__uint_as_float(dr[i]) - dsum);
-            }
-            pk[j] = pack_bf16x2(dsv[0], dsv[1]);
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * j + e;
+            dsv[e] = ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) * (__uint_as_float(dr[i]) - dsum);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float dsv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int i = 16 * c + 2 * j + e;
-              const bool legal = i >= i_lo && i < i_hi;
-              const float pv = legal ? ex2_approx(__uint_as_float(sr[i - 16 * c]) * sl2 - lse) : 0.0f;
-              dsv[e] = pv * (__uint_as_float(dr[i - 16 * c]) - dsum);
-            }
-            pk[j] = pack_bf16x2(dsv[0], dsv[1]);
-          }
+          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
         }
-        // keys 32 half .. 32 half + 31 end up as BF16 pairs in columns 32 half .. 32 half + 15
-        tmem_st_x8(tm_dp(t) + lane_off + 32 * half + 8 * c, pk);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * j + e;
+            const bool legal = i >= i_lo && i < i_hi;
+            const float pv = legal ? ex2_approx(__uint_as_float(sr[i]) * sl2 - lse) : 0.0f;
+            dsv[e] = pv * (__uint_as_float(dr[i]) - dsum);
+          }
+          pk[j] = pack_bf16x2(dsv[0], dsv[1]);
+        }
       }
+      // over this thread's own, already read columns: 32 half .. 32 half + 15
+      tmem_st_x16(tm_dp(t) + lane_off + 32 * half, pk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[tb]);
     }
-    // epilogue: dQ (scaled) of this thread's row, dims 64 half + 32 grp .. + 31.
+    // epilogue: dQ (scaled) of this thread's row, dims 64 half .. 64 half + 63.
     // tcgen05.ld is warp-collective: every lane loads (the condition is warp
     // uniform), only the stores of absent rows are skipped.
     if (ok && ntiles > 0) ok = warp_wait(done, 0, abort_flag);
     tc_fence_after();
     const bool store = pos >= 0;
     const int64_t grow = (static_cast<int64_t>(b) * p.Sq + (store ? pos : 0)) * p.Hq + g * p.r + (R0 + row) % p.r;
-    __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half + 32 * grp;
+    __nv_bfloat16* dst = p.dq + grow * 128 + 64 * half;
     const float sc = p.scale;
-    uint32_t r[32];
-    if (ntiles > 0 && ok) {
-      tmem_ld_x32(tm_dq + lane_off + 64 * half + 32 * grp, r);
-      tmem_ld_wait();
-      reg_fence32(r);
-    } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) r[j] = 0u;
-    }
-    if (store) {
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t r[32];
+      if (ntiles > 0 && ok) {
+        tmem_ld_x32(tm_dq + lane_off + 64 * half + 32 * cc, r);
+        tmem_ld_wait();
+        reg_fence32(r);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 w;
-        w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
-        w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
-        w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
-        w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
-        *reinterpret_cast<uint4*>(dst + 8 * j) = w;
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (store) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(r[8 * j]) * sc, __uint_as_float(r[8 * j + 1]) * sc);
+          w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * sc, __uint_as_float(r[8 * j + 3]) * sc);
+          w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * sc, __uint_as_float(r[8 * j + 5]) * sc);
+          w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * sc, __uint_as_float(r[8 * j + 7]) * sc);
+          *reinterpret_cast<uint4*>(dst + 32 * cc + 8 * j) = w;
+        }
       }
     }
   }
