@@ -79,16 +79,18 @@ def gather_units(out: torch.Tensor, lse: torch.Tensor, plan: list[list[int]], *,
     n_max = max(len(p) for p in plan)
     if n_max == 0:
         return
-    stage_o = out.new_zeros((n_max, S, r, D))
-    stage_l = lse.new_zeros((n_max, S, r))
+    # staging slots past a rank's own units are sent but never read: no fill
+    stage_o = out.new_empty((n_max, S, r, D))
+    stage_l = lse.new_empty((n_max, S, r))
     for i, u in enumerate(plan[rank]):
         b, g = divmod(u, hkv)
         stage_o[i].copy_(out[b, :, g * r:(g + 1) * r, :])
         stage_l[i].copy_(lse[b, :, g * r:(g + 1) * r])
-    got_o = [torch.empty_like(stage_o) for _ in range(world)]
-    got_l = [torch.empty_like(stage_l) for _ in range(world)]
-    dist.all_gather(got_o, stage_o, group=group)
-    dist.all_gather(got_l, stage_l, group=group)
+    # one collective per tensor straight into a [world, n_max, ...] buffer
+    got_o = out.new_empty((world, n_max, S, r, D))
+    got_l = lse.new_empty((world, n_max, S, r))
+    dist.all_gather_into_tensor(got_o.view(world * n_max, S, r, D), stage_o, group=group)
+    dist.all_gather_into_tensor(got_l.view(world * n_max, S, r), stage_l, group=group)
     for p in range(world):
         if p == rank:
             continue

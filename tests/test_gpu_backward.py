@@ -92,3 +92,38 @@ def test_autograd_function(cuda_device):
     dq, dk, dv = switch_gqa_prefill_backward(q.detach(), k.detach(), v.detach(), out.detach(), lse, dout, fi, li,
                                              window_size=W)
     assert torch.equal(q.grad, dq) and torch.equal(k.grad, dk) and torch.equal(v.grad, dv)
+
+
+def test_backward_context_parallel_rows(cuda_device):
+    # one rank's rows of a zigzag split against the whole K/V axis: Sq != Skv, per-row
+    # key bounds from the metadata (the layout context_parallel.py hands the kernels)
+    from switchattentionkernels_b200 import context_parallel as cp
+
+    dev = cuda_device
+    g = torch.Generator().manual_seed(13)
+    S, Hq, Hkv, W = 900, 8, 2, 150
+    cu = np.array([0, 300, 301, 650, S])
+    q = torch.randn(1, S, Hq, 128, generator=g).bfloat16()
+    k = torch.randn(1, S, Hkv, 128, generator=g).bfloat16()
+    v = torch.randn(1, S, Hkv, 128, generator=g).bfloat16()
+    dout = torch.randn(1, S, Hq, 128, generator=g).bfloat16()
+    mask = (torch.rand(S, generator=g) < 0.4).numpy()
+    rows = cp.make_cp_plan(S, 2, cp.cp_row_costs(mask, W, cu)).rows(1)
+    idx = torch.from_numpy(rows)
+    md = cp.cp_metadata(S, rows, device=dev, window_size=W, cu_seqlens=torch.from_numpy(cu).int())
+    lmask = mask[rows]
+    full, local = np.nonzero(lmask)[0].astype(np.int32), np.nonzero(~lmask)[0].astype(np.int32)
+    fi = torch.from_numpy(full)[None].to(dev)
+    li = torch.from_numpy(local)[None].to(dev)
+    ql, dol = q[:, idx].contiguous(), dout[:, idx].contiguous()
+    qd, kd, vd, dod = (t.to(dev) for t in (ql, k, v, dol))
+    out, lse = _core.forward(qd, kd, vd, fi, li, metadata=md, window_size=W)
+    dq, dk, dv = switch_gqa_prefill_backward(qd, kd, vd, out, lse, dod, fi, li, metadata=md, window_size=W)
+    torch.cuda.synchronize()
+    full_md = oracle_md.build_metadata(S, S, W, cu)
+    md_rows = {key: (val[rows] if key in ("q_positions", "q_segment_ids", "full_starts", "local_starts",
+                                           "causal_ends") else val) for key, val in full_md.items()}
+    rq, rk, rv = oracle_attn.prefill_backward(ql, k, v, dol, [full], [local], window=W, metadata=md_rows)
+    _close(dq, rq, "context-parallel rows dq")
+    _close(dk, rk, "context-parallel rows dk")
+    _close(dv, rv, "context-parallel rows dv")

@@ -191,3 +191,15 @@ def test_config_shapes():
     assert w["mask"].shape == (1, 1024) and w["mask"].dtype == torch.bool
     lengths = workloads.varlen_lengths(c[4])
     assert lengths.size == 16 and lengths.min() >= 512 and lengths.max() <= 8192
+
+
+def test_backward_workspace_query():
+    # host arithmetic only: status word, then per (list slot, head) a 16-byte record,
+    # a 4-byte position and the 256-byte Q and dO rows, each section 256-byte aligned
+    lib = _native.load()
+    for B, Hq, fs, ls in [(1, 32, 4096, 28672), (3, 16, 7, 300), (2, 8, 0, 5), (1, 1, 1, 0)]:
+        rows = B * Hq * (fs + ls)
+        got = lib.swa_backward_workspace_bytes(B, Hq, fs, ls)
+        assert rows * 532 <= got <= rows * 532 + 256 * 6
+    assert lib.swa_backward_workspace_bytes(0, 8, 4, 4) == 0
+    assert lib.swa_backward_workspace_bytes(2, 8, -1, 4) == 0
