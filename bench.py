@@ -327,7 +327,7 @@ def run_backward(args, world, rank, local_rank):
     """Prefill backward of the config-3 workload (``--batch`` sequences per GPU).
 
     One step = dQ, dK, dV from the forward's O and LSE for a random upstream
-    gradient (rowsum pass, dQ pass, dK/dV pass).  ``value`` uses the usual
+    gradient (pack pass, dQ pass, dK/dV pass).  ``value`` uses the usual
     convention of 2.5 x the forward's effective FLOP (five matrix products of
     the forward's size, over the legal entries only).
     """
