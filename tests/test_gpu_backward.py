@@ -67,6 +67,7 @@ def _run(dev, B, S, Hq, Hkv, W, p, seed, sm_scale=None, cu=None):
 @pytest.mark.parametrize("B,S,Hq,Hkv,W,p", [
     (1, 200, 4, 2, 64, 0.3), (1, 700, 8, 2, 100, 0.5), (2, 513, 4, 1, 37, 0.2), (3, 300, 16, 4, 1000, 0.7),
     (1, 1000, 8, 8, 128, 0.0), (1, 1000, 8, 8, 128, 1.0), (2, 333, 32, 1, 50, 0.4), (1, 260, 6, 3, 1, 0.5),
+    (1, 2048, 8, 2, 1024, 0.125),  # config 3's window and routing density, many tiles per CTA
 ])
 def test_backward_matches_oracle(cuda_device, B, S, Hq, Hkv, W, p):
     _run(cuda_device, B, S, Hq, Hkv, W, p, seed=B * 131 + S + Hq + W)
