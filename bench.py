@@ -3,27 +3,35 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one pass of the hot path over one batch of the 32K-token
-mixed-routing workload (config 3: B=4, S=32768, Hq=32, Hkv=8, D=128, W=1024,
-q/k/v ~ 0.5*N(0,1) BF16, two-state Markov routing with stationary p_full=0.125):
-routing-mask compaction, index validation and the persistent prefill kernel.
-Effective work counts only legal score entries (4*D per entry and head).
+Workload: config 3, the 32K-token mixed-routing batch (B=4, S=32768, Hq=32,
+Hkv=8, D=128, W=1024, q/k/v ~ 0.5*N(0,1) BF16, two-state Markov routing with
+stationary p_full=0.125).  Effective work counts only legal score entries
+(4*D per entry and head).
 
-With N GPUs (torchrun, one process per GPU) every rank owns 4 sequences of a
-global batch of 4N (its own seeded draw) and computes all of their
-(batch, KV group) units: no data-path collective, weak scaling.
+The batch's 32 (batch, KV group) units are sharded over the N ranks
+(longest-processing-time first on their legal-entry cost; strong scaling: the
+batch is fixed as N grows).  A rank holds only its units, unit-major
+([units, S, Hq/Hkv, 128] q, [units, S, 1, 128] k / v, the units' mask rows),
+and one step is the hot path over them: routing-mask compaction and the
+persistent prefill kernel.  No collective is in the data path.
 
-``value`` is device-resident throughput (inputs in HBM, no host sync inside a
-step).  ``e2e`` is the same metric through the public API with pinned host
-buffers: every step copies mask/q/k/v host->device, runs
-build_switch_query_indices_batched + switch_gqa_prefill_forward (validating,
-as the reference does) and copies O and LSE back; consecutive steps are
+``value`` = effective FLOP of the batch / the slowest rank's device-timed step
+(inputs resident in HBM, no host sync inside a step).  ``gather`` = the same
+with every step ending in the NCCL all-gather of every rank's O and LSE and the
+scatter kernel into [B, S, Hq, ...] on every rank (a replicated result).
+``e2e`` = the same metric through the public API from pinned host buffers: every
+step copies the rank's own units (q/k/v/mask) host->device, runs
+build_switch_query_indices_batched + switch_gqa_prefill_forward (validating, as
+the reference does) and copies the rank's O and LSE back; consecutive steps are
 pipelined over a copy-in, a compute and a copy-out stream (two device input
-slots), so one step's copies overlap its neighbours' compute, as in a serving
-loop.  The timed region runs from the first copy-in to the last copy-out.
-``--impl reference`` times
-the CPU restatement of the reference path (the reference kernels are
-Hopper-only TileLang programs and cannot run on B200 or on a CPU).
+slots), as a serving loop would run them.  The copy byte counts are summed over
+the ranks.  ``steady`` repeats the device-timed step back to back for at least
+two seconds with its own clock record.  At N=1 the line also carries the same
+kernel on the row-major [B, S, Hq, 128] layout (``standard_layout``), one
+backward step (dQ, dK, dV) and one decode step.  ``--replicas`` instead gives
+every rank its own 4 sequences (weak scaling).  ``--impl reference`` times the
+CPU restatement of the reference path (the reference kernels are Hopper-only
+TileLang programs and cannot run on B200 or on a CPU).
 """
 from __future__ import annotations
 
@@ -64,10 +72,12 @@ def parse_args():
     ap.add_argument("--cp", action="store_true",
                     help="instead of the default line: context-parallel prefill over the N ranks "
                          "(strong scaling; K/V all-gather + kernel per step)")
-    ap.add_argument("--sharded", action="store_true",
-                    help="instead of the default line: config 3's batch split over the N ranks by (batch, KV group) "
-                         "units (strong scaling)")
-    ap.add_argument("--gather", action="store_true", help="with --sharded: all-gather O and LSE to every rank")
+    ap.add_argument("--replicas", action="store_true",
+                    help="instead of the default line: every rank computes its own 4 sequences (weak scaling)")
+    ap.add_argument("--steady-seconds", type=float, default=2.0,
+                    help="length of the back-to-back steady-state block after the timed steps")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the N=1 extras (standard-layout kernel, backward and decode steps)")
     ap.add_argument("--backward", action="store_true",
                     help="instead of the default line: the prefill backward (dQ, dK, dV) of the config-3 workload")
     ap.add_argument("--decode", action="store_true",
@@ -186,6 +196,16 @@ def unit_flops(mask: np.ndarray, window: int, hq: int, skv: int) -> float:
     return workloads.effective_flops(mask, window, skv, hq)
 
 
+def config3_dict(world: int) -> dict:
+    """``config`` of the default line: the same keys and values in both arms."""
+    cfg = workloads.CONFIGS[CONFIG_ID]
+    return {"workload": cfg.name, "B": cfg.B, "S": cfg.S, "Hq": cfg.Hq, "Hkv": cfg.Hkv, "head_dim": 128,
+            "window": cfg.window, "p_full": cfg.p_full, "routing": "markov(switch=0.02)",
+            "units": cfg.B * cfg.Hkv,
+            "parallelism": f"(batch, KV group) units sharded over {world} rank(s), LPT on legal entries",
+            "l2": "inputs larger than L2 (q/k/v 1.5 GiB)"}
+
+
 # --------------------------------------------------------------------------- CPU baseline (oracle)
 def cpu_oracle_sample(inputs, seconds: float, rng_seed: int = 123):
     """Time the CPU restatement on random 256-position blocks until ``seconds`` elapse."""
@@ -229,100 +249,31 @@ def run_reference(args, world, rank):
     per_step = max(1.0, 60.0 / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
         cpu_oracle_sample(inputs, per_step / 4, rng_seed=7)
-    t_flops, t_time, samples = 0.0, 0.0, []
+    samples = []
     for s in range(args.steps):
         res = cpu_oracle_sample(inputs, per_step, rng_seed=1000 + s)
         samples.append(res)
     value = statistics.fmean([r["value"] for r in samples])
-    cfg = workloads.CONFIGS[CONFIG_ID]
+    flops = workloads.effective_flops(inputs["mask"], inputs["window"], inputs["q_cpu"].shape[1],
+                                      inputs["q_cpu"].shape[2])
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1000.0, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg.name, "B": cfg.B, "S": cfg.S, "Hq": cfg.Hq, "Hkv": cfg.Hkv, "head_dim": 128,
-                   "window": cfg.window, "p_full": cfg.p_full, "routing": "markov(switch=0.02)"},
+        "steps": args.steps, "warmup": args.warmup,
+        # one whole config-3 batch at the sampled rate (each step times a bounded sample)
+        "ms_per_step": flops / (value * 1e12) * 1e3, "sample_seconds_per_step": per_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config3_dict(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port",
                          "sample": f"each step: {samples[0]['sample']}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference kernels are TileLang programs that lower only for Hopper (T.wgmma_gemm); the "
-                "reference path is timed as its CPU restatement (oracle/)",
+                "reference path is timed as its CPU restatement (oracle/) on one host, whatever N is",
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
 # --------------------------------------------------------------------------- GPU arm
-def run_sharded(args, world, rank, local_rank):
-    """Config 3's batch (B = 4, 32 (batch, KV group) units) split over ``world`` ranks.
-
-    Every rank holds the same inputs; units go to ranks longest-processing-time
-    first on their legal-entry cost (``sharded.plan_units``) and each rank runs
-    the kernel on its units only.  With ``--gather`` every step ends with the
-    NCCL all-gather of O and LSE, so every rank holds the whole result.
-    ``value`` = effective FLOP of the batch / the slowest rank's step time
-    (strong scaling).
-    """
-    import torch.distributed as dist
-    from switchattentionkernels_b200 import build_switch_query_indices_batched
-    from switchattentionkernels_b200.sharded import _host_lists, sharded_switch_gqa_prefill_forward, unit_costs
-
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    if world == 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", str(29650 + os.getpid() % 200))
-        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-    w = workloads.make_inputs(CONFIG_ID, device=dev, on_device=True)
-    cfg = w["cfg"]
-    q, k, v, mask, W = w["q"], w["k"], w["v"], w["mask"], w["window"]
-    full, local, counts = build_switch_query_indices_batched(mask.to(dev))
-    fl, ll = _host_lists(full, local, counts, q.shape[0])
-    costs = unit_costs(fl, ll, hkv=k.shape[2], skv=k.shape[1], window=W)
-    flops = workloads.effective_flops(mask.numpy(), W, q.shape[1], q.shape[2])
-
-    def step():
-        return sharded_switch_gqa_prefill_forward(q, k, v, full, local, window_size=W, query_counts=counts,
-                                                  gather=args.gather, validate=False, costs=costs)
-
-    plan = None
-    for _ in range(args.warmup):
-        _, _, plan = step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    clocks = ClockSampler(dev.index)
-    clocks.start()
-    clocks.mark("begin")
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        step()
-    t1.record()
-    torch.cuda.synchronize()
-    clocks.mark("end")
-    dist.barrier()
-    clock_info = clocks.stop()
-    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms_max = float(ms.item())
-    dist.destroy_process_group()
-    if rank == 0:
-        peak_burst, _, peak_src = measured_peaks()
-        value = flops / (ms_max * 1e-3) / 1e12
-        print(json.dumps({
-            "metric": "effective TFLOP/s, (batch, KV group) units sharded over the GPUs", "value": value,
-            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": cfg.name, "units": len(costs), "units_per_rank": [len(u) for u in plan],
-                       "gather_o_lse": bool(args.gather), "effective_tflop_per_step": flops / 1e12},
-            "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst, "peak_source": peak_src,
-            "gpu_launches": args.steps,  # the prefill kernel, once per step and rank
-            "clocks": clock_info,
-        }), flush=True)
-    return 0
-
-
 def run_backward(args, world, rank, local_rank):
     """Prefill backward of the config-3 workload (``--batch`` sequences per GPU).
 
@@ -390,6 +341,48 @@ def run_backward(args, world, rank, local_rank):
     return 0
 
 
+DECODE_B, DECODE_SMAX, DECODE_HQ, DECODE_HKV, DECODE_W, DECODE_P = 64, 32768, 32, 8, 1024, 0.125
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            hbm = float(json.load(fh).get("hbm_gbs", 0.0))
+        if hbm > 0:
+            return hbm, "measured hbm_gbs"
+    return 6650.0, "fallback"
+
+
+def make_decode_batch(dev, seed):
+    """The decode step's batch: 64 sequences with 16K-32K cached keys each, Hq 32 /
+    Hkv 8, each new token routed full with p = 0.125; returns q, k, v, lens, route
+    and the legal K/V bytes one step reads."""
+    B, Smax, Hq, Hkv, W, p_full = DECODE_B, DECODE_SMAX, DECODE_HQ, DECODE_HKV, DECODE_W, DECODE_P
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn((B, Hq, 128), generator=g, device=dev).bfloat16()
+    k = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
+    v = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
+    lens = torch.randint(Smax // 2, Smax + 1, (B,), generator=g, device=dev, dtype=torch.int32)
+    route = torch.rand((B,), generator=g, device=dev) < p_full
+    L = lens.cpu().numpy().astype(np.int64)
+    keys = np.where(route.cpu().numpy(), L, np.minimum(L, W))
+    kv_bytes = float(keys.sum()) * Hkv * 128 * 2 * 2
+    return q, k, v, lens, route, kv_bytes
+
+
+def time_steps(fn, steps, stream=None):
+    """Average milliseconds of ``fn`` over ``steps`` back-to-back calls (CUDA events)."""
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
 def run_decode(args, world, rank, local_rank):
     """Decode step of the config-3 model shape: 64 sequences with 16K-32K cached
     keys each, Hq 32 / Hkv 8, W 1024, each new token routed full with p = 0.125.
@@ -402,16 +395,8 @@ def run_decode(args, world, rank, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    B, Smax, Hq, Hkv, W, p_full = 64, 32768, 32, 8, 1024, 0.125
-    g = torch.Generator(device=dev).manual_seed(11 + rank)
-    q = torch.randn((B, Hq, 128), generator=g, device=dev).bfloat16()
-    k = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
-    v = torch.randn((B, Smax, Hkv, 128), generator=g, device=dev).bfloat16()
-    lens = torch.randint(Smax // 2, Smax + 1, (B,), generator=g, device=dev, dtype=torch.int32)
-    route = torch.rand((B,), generator=g, device=dev) < p_full
-    L = lens.cpu().numpy().astype(np.int64)
-    keys = np.where(route.cpu().numpy(), L, np.minimum(L, W))
-    kv_bytes = float(keys.sum()) * Hkv * 128 * 2 * 2
+    B, W = DECODE_B, DECODE_W
+    q, k, v, lens, route, kv_bytes = make_decode_batch(dev, 11 + rank)
     for _ in range(args.warmup):
         switch_gqa_decode_forward(q, k, v, lens, route, window_size=W)
     torch.cuda.synchronize()
@@ -438,12 +423,7 @@ def run_decode(args, world, rank, local_rank):
         ms = float(t.item())
         dist.destroy_process_group()
     if rank == 0:
-        hbm = None
-        path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-        if os.path.exists(path):
-            with open(path) as fh:
-                hbm = float(json.load(fh).get("hbm_gbs", 0.0)) or None
-        peak = hbm or 6650.0
+        peak, hbm_src = hbm_peak()
         gbs = kv_bytes * world / (ms * 1e-3) / 1e9
         print(json.dumps({
             "metric": "decode step: legal K/V bytes read per second", "value": gbs, "unit": "GB/s",
@@ -453,7 +433,7 @@ def run_decode(args, world, rank, local_rank):
             "config": {"workload": "decode: 64 sequences, 16K-32K cached keys, Hq 32, Hkv 8, W 1024, p_full 0.125",
                        "kv_bytes_per_step": kv_bytes},
             "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / world / peak, "peak_source": "measured hbm_gbs" if hbm else "fallback"},
+                         "frac": gbs / world / peak, "peak_source": hbm_src},
             "gpu_launches": 2 * args.steps,  # split-KV kernel + merge per step
             "clocks": clock_info,
         }), flush=True)
@@ -550,33 +530,9 @@ def run_cp(args, world, rank, local_rank):
     return 0
 
 
-def main():
-    args = parse_args()
-    world, rank, local_rank = dist_env()
-    if world > 1:
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
-    if args.decode and args.impl == "ours":
-        return run_decode(args, world, rank, local_rank)
-    if args.backward and args.impl == "ours":
-        return run_backward(args, world, rank, local_rank)
-    if args.sharded and args.impl == "ours":
-        return run_sharded(args, world, rank, local_rank)
-    if args.cp and args.impl == "ours":
-        rc = run_cp(args, world, rank, local_rank)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return rc
-    if args.impl == "reference":
-        rc = run_reference(args, world, rank)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return rc
-
+def run_replicas(args, world, rank, local_rank):
+    """Weak scaling: every rank draws its own 4 sequences (seed offset by rank) and
+    computes all of their (batch, KV group) units; no collective."""
     from switchattentionkernels_b200 import _core, build_switch_query_indices_batched, switch_gqa_prefill_forward
 
     dev = torch.device("cuda", local_rank)
@@ -605,7 +561,7 @@ def main():
         _core.forward(q, k, v, full, local, window_size=W, validate=False, query_counts=counts, out=out, lse=lse,
                       prefill_events=ev)
 
-    launches_per_step = 2  # mask compaction + persistent prefill kernel
+    launches_per_step = 3  # mask compaction (two launches for rows over 4096 tokens) + prefill kernel
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -725,6 +681,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "mode": "replicas",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": cfg.name, "B_per_gpu": B, "S": S, "Hq": Hq, "Hkv": k.shape[2], "head_dim": D,
                        "window": W, "p_full": cfg.p_full, "routing": "markov(switch=0.02)",
@@ -751,6 +708,341 @@ def main():
         import torch.distributed as dist
         dist.destroy_process_group()
     return 0
+
+
+def run_default(args, world, rank, local_rank):
+    """Config 3's (batch, KV group) units sharded over the ranks (see the module docstring)."""
+    import math
+
+    import torch.distributed as dist
+    from switchattentionkernels_b200 import (_core, build_switch_query_indices_batched, sharded,
+                                             switch_gqa_prefill_forward)
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    multi = world > 1
+    K, WU = args.steps, args.warmup
+
+    def barrier():
+        if multi:
+            dist.barrier()
+
+    def reduce(vals, op):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if multi:
+            dist.all_reduce(t, op=op)
+        return t.tolist()
+
+    # every rank draws the same batch and keeps its own units
+    w = workloads.make_inputs(CONFIG_ID, device=dev, on_device=True)
+    q, k, v, mask_cpu, W = w["q"], w["k"], w["v"], w["mask"], w["window"]
+    B, S, Hq, D = q.shape
+    Hkv = k.shape[2]
+    r = Hq // Hkv
+    mask_np = mask_cpu.numpy()
+    fl = [np.nonzero(m)[0] for m in mask_np]
+    ll = [np.nonzero(~m)[0] for m in mask_np]
+    costs = sharded.unit_costs(fl, ll, hkv=Hkv, skv=S, window=W)
+    plan = sharded.plan_units(costs, world)
+    mine = plan[rank]
+    n, n_max = len(mine), max(len(p) for p in plan)
+    flops_total = workloads.effective_flops(mask_np, W, S, Hq)
+    flops_rank = 4.0 * D * r * float(sum(costs[u] for u in mine))
+    q_u = sharded.take_units(q, mine, hkv=Hkv)
+    k_u = sharded.take_units(k, mine, hkv=Hkv)
+    v_u = sharded.take_units(v, mine, hkv=Hkv)
+    mask_u_cpu = mask_cpu[torch.tensor([u // Hkv for u in mine], dtype=torch.long)].contiguous()
+    mask_u = mask_u_cpu.to(dev)
+    o_u = torch.empty((n_max, S, r, D), dtype=torch.bfloat16, device=dev)
+    l_u = torch.empty((n_max, S, r), dtype=torch.float32, device=dev)
+    if multi:
+        del q, k, v
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(dev)
+    pf_events = []
+
+    def step(record=False):
+        if n == 0:
+            return
+        full, local, counts = build_switch_query_indices_batched(mask_u)
+        ev = None
+        if record:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            pf_events.append(ev)
+        _core.forward(q_u, k_u, v_u, full, local, window_size=W, validate=False, query_counts=counts,
+                      out=o_u[:n], lse=l_u[:n], prefill_events=ev)
+
+    launches_per_step = 3  # mask compaction (two launches: rows over 4096 tokens) + the prefill kernel
+    for _ in range(WU):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.mark("begin")
+    ms = time_steps(lambda: step(record=True), K, stream)
+    clocks.mark("end")
+    barrier()
+    clock_info = clocks.stop()
+    pf_avg = statistics.fmean([a.elapsed_time(b) for a, b in pf_events]) if pf_events else 0.0
+
+    # the same step with a replicated result: all-gather of every rank's O / LSE + scatter
+    out_all = torch.empty((B, S, Hq, D), dtype=torch.bfloat16, device=dev)
+    lse_all = torch.empty((B, S, Hq), dtype=torch.float32, device=dev)
+    gbufs = {}
+    g_events = []
+
+    def step_gather(record=False):
+        step()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if e:
+            e[0].record(stream)
+        got_o, got_l = sharded.all_gather_units(o_u, l_u, plan, bufs=gbufs)
+        if e:
+            e[1].record(stream)
+        sharded.scatter_gathered(got_o, got_l, plan, hkv=Hkv, out=out_all, lse=lse_all)
+        if e:
+            e[2].record(stream)
+            g_events.append(e)
+
+    for _ in range(2):
+        step_gather()
+    torch.cuda.synchronize()
+    barrier()
+    g_ms = time_steps(lambda: step_gather(record=True), K, stream)
+    barrier()
+    coll_ms = statistics.fmean([a.elapsed_time(b) for a, b, _ in g_events])
+    scat_ms = statistics.fmean([b.elapsed_time(c) for _, b, c in g_events])
+    del gbufs
+
+    # steady state: back-to-back steps for at least --steady-seconds, own clock record
+    ms_max0 = reduce([ms], dist.ReduceOp.MAX)[0] if multi else ms
+    n_steady = max(K, int(math.ceil(args.steady_seconds * 1000.0 / max(ms_max0, 1e-3))))
+    barrier()
+    torch.cuda.synchronize()
+    clocks2 = ClockSampler(dev.index)
+    clocks2.start()
+    clocks2.mark("begin")
+    st_ms = time_steps(step, n_steady, stream)
+    clocks2.mark("end")
+    barrier()
+    steady_clocks = clocks2.stop()
+
+    # e2e through the public API from pinned host buffers (the rank's own units)
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q_u, k_u, v_u))
+        hm = mask_u_cpu.pin_memory()
+        ho = torch.empty((n, S, r, D), dtype=torch.bfloat16).pin_memory()
+        hl = torch.empty((n, S, r), dtype=torch.float32).pin_memory()
+        s_in = torch.cuda.Stream(dev)
+        s_out = torch.cuda.Stream(dev)
+        slots = [(torch.empty_like(q_u), torch.empty_like(k_u), torch.empty_like(v_u),
+                  torch.empty(hm.shape, dtype=hm.dtype, device=dev)) for _ in range(2)]
+
+        def e2e_run(count):
+            if n == 0:
+                return
+            in_done = [torch.cuda.Event() for _ in range(count)]
+            comp_done = [torch.cuda.Event() for _ in range(count)]
+
+            def copy_in(i):
+                with torch.cuda.stream(s_in):
+                    if i >= 2:
+                        s_in.wait_event(comp_done[i - 2])  # slot i % 2 no longer read
+                    dq, dk, dv, dm = slots[i % 2]
+                    dq.copy_(hq, non_blocking=True)
+                    dk.copy_(hk, non_blocking=True)
+                    dv.copy_(hv, non_blocking=True)
+                    dm.copy_(hm, non_blocking=True)
+                    in_done[i].record(s_in)
+
+            copy_in(0)
+            for i in range(count):
+                if i + 1 < count:
+                    copy_in(i + 1)
+                stream.wait_event(in_done[i])
+                dq, dk, dv, dm = slots[i % 2]
+                full, local, cnt = build_switch_query_indices_batched(dm)
+                o, l_ = switch_gqa_prefill_forward(dq, dk, dv, full, local, window_size=W, query_counts=cnt)
+                comp_done[i].record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(comp_done[i])
+                    o.record_stream(s_out)
+                    l_.record_stream(s_out)
+                    ho.copy_(o, non_blocking=True)
+                    hl.copy_(l_, non_blocking=True)
+
+        e2e_run(min(2, WU) + 1)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        s_in.wait_event(e0)
+        e2e_run(K)
+        e1.record(s_out)
+        torch.cuda.synchronize()
+        barrier()
+        e2e = {"ms": e0.elapsed_time(e1) / K,
+               "h2d": (hq.numel() + hk.numel() + hv.numel()) * 2 + hm.numel(),
+               "d2h": ho.numel() * 2 + hl.numel() * 4}
+
+    # N = 1 extras: the row-major layout of the single-GPU API, one backward and one decode step
+    extras = {}
+    if not multi and not args.no_extras:
+        from switchattentionkernels_b200.backward import switch_gqa_prefill_backward
+        from switchattentionkernels_b200.decode import switch_gqa_decode_forward
+
+        mask_dev = mask_cpu.to(dev)
+        full, local, counts = build_switch_query_indices_batched(mask_dev)
+        out = torch.empty_like(q)
+        lse = torch.empty((B, S, Hq), dtype=torch.float32, device=dev)
+        std_events = []
+
+        def step_std():
+            f, l_, c = build_switch_query_indices_batched(mask_dev)
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            std_events.append(ev)
+            _core.forward(q, k, v, f, l_, window_size=W, validate=False, query_counts=c, out=out, lse=lse,
+                          prefill_events=ev)
+
+        for _ in range(WU):
+            step_std()
+        torch.cuda.synchronize()
+        std_events.clear()
+        std_ms = time_steps(step_std, K, stream)
+        std_k = statistics.fmean([a.elapsed_time(b) for a, b in std_events])
+        extras["standard_layout"] = {"value": flops_total / (std_ms * 1e-3) / 1e12, "unit": UNIT,
+                                     "ms_per_step": std_ms, "kernel_ms": std_k,
+                                     "layout": "q [B, S, Hq, 128], k / v [B, S, Hkv, 128] (the single-GPU API)"}
+        peak_burst, _, peak_src = measured_peaks()
+        g = torch.Generator(device=dev).manual_seed(5)
+        dout = torch.randn(out.shape, generator=g, device=dev).bfloat16()
+
+        def step_bwd():
+            switch_gqa_prefill_backward(q, k, v, out, lse, dout, full, local, window_size=W, query_counts=counts)
+
+        for _ in range(2):
+            step_bwd()
+        torch.cuda.synchronize()
+        nb = max(3, K // 4)
+        b_ms = time_steps(step_bwd, nb, stream)
+        bval = 2.5 * flops_total / (b_ms * 1e-3) / 1e12
+        extras["backward"] = {
+            "metric": "prefill backward (dQ, dK, dV): effective TFLOP/s, 2.5 x the forward's legal-entry FLOP",
+            "value": bval, "unit": UNIT, "ms_per_step": b_ms, "steps": nb,
+            "roofline": {"bound": "tensor", "achieved": bval, "peak": peak_burst, "unit": UNIT,
+                         "frac": bval / peak_burst, "peak_source": f"{peak_src} bf16_tflops (burst)"},
+            "gpu_launches_per_step": 3}
+        del dout
+        dq_, dk_, dv_, dl, dr, kv_bytes = make_decode_batch(dev, 11)
+
+        def step_dec():
+            switch_gqa_decode_forward(dq_, dk_, dv_, dl, dr, window_size=DECODE_W)
+
+        for _ in range(2):
+            step_dec()
+        torch.cuda.synchronize()
+        nd = max(5, K // 2)
+        d_ms = time_steps(step_dec, nd, stream)
+        gbs = kv_bytes / (d_ms * 1e-3) / 1e9
+        hpk, hsrc = hbm_peak()
+        extras["decode"] = {
+            "metric": "decode step (one new token per sequence): legal K/V bytes read per second",
+            "value": gbs, "unit": "GB/s", "ms_per_step": d_ms, "steps": nd,
+            "tokens_per_s": DECODE_B / (d_ms * 1e-3),
+            "workload": f"{DECODE_B} sequences, 16K-32K cached keys, Hq {DECODE_HQ}, Hkv {DECODE_HKV}, "
+                        f"W {DECODE_W}, p_full {DECODE_P}",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hpk, "unit": "GB/s", "frac": gbs / hpk,
+                         "peak_source": hsrc},
+            "gpu_launches_per_step": 2}
+        del dq_, dk_, dv_
+
+    e2e_ms = e2e["ms"] if e2e else 0.0
+    mx = reduce([ms, g_ms, coll_ms, scat_ms, st_ms, e2e_ms, pf_avg], dist.ReduceOp.MAX)
+    sm = reduce([flops_rank, pf_avg, float(e2e["h2d"] if e2e else 0), float(e2e["d2h"] if e2e else 0)],
+                dist.ReduceOp.SUM)
+    ms_max, g_ms_max, coll_max, scat_max, st_max, e2e_max, pf_max = mx
+    flops_sum, pf_sum, h2d_sum, d2h_sum = sm
+
+    cpu = None
+    if rank == 0 and not multi and not args.no_cpu_baseline:
+        # rank 0 at N=1 only: the CPU restatement on a bounded sample of the same workload
+        cpu_inputs = {"q_cpu": q.cpu(), "k_cpu": k.cpu(), "v_cpu": v.cpu(), "mask": mask_np, "window": W}
+        cpu = cpu_oracle_sample(cpu_inputs, args.cpu_seconds)
+
+    if rank == 0:
+        peak_burst, peak_sustained, peak_src = measured_peaks()
+        value = flops_total / (ms_max * 1e-3) / 1e12
+        achieved = flops_sum / (pf_sum * 1e-3) / 1e12 if pf_sum > 0 else 0.0
+        recv = (world - 1) * n_max * S * r * (D * 2 + 4)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": WU,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": config3_dict(world),
+            "units_per_rank": [len(p) for p in plan],
+            "layout": "each rank holds its units unit-major: q [units, S, Hq/Hkv, 128], k / v [units, S, 1, 128]",
+            "effective_tflop_per_step": flops_total / 1e12,
+            "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": UNIT,
+                         "frac": achieved / peak_burst, "traffic": profile_traffic(config3_dict(1)["workload"]),
+                         "kernel": "switch_prefill_kernel", "kernel_ms": pf_max,
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "frac_of_sustained": achieved / peak_sustained},
+            "gather": {"value": flops_total / (g_ms_max * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": g_ms_max,
+                       "all_gather_ms": coll_max, "scatter_ms": scat_max,
+                       "bytes_received_per_rank": recv,
+                       "all_gather_gbs_per_rank": recv / (coll_max * 1e-3) / 1e9 if recv and coll_max > 0 else None,
+                       "reference_nvlink_peer_copy_gbs": 770.0,
+                       "what": "every step ends with NCCL all_gather_into_tensor of every rank's unit-major O and "
+                               "LSE and the scatter kernel into [B, S, Hq, ...] on every rank"},
+            "steady": {"value": flops_total / (st_max * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": st_max,
+                       "steps": n_steady, "clocks": steady_clocks,
+                       "mcycles_per_step": (st_max * 1e-3 * steady_clocks["sm_mhz"] * 1e6 / 1e6
+                                            if steady_clocks else None)},
+            "gpu_launches": launches_per_step * K,  # per rank: compaction (2) + prefill kernel, every step
+            "clocks": clock_info,
+        }
+        if e2e is not None:
+            line["e2e"] = {"value": flops_total / (e2e_max * 1e-3) / 1e12, "unit": UNIT,
+                           "h2d_bytes_per_step": int(h2d_sum), "d2h_bytes_per_step": int(d2h_sum),
+                           "ms_per_step": e2e_max,
+                           "what": "every step: the rank's own units' q/k/v/mask host->device, compaction + "
+                                   "validating public forward, its O/LSE device->host (bytes summed over ranks)"}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    return 0
+
+def main():
+    args = parse_args()
+    world, rank, local_rank = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        if args.decode:
+            return run_decode(args, world, rank, local_rank)
+        if args.backward:
+            return run_backward(args, world, rank, local_rank)
+        if args.cp:
+            return run_cp(args, world, rank, local_rank)
+        if args.replicas:
+            return run_replicas(args, world, rank, local_rank)
+        return run_default(args, world, rank, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
 
 
 if __name__ == "__main__":

@@ -194,6 +194,23 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Unit-major <-> row-major moves of the multi-GPU driver (no counterpart in the
+ * reference, which has no distributed code; its per-(batch, head) grid,
+ * swiattn_gqa_prefill.py:69, admits the (batch, KV group) split these serve).
+ * A unit is u = b * hkv + g.  Unit-major: [n_slots, S, chunk_bytes]; slot i
+ * holds unit unit_of_slot[i] (device int32; -1 = padding slot, skipped).
+ * Row-major: [B, S, row_bytes] with unit (b, g) at byte offset g * chunk_bytes of
+ * each row (e.g. O: chunk_bytes = r * 128 * 2, row_bytes = Hq * 128 * 2; LSE:
+ * r * 4 and Hq * 4).  swa_scatter_units: unit-major src -> row-major dst (the
+ * permute after an all-gather of every rank's units); swa_gather_units: row-major
+ * src -> unit-major dst (a rank's unit slices).  chunk_bytes, row_bytes and the
+ * pointers must be multiples of 4; 16 gives 16-byte vector moves.  At most 65535
+ * slots. */
+int swa_scatter_units(const void* src, const int32_t* unit_of_slot, int n_slots, int S, int hkv, int chunk_bytes,
+                      int row_bytes, void* dst, void* stream);
+int swa_gather_units(const void* src, const int32_t* unit_of_slot, int n_slots, int S, int hkv, int chunk_bytes,
+                     int row_bytes, void* dst, void* stream);
+
 /* Allocation-free batched prefill.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory when they run attention --
  * e.g. a plugin whose host framework owns all device memory and passes only
@@ -209,7 +226,8 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
  *     the GPU (different streams, or a second call before the first finished on
  *     another stream) race -- serialise them on one stream;
  *   - the first call on a device resolves the array's device address (with that
- *     device current); make that first call before any stream capture;
+ *     device current); make that first call before any stream capture (a lookup
+ *     that fails returns SWA_E_CUDA and is retried by the next call);
  *   - status_out (nullable, device int32[2]) receives the validation bits
  *     (SWA_STATUS_FULL_* / LOCAL_* / COVER; a non-zero value means nothing was
  *     computed) and the kernel status bits (SWA_STATUS_TIMEOUT). */

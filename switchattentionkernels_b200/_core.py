@@ -33,6 +33,8 @@ ERR_META = "invalid Switch Attention position metadata"
 
 # When set (environment variable SWA_CHECK_STATUS=1), every forward call reads
 # back the kernel's status word and raises if a device-side wait timed out.
+# Without it no call synchronises; a caller that wants the status passes a
+# device int32 tensor as ``status_out`` and reads it after its own synchronisation.
 CHECK_DEVICE_STATUS = os.environ.get("SWA_CHECK_STATUS", "0") == "1"
 
 
@@ -67,6 +69,29 @@ def bucket_capacity(count: int, block_m: int) -> int:
     if padded < count:
         padded <<= 1
     return padded
+
+
+def _check_status_out(status_out, dev) -> None:
+    if status_out is None:
+        return
+    if (not isinstance(status_out, torch.Tensor) or status_out.dtype != torch.int32 or status_out.device != dev
+            or status_out.numel() < 1):
+        raise ValueError("status_out must be an int32 tensor with at least one element on the device of Q")
+
+
+def publish_status(status_word: torch.Tensor, status_out) -> None:
+    """Hand the launch's device status word to the caller without a host sync.
+
+    ``status_word`` is a one-element int32 device tensor that the launch's kernels
+    write; it is copied into ``status_out[0]`` on the current stream.  A non-zero
+    value (``_native.STATUS_*`` bits; ``STATUS_TIMEOUT`` = a device-side wait gave
+    up) means the outputs of that call are undefined.  With SWA_CHECK_STATUS=1 the
+    word is also read back here and raised as an exception.
+    """
+    if status_out is not None:
+        status_out.view(-1)[:1].copy_(status_word.view(-1)[:1])
+    if CHECK_DEVICE_STATUS:
+        _raise_status(int(status_word.item()))
 
 
 def _raise_status(status: int) -> None:
@@ -250,7 +275,8 @@ def _index_rows(indices: torch.Tensor, B: int, device: torch.device, name: str) 
 
 
 def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, window_size=1024, sm_scale=None,
-            validate=True, query_counts=None, bg_list=None, out=None, lse=None, prefill_events=None):
+            validate=True, query_counts=None, bg_list=None, out=None, lse=None, prefill_events=None,
+            status_out=None):
     """Both branches of Switch Attention GQA prefill (see ``switch_gqa_prefill_forward``).
 
     ``query_counts``: optional int32 ``[B, 2]`` device tensor of per-row
@@ -262,6 +288,11 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     (rows outside the computed units are left untouched).
     ``prefill_events``: optional pair of CUDA events recorded on the current
     stream right before and after the prefill kernel launch (kernel timing).
+    ``status_out``: optional int32 device tensor; element 0 receives the call's
+    status word on the current stream (no host sync): 0 when the results are
+    valid; otherwise the validation bits of an unvalidated call
+    (``validate=False``: the kernel then wrote nothing) or ``STATUS_TIMEOUT``
+    (a device-side wait gave up; O / LSE are undefined).
     """
     validate_qkv(q, k, v)
     if window_size <= 0:
@@ -291,6 +322,7 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
             raise ValueError("bg_list must be a non-empty 1-D list of b * Hkv + g unit ids")
         if bool(((bg_list < 0) | (bg_list >= B * Hkv)).any()):
             raise ValueError("bg_list entries must lie in [0, B * Hkv)")
+    _check_status_out(status_out, dev)
     lib = _native.load()
     stream = _native.stream_ptr(dev)
     ws = torch.zeros(4 + 2 * B, dtype=torch.int32, device=dev)
@@ -355,6 +387,7 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
         _native.check(rc, "switch_gqa_prefill_forward")
         if prefill_events is not None:
             prefill_events[1].record()
-        if CHECK_DEVICE_STATUS:
-            _raise_status(int(ws[1].item()))
+        if status_out is not None or CHECK_DEVICE_STATUS:
+            # ws[1]: kernel status (timeout); ws[2]: validation bits of the gated launch
+            publish_status(torch.bitwise_or(ws[1:2], ws[2:3]), status_out)
     return out, lse

@@ -45,6 +45,8 @@ EXPORTED = (
     "swa_decode_forward",
     "swa_prefill_backward",
     "swa_backward_workspace_bytes",
+    "swa_scatter_units",
+    "swa_gather_units",
 )
 
 _lock = threading.Lock()
@@ -129,6 +131,10 @@ def _declare(lib) -> None:
         _i, _f,                # window, scale_log2
         _p, _sz, _p,           # workspace, workspace_bytes, stream
     ]
+    for name in ("swa_scatter_units", "swa_gather_units"):
+        fn = getattr(lib, name)
+        fn.restype = _i
+        fn.argtypes = [_p, _p, _i, _i, _i, _i, _i, _p, _p]  # src, unit_of_slot, n_slots, S, hkv, chunk, row, dst, stream
 
 
 def load():

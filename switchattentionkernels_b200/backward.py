@@ -9,12 +9,10 @@ rows, and the dK / dV pass over 64-key tiles.
 """
 from __future__ import annotations
 
-import os
-
 import torch
 
 from . import _core, _native
-from ._core import LOG2E, _raise_status
+from ._core import LOG2E
 
 
 def _lists(full, local, query_counts, B, dev):
@@ -37,13 +35,17 @@ def _lists(full, local, query_counts, B, dev):
 
 
 def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, local_query_indices, *, metadata=None,
-                                window_size: int = 1024, sm_scale: float | None = None, query_counts=None):
+                                window_size: int = 1024, sm_scale: float | None = None, query_counts=None,
+                                status_out=None):
     """``(dq, dk, dv)`` of ``switch_gqa_prefill_forward`` for the upstream gradient ``dout``.
 
     ``q`` / ``k`` / ``v`` / ``out`` / ``dout``: contiguous BF16 as in the forward;
     ``lse``: the forward's FP32 ``[B, Sq, Hq]`` (log2 units).  Index lists: the
     forward's (1-D for ``B == 1``, or -1 padded ``[B, N]`` with ``query_counts``).
-    Returns BF16 tensors shaped like ``q``, ``k`` and ``v``.
+    Returns BF16 tensors shaped like ``q``, ``k`` and ``v``.  ``status_out``:
+    optional int32 device tensor whose element 0 receives the launch's status word
+    on the current stream (no host sync); non-zero (``STATUS_TIMEOUT``) means the
+    gradients are undefined.
     """
     _core.validate_qkv(q, k, v)
     for name, t in (("out", out), ("dout", dout)):
@@ -62,6 +64,7 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
     scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * LOG2E
     if not scale > 0:
         raise ValueError("sm_scale must be positive")
+    _core._check_status_out(status_out, dev)
     f, l, counts = _lists(full_query_indices, local_query_indices, query_counts, B, dev)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
@@ -80,8 +83,8 @@ def switch_gqa_prefill_backward(q, k, v, out, lse, dout, full_query_indices, loc
             _native.ptr(dq), _native.ptr(dk), _native.ptr(dv), B, Sq, Skv, Hq, Hkv, D, int(window_size),
             float(scale), _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
     _native.check(rc, "switch_gqa_prefill_backward")
-    if os.environ.get("SWA_CHECK_STATUS") == "1":
-        _raise_status(int(ws[0].item()))
+    if status_out is not None or _core.CHECK_DEVICE_STATUS:
+        _core.publish_status(ws[0:1], status_out)
     return dq, dk, dv
 
 

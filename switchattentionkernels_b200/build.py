@@ -18,7 +18,7 @@ LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libswattn_b200.so")
 BUILD_DIR = os.path.join(os.path.dirname(PKG_DIR), "_build")
 
-SOURCES = ["api.cu", "prefill_sm100.cu", "decode_sm100.cu", "backward_sm100.cu", "index_kernels.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "prefill_sm100.cu", "decode_sm100.cu", "backward_sm100.cu", "index_kernels.cu", "units.cu", "noalloc.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -89,8 +89,14 @@ __global__ void __launch_bounds__(256) bwd_pack_kernel(const __grid_constant__ B
       for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(hmask, d, off);
       int lo, hi;
       bwd_row_bounds(p, branch, pos, lo, hi);
-      const float lse = p.lse[row];
-      if (!(lse > -INFINITY)) hi = lo;  // a row without legal keys has no gradient
+      float lse = p.lse[row];
+      if (!(lse > -INFINITY)) {
+        // a row without legal keys (forward O = NaN, LSE = -inf) has no gradient:
+        // empty key range, and finite LSE / D so that no NaN reaches its masked entries
+        hi = lo;
+        lse = 0.0f;
+        d = 0.0f;
+      }
       rec = make_int4(lo, max(hi, lo), __float_as_int(lse), __float_as_int(d));
     }
     *reinterpret_cast<uint4*>(p.qp + static_cast<int64_t>(pr) * 128 + 8 * hl) = qv;

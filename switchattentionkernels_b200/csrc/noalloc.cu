@@ -28,25 +28,31 @@ constexpr int kScratchWords = 4096;  // 16 KB
 static __device__ __align__(256) int32_t g_noalloc_scratch[kScratchWords];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_setup_once[kMaxDevices];
+std::mutex g_setup_mutex;
 int32_t* g_scratch_ptr[kMaxDevices] = {};
-cudaError_t g_setup_err[kMaxDevices] = {};
 
 int fail(int code, const char* msg) {
   swa::set_last_error(msg);
   return code;
 }
 
-// Device address of the scratch array for the current device (resolved once per
-// device, with that device current).
+// Device address of the scratch array for the current device, resolved with that
+// device current.  Only a successful lookup is kept: if it fails (no context yet,
+// or the call came during a stream capture), the error is returned and the next
+// call on that device tries again, so the failure is not sticky.
 cudaError_t scratch_for_device(int dev, int32_t** out) {
-  std::call_once(g_setup_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
-    g_setup_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (g_setup_err[dev] == cudaSuccess) g_scratch_ptr[dev] = static_cast<int32_t*>(p);
-  });
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *out = nullptr;
+      return e;
+    }
+    g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
   *out = g_scratch_ptr[dev];
-  return g_setup_err[dev];
+  return cudaSuccess;
 }
 
 }  // namespace

@@ -157,13 +157,23 @@ __device__ __forceinline__ int load_pos(const PrefillParams& p, int branch, int 
 }
 
 // Decode work item `it` into a unit; returns false for an empty item.
+//
+// Full-branch items are ordered (b, g)-major: all units of one (batch, KV group),
+// longest first, then the next group.  The CTAs running at one time then stream
+// the K/V prefix of one or two groups (16 MB each at S = 32K), which stays in L2
+// while every unit of the group reads it; ordered by length across all groups,
+// they streamed the prefixes of every group at once and re-read K/V from DRAM.
+// The tail stays short: the last full units of a group are its shortest, and the
+// local-branch units (all about W keys) come after every full unit.
 __device__ bool decode_item(const PrefillParams& p, int it, int nf, int maxnpb0, int maxnpb1, Unit& u) {
   const int per_level = p.n_bg * p.nhb;
   int branch, pb, rem;
   if (it < nf) {
     branch = 0;
-    pb = maxnpb0 - 1 - it / per_level;  // longest full-causal units first
-    rem = it % per_level;
+    const int per_bg = maxnpb0 * p.nhb;
+    const int within = it % per_bg;
+    pb = maxnpb0 - 1 - within / p.nhb;  // longest full-causal units of the group first
+    rem = (it / per_bg) * p.nhb + within % p.nhb;
   } else {
     it -= nf;
     branch = 1;
@@ -290,7 +300,11 @@ __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit&
 // [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted for minimum maximal relative
 // error on that interval (max relative error 7.5e-5, below the BF16 rounding that
 // P receives); 2^j is added to the exponent field.  Arguments are clamped at
-// -125 so the result stays a normal number (masked entries, -inf, give 2^-125).
+// -125 so the result stays a normal number: masked entries (-inf) give 2^-125
+// instead of 0.  In a row with a legal key the entry that set the running max
+// contributes 1 to the row sum, so these terms lie far below FP32 resolution; a
+// row without any legal key is detected from its bounds in the epilogue and
+// written as the reference writes it (O = 0/0 = NaN, LSE = log2(0) = -inf).
 __device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& p0, float& p1) {
   float x0, x1;
   f2_unpack(x2, x0, x1);
@@ -843,8 +857,12 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       tr.ev(21, s_use);
       named_bar_sync(bar_id, 256);
       l += xsum[tile * 256 + (half ^ 1) * 128 + t];
-      const float inv_l = 1.0f / l;
-      if (half == 0 && valid_row) p.lse[orow] = lg2_approx(l) + m;
+      // A row whose key range is empty (metadata start >= end, or a local row at
+      // t >= Skv + W - 1) has row sum 0 in the reference (swiattn_gqa_prefill.py:201-206,
+      // swiattn_gqa_prefill_varlen.py:236-241): O = 0/0 and LSE = log2(0) + m.
+      const bool no_keys = rb.hi <= rb.lo;
+      const float inv_l = no_keys ? __int_as_float(0x7FC00000) : 1.0f / l;
+      if (half == 0 && valid_row) p.lse[orow] = no_keys ? -INFINITY : lg2_approx(l) + m;
       tc_fence_after();
       uint32_t ch[8][4];  // ch[j]: chunk j (columns 8 j .. 8 j + 7 of this half) as BF16 pairs
 #pragma unroll
@@ -890,6 +908,13 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       }
       tr.ev(22, s_use);
     }
+    // Abort path only: this warp left the loop on a timed-out (or flagged) wait.  Its
+    // partner warps of the tile may sit in the row-exchange or epilogue barrier that
+    // this warp will not reach; one arrival completes that phase for them, and after
+    // any phase of that barrier the next blocking step of every softmax warp is a
+    // bounded mbarrier wait, which sees the abort flag.  An arrival that no warp
+    // waits for is harmless: the barrier is not used again before the CTA exits.
+    if (__any_sync(0xffffffffu, *abort_flag != 0)) named_bar_arrive(bar_id, 256);
   }
 
   // ------------------------------------------------------------------ teardown

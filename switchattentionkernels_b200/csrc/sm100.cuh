@@ -28,12 +28,16 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// Every wait on a barrier is bounded.  A wait that exceeds kWaitLimitNs sets the
-// CTA-wide abort flag (shared memory) and returns false; every other wait sees
-// the flag and returns false as well, so all roles leave their loops, the CTA
-// frees its tensor memory and the kernel returns with an error code recorded in
-// global memory.  No legitimate wait in these kernels lasts longer than one
-// work unit (well under 10 ms), so one second is a wide margin.
+// Every wait on an mbarrier is bounded.  A wait that exceeds kWaitLimitNs sets
+// the CTA-wide abort flag (shared memory) and returns false; every other wait
+// sees the flag and returns false as well, so all roles leave their loops, the
+// CTA frees its tensor memory and the kernel returns with an error code recorded
+// in global memory.  No legitimate wait in these kernels lasts longer than one
+// work unit (well under 10 ms), so one second is a wide margin.  Named barriers
+// (bar.sync) have no time limit: a kernel whose warps also meet in one gives
+// every warp that leaves on an abort a bar.arrive on it (named_bar_arrive), so
+// partner warps already waiting there are released and reach their next bounded
+// mbarrier wait, which sees the flag.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 // ---------------------------------------------------------------------------
@@ -371,6 +375,12 @@ __device__ __forceinline__ void reg_fence32(uint32_t* r) {
 // Named barrier over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Arrive on a named barrier without waiting (counts this warp's threads toward
+// the current phase of barrier `id` over `count` threads).
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void reg_fence16(uint32_t* r) {

@@ -11,17 +11,15 @@ merge of the splits.
 """
 from __future__ import annotations
 
-import os
-
 import torch
 
-from . import _native
-from ._core import LOG2E, _raise_status
+from . import _core, _native
+from ._core import LOG2E
 
 
 def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                               seq_lens: torch.Tensor, route_full: torch.Tensor, *, window_size: int = 1024,
-                              sm_scale: float | None = None):
+                              sm_scale: float | None = None, status_out: torch.Tensor | None = None):
     """Attention of each sequence's new token over its KV cache.
 
     ``q``: BF16 ``[B, Hq, 128]`` (or ``[B, 1, Hq, 128]``); ``k_cache`` / ``v_cache``:
@@ -30,6 +28,9 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     ``route_full``: bool ``[B]``, True = full causal attention, False = the
     sliding window of the last ``window_size`` keys.  Returns ``(O, LSE)``:
     BF16 ``[B, Hq, 128]`` and FP32 ``[B, Hq]`` (log2 units), shaped like ``q``.
+    ``status_out``: optional int32 device tensor whose element 0 receives the
+    launch's status word on the current stream (no host sync); non-zero
+    (``STATUS_TIMEOUT``) means the outputs are undefined.
     """
     squeeze = q.ndim == 4
     if squeeze:
@@ -63,6 +64,7 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * LOG2E
     if not scale > 0:
         raise ValueError("sm_scale must be positive")
+    _core._check_status_out(status_out, dev)
     lib = _native.load()
     out = torch.empty_like(q)
     lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
@@ -78,8 +80,8 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
                                     _native.ptr(lse), B, Smax, Hq, Hkv, D, int(window_size), float(scale),
                                     _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
     _native.check(rc, "switch_gqa_decode_forward")
-    if os.environ.get("SWA_CHECK_STATUS") == "1":
-        _raise_status(int(ws[0].item()))
+    if status_out is not None or _core.CHECK_DEVICE_STATUS:
+        _core.publish_status(ws[0:1], status_out)
     if squeeze:
         return out.unsqueeze(1), lse.unsqueeze(1)
     return out, lse

@@ -4,10 +4,19 @@ The unit of work is a (batch b, KV group g) pair: it reads ``q[b, :, g*r:(g+1)*r
 ``k/v[b, :, g]`` and batch b's index lists, and writes the same slice of O/LSE,
 so units are independent and need no communication.  Units are assigned to
 ranks by longest-processing-time-first on their cost (the legal score entries
-of batch b), every rank computes only its own units (the kernel's ``bg_list``),
-and -- only when the caller asks for a replicated result -- one all-gather moves
-O (BF16) and LSE (FP32) of every unit to every rank (NCCL over NVLink for CUDA
-tensors; any backend that implements ``all_gather``).
+of batch b).  Two ways to run a rank's share:
+
+* replicated inputs: every rank holds the whole q/k/v and the kernel computes
+  only the rank's units (its ``bg_list``): ``sharded_switch_gqa_prefill_forward``;
+* unit-major inputs: a rank holds only its units, as ``[n, S, r, 128]`` q and
+  ``[n, S, 1, 128]`` k / v (``take_units``), which is the ordinary forward with
+  ``B = n`` sequences of ``r`` query heads over one KV head -- the shape in which
+  a head-sharded model layer produces them, and the only bytes a rank needs.
+
+Only when the caller asks for a replicated result does one all-gather move O
+(BF16) and LSE (FP32) of every unit to every rank (NCCL over NVLink for CUDA
+tensors), followed by one scatter kernel into the ``[B, S, Hq, ...]`` layout
+(``gather_units_to_rows``).
 
 The reference has no distributed code; this driver implements the sharding
 that its per-(batch, head) grid (``swiattn_gqa_prefill.py:69``) admits.
@@ -20,19 +29,38 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import _core
+from . import _core, _native
 
 
 def unit_costs(full_lists: Sequence[np.ndarray], local_lists: Sequence[np.ndarray], *, hkv: int, skv: int,
-               window: int) -> np.ndarray:
-    """Cost of every unit ``b * hkv + g``: legal (row, key) entries of batch b."""
+               window: int, metadata=None) -> np.ndarray:
+    """Cost of every unit ``b * hkv + g``: legal (row, key) entries of batch b.
+
+    Without ``metadata`` a row at position t has the fixed-length key ranges
+    (full ``[0, t]``, local ``[t - W + 1, t]``, clipped to ``[0, Skv)``).  With
+    ``metadata`` (a ``SwitchAttentionMetadata`` or a dict of its arrays) the
+    ranges are the per-row bounds ``[start, causal_end)`` the kernel uses, so
+    packed sequences are costed by their own lengths.
+    """
+    bounds = None
+    if metadata is not None:
+        def arr(name):
+            a = metadata[name] if isinstance(metadata, dict) else getattr(metadata, name)
+            return a.detach().cpu().numpy() if isinstance(a, torch.Tensor) else np.asarray(a)
+        ends = np.minimum(arr("causal_ends").astype(np.int64), skv)
+        bounds = (np.maximum(arr("full_starts").astype(np.int64), 0),
+                  np.maximum(arr("local_starts").astype(np.int64), 0), ends)
     B = len(full_lists)
     costs = np.zeros(B * hkv, dtype=np.float64)
     for b in range(B):
         f = np.asarray(full_lists[b], dtype=np.int64)
         l = np.asarray(local_lists[b], dtype=np.int64)
-        n = float(np.minimum(f + 1, skv).sum())
-        n += float(np.maximum(np.minimum(l + 1, skv) - np.maximum(l - window + 1, 0), 0).sum())
+        if bounds is None:
+            n = float(np.minimum(f + 1, skv).sum())
+            n += float(np.maximum(np.minimum(l + 1, skv) - np.maximum(l - window + 1, 0), 0).sum())
+        else:
+            fs, ls, ce = bounds
+            n = float(np.maximum(ce[f] - fs[f], 0).sum()) + float(np.maximum(ce[l] - ls[l], 0).sum())
         costs[b * hkv:(b + 1) * hkv] = n
     return costs
 
@@ -70,34 +98,147 @@ def _host_lists(full, local, query_counts, B):
     return fl, ll
 
 
+def slot_map(plan: list[list[int]], n_slots: int | None = None) -> list[int]:
+    """Unit id of every slot of an all-gathered unit-major buffer: rank p's units
+    fill slots ``[p * n, p * n + len(plan[p]))`` (``n`` = the largest share), -1 pads."""
+    n = max((len(p) for p in plan), default=0) if n_slots is None else n_slots
+    ids = []
+    for p in plan:
+        ids.extend(list(p) + [-1] * (n - len(p)))
+    return ids
+
+
+_ID_CACHE: dict = {}
+
+
+def _device_ids(unit_ids: Sequence[int], device: torch.device) -> torch.Tensor:
+    """int32 device copy of a slot -> unit map, made once per (map, device): later
+    calls enqueue no host-to-device copy."""
+    key = (tuple(int(u) for u in unit_ids), device)
+    t = _ID_CACHE.get(key)
+    if t is None:
+        if len(_ID_CACHE) > 256:
+            _ID_CACHE.clear()
+        t = torch.tensor(key[0], dtype=torch.int32).to(device)
+        _ID_CACHE[key] = t
+    return t
+
+
+def _move_units(src: torch.Tensor, dst: torch.Tensor, unit_ids: Sequence[int], *, hkv: int, to_rows: bool) -> None:
+    """Copy between a row-major ``[B, S, H, ...]`` tensor and a unit-major
+    ``[n, S, r, ...]`` one (``H = hkv * r``); slots with unit id -1 are skipped.
+
+    CUDA tensors: one ``swa_scatter_units`` / ``swa_gather_units`` kernel.  CPU
+    tensors (the host-side tests over gloo): the same move by torch indexing.
+    """
+    rows, units = (dst, src) if to_rows else (src, dst)
+    B, S, H = rows.shape[:3]
+    r = H // hkv
+    if units.shape[1] != S or units.shape[2] != r or units.shape[0] < len(unit_ids):
+        raise ValueError("unit-major tensor must be [n, S, Hq / Hkv, ...] with a slot per unit id")
+    if rows.dtype != units.dtype or not rows.is_contiguous() or not units.is_contiguous():
+        raise ValueError("row-major and unit-major tensors must be contiguous and of one dtype")
+    if rows.device.type == "cuda":
+        lib = _native.load()
+        ids = _device_ids(unit_ids, rows.device)
+        chunk = r * rows[0, 0, 0].numel() * rows.element_size()
+        fn = lib.swa_scatter_units if to_rows else lib.swa_gather_units
+        with torch.cuda.device(rows.device):
+            rc = fn(_native.ptr(src), _native.ptr(ids), len(unit_ids), S, hkv, chunk, H * chunk // r,
+                    _native.ptr(dst), _native.stream_ptr(rows.device))
+        _native.check(rc, "swa_scatter_units" if to_rows else "swa_gather_units")
+        return
+    view = rows.view(B, S, hkv, r, *rows.shape[3:])
+    for i, u in enumerate(unit_ids):
+        if u < 0:
+            continue
+        b, g = divmod(int(u), hkv)
+        if to_rows:
+            view[b, :, g].copy_(units[i])
+        else:
+            units[i].copy_(view[b, :, g])
+
+
+def take_units(x: torch.Tensor, unit_ids: Sequence[int], *, hkv: int, slots: int | None = None) -> torch.Tensor:
+    """Unit-major copy ``[max(n, slots), S, r, ...]`` of the units' slices of a
+    row-major ``[B, S, H, ...]`` tensor (``r = H / hkv``; k / v: ``H = hkv``, r = 1)."""
+    B, S, H = x.shape[:3]
+    n = max(len(unit_ids), slots or 0)
+    out = x.new_empty((n, S, H // hkv, *x.shape[3:]))
+    _move_units(x, out, list(unit_ids), hkv=hkv, to_rows=False)
+    return out
+
+
+def all_gather_units(o_u: torch.Tensor, lse_u: torch.Tensor, plan: list[list[int]], *, group=None,
+                     bufs: dict | None = None):
+    """Every rank's unit-major outputs on every rank: ``([world * n, S, r, 128],
+    [world * n, S, r])`` with rank p's units in slots ``[p * n, p * n + len(plan[p]))``
+    (``n`` = the largest share).  One ``all_gather_into_tensor`` per tensor; at one
+    rank (or without a process group) the inputs themselves.  ``bufs``: optional
+    dict that keeps the receive buffers across calls."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    n_max = max(len(p) for p in plan)
+    _, S, r, D = o_u.shape
+    if o_u.shape[0] < n_max or lse_u.shape[0] < n_max:
+        raise ValueError("o_u / lse_u need a slot for each unit of the largest share")
+    send_o, send_l = o_u[:n_max], lse_u[:n_max]
+    if world == 1:
+        return send_o, send_l
+    bufs = bufs if bufs is not None else {}
+    key = (world, n_max, S, r, D, o_u.device)
+    if bufs.get("key") != key:
+        bufs.clear()
+        bufs["key"] = key
+        bufs["o"] = o_u.new_empty((world * n_max, S, r, D))
+        bufs["l"] = lse_u.new_empty((world * n_max, S, r))
+    dist.all_gather_into_tensor(bufs["o"], send_o, group=group)
+    dist.all_gather_into_tensor(bufs["l"], send_l, group=group)
+    return bufs["o"], bufs["l"]
+
+
+def scatter_gathered(got_o: torch.Tensor, got_l: torch.Tensor, plan: list[list[int]], *, hkv: int,
+                     out: torch.Tensor, lse: torch.Tensor) -> None:
+    """Write all-gathered unit-major slots (``all_gather_units``) into row-major
+    ``out`` ``[B, S, Hq, 128]`` / ``lse`` ``[B, S, Hq]``: one scatter kernel each."""
+    n_max = max(len(p) for p in plan)
+    ids = slot_map(plan, n_max)
+    _move_units(got_o, out, ids, hkv=hkv, to_rows=True)
+    _move_units(got_l, lse, ids, hkv=hkv, to_rows=True)
+
+
+def gather_units_to_rows(o_u: torch.Tensor, lse_u: torch.Tensor, plan: list[list[int]], *, B: int, hkv: int,
+                         out: torch.Tensor | None = None, lse: torch.Tensor | None = None, group=None,
+                         _bufs: dict | None = None):
+    """Replicate every rank's unit-major outputs on every rank, in row-major form.
+
+    ``o_u`` ``[n, S, r, 128]`` / ``lse_u`` ``[n, S, r]``: this rank's units
+    (``plan[rank]`` in order) in their first slots, ``n`` at least the largest
+    share (slots past the rank's units are sent but never read).  One
+    ``all_gather_into_tensor`` per tensor, then one scatter kernel each into
+    ``out`` ``[B, S, Hq, 128]`` / ``lse`` ``[B, S, Hq]`` (allocated when None).
+    """
+    _, S, r, D = o_u.shape
+    if out is None:
+        out = o_u.new_empty((B, S, hkv * r, D))
+    if lse is None:
+        lse = lse_u.new_empty((B, S, hkv * r))
+    if max(len(p) for p in plan) == 0:
+        return out, lse
+    got_o, got_l = all_gather_units(o_u, lse_u, plan, group=group, bufs=_bufs)
+    scatter_gathered(got_o, got_l, plan, hkv=hkv, out=out, lse=lse)
+    return out, lse
+
+
 def gather_units(out: torch.Tensor, lse: torch.Tensor, plan: list[list[int]], *, hkv: int, group=None) -> None:
-    """All-gather the O/LSE slices of every rank's units into ``out`` / ``lse`` in place."""
-    world = dist.get_world_size(group)
+    """All-gather the O/LSE slices of every rank's units into ``out`` / ``lse`` in place
+    (replicated-input form: this rank's units are already in place in ``out`` / ``lse``)."""
     rank = dist.get_rank(group)
-    B, S, Hq, D = out.shape
-    r = Hq // hkv
     n_max = max(len(p) for p in plan)
     if n_max == 0:
         return
-    # staging slots past a rank's own units are sent but never read: no fill
-    stage_o = out.new_empty((n_max, S, r, D))
-    stage_l = lse.new_empty((n_max, S, r))
-    for i, u in enumerate(plan[rank]):
-        b, g = divmod(u, hkv)
-        stage_o[i].copy_(out[b, :, g * r:(g + 1) * r, :])
-        stage_l[i].copy_(lse[b, :, g * r:(g + 1) * r])
-    # one collective per tensor straight into a [world, n_max, ...] buffer
-    got_o = out.new_empty((world, n_max, S, r, D))
-    got_l = lse.new_empty((world, n_max, S, r))
-    dist.all_gather_into_tensor(got_o.view(world * n_max, S, r, D), stage_o, group=group)
-    dist.all_gather_into_tensor(got_l.view(world * n_max, S, r), stage_l, group=group)
-    for p in range(world):
-        if p == rank:
-            continue
-        for i, u in enumerate(plan[p]):
-            b, g = divmod(u, hkv)
-            out[b, :, g * r:(g + 1) * r, :].copy_(got_o[p][i])
-            lse[b, :, g * r:(g + 1) * r].copy_(got_l[p][i])
+    stage_o = take_units(out, plan[rank], hkv=hkv, slots=n_max)
+    stage_l = take_units(lse, plan[rank], hkv=hkv, slots=n_max)
+    gather_units_to_rows(stage_o, stage_l, plan, B=out.shape[0], hkv=hkv, out=out, lse=lse, group=group)
 
 
 def sharded_switch_gqa_prefill_forward(q, k, v, full_query_indices, local_query_indices, *, window_size=1024,
@@ -119,7 +260,7 @@ def sharded_switch_gqa_prefill_forward(q, k, v, full_query_indices, local_query_
     hkv = k.shape[2]
     if costs is None:
         fl, ll = _host_lists(full_query_indices, local_query_indices, query_counts, B)
-        costs = unit_costs(fl, ll, hkv=hkv, skv=k.shape[1], window=window_size)
+        costs = unit_costs(fl, ll, hkv=hkv, skv=k.shape[1], window=window_size, metadata=metadata)
     plan = plan_units(costs, world)
     mine = plan[rank]
     if compute is None:

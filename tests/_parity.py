@@ -39,10 +39,22 @@ def device_lists(full, local, device, B):
 
 
 def compare(O, LSE, O_ref, LSE_ref, rows=None, label=""):
-    """Compare on the rows where the oracle is defined (finite LSE)."""
+    """Compare with the oracle: within tolerance where it is defined (finite LSE),
+    and exactly ``O = NaN``, ``LSE = -inf`` on the rows where it has no legal key
+    (the reference's ``0/0`` and ``log2(0)``, ``swiattn_gqa_prefill.py:201-206``).
+
+    ``rows`` (bool, the shape of ``LSE``) restricts the comparison to a subset.
+    """
     O = O.float().cpu()
     LSE = LSE.float().cpu()
-    sel = torch.isfinite(LSE_ref) if rows is None else rows
+    O_ref = O_ref.float()
+    LSE_ref = LSE_ref.float()
+    scope = torch.ones_like(LSE_ref, dtype=torch.bool) if rows is None else rows
+    empty = scope & torch.isneginf(LSE_ref)
+    if empty.any():
+        assert torch.isneginf(LSE[empty]).all(), f"{label}: rows without a legal key must have LSE = -inf"
+        assert torch.isnan(O[empty]).all(), f"{label}: rows without a legal key must have O = NaN"
+    sel = scope & torch.isfinite(LSE_ref)
     assert sel.any(), f"{label}: nothing to compare"
     o_err = (O[sel] - O_ref[sel]).abs()
     l_err = (LSE[sel] - LSE_ref[sel]).abs()

@@ -128,3 +128,39 @@ def test_backward_context_parallel_rows(cuda_device):
     _close(dq, rq, "context-parallel rows dq")
     _close(dk, rk, "context-parallel rows dk")
     _close(dv, rv, "context-parallel rows dv")
+
+
+def test_backward_rows_without_keys(cuda_device):
+    # metadata rows with start == end (a sequence's first row) and start > end (its
+    # last row): the forward gives O = NaN and LSE = -inf there, and those rows
+    # carry no gradient; every gradient must stay finite
+    dev = cuda_device
+    g = torch.Generator().manual_seed(21)
+    cu = np.array([0, 200, 201, 520, 700])
+    S, Hq, Hkv, W = int(cu[-1]), 8, 2, 96
+    md_or = oracle_md.build_metadata(S, S, W, cu)
+    fs, ls, ce = (md_or[n].copy() for n in ("full_starts", "local_starts", "causal_ends"))
+    for s in cu[1:-1]:
+        ce[s] = s
+    for e in cu[2:]:
+        if e - 1 not in cu:
+            fs[e - 1] = ls[e - 1] = e
+            ce[e - 1] = e - 1
+    md_or = dict(md_or, full_starts=fs, local_starts=ls, causal_ends=ce)
+    md = _core.SwitchAttentionMetadata(**{n: torch.from_numpy(a).to(dev) for n, a in md_or.items()})
+    q = torch.randn(1, S, Hq, 128, generator=g).bfloat16()
+    k = torch.randn(1, S, Hkv, 128, generator=g).bfloat16()
+    v = torch.randn(1, S, Hkv, 128, generator=g).bfloat16()
+    dout = torch.randn(1, S, Hq, 128, generator=g).bfloat16()
+    mask = torch.rand(1, S, generator=g) < 0.4
+    full, local = lists_from_mask(mask)
+    fi, li = device_lists(full, local, dev, 1)
+    qd, kd, vd, dod = (t.to(dev) for t in (q, k, v, dout))
+    out, lse = _core.forward(qd, kd, vd, fi, li, metadata=md, window_size=W)
+    assert torch.isneginf(lse).any()
+    dq, dk, dv = switch_gqa_prefill_backward(qd, kd, vd, out, lse, dod, fi, li, metadata=md, window_size=W)
+    torch.cuda.synchronize()
+    rq, rk, rv = oracle_attn.prefill_backward(q, k, v, dout, full, local, window=W, metadata=md_or)
+    _close(dq, rq, "rows without keys dq")
+    _close(dk, rk, "rows without keys dk")
+    _close(dv, rv, "rows without keys dv")

@@ -143,3 +143,52 @@ def test_varlen_default_metadata_matches_fixed(cuda_device):
 def test_config2_full_parity(cuda_device):
     w = workloads.make_inputs(2, device=cuda_device)
     _run(w["q"], w["k"], w["v"], w["mask"], w["window"], "config2")
+
+
+@pytest.mark.parametrize("Sq,Skv,W,Hq,Hkv", [(900, 300, 64, 8, 2), (700, 500, 96, 8, 4), (1200, 200, 1, 4, 1)])
+def test_rows_without_keys_fixed_length(cuda_device, Sq, Skv, W, Hq, Hkv):
+    # local rows at t >= Skv + W - 1 have no legal key; they share units with
+    # rows that have keys (full rows, and local rows below the threshold)
+    q, k, v = _rand_qkv(1, Sq, Skv, Hq, Hkv, Sq * 3 + W, cuda_device)
+    mask = torch.rand(1, Sq, generator=torch.Generator().manual_seed(Sq + W)) < 0.5
+    full, local = lists_from_mask(mask)
+    assert (local[0] >= Skv + W - 1).any() and (local[0] < Skv + W - 1).any()
+    fi, li = device_lists(full, local, cuda_device, 1)
+    O, LSE = fixed.switch_gqa_prefill_forward(q, k, v, fi, li, window_size=W)
+    torch.cuda.synchronize()
+    O_ref, LSE_ref = oracle_subset(q, k, v, full, local, W)
+    empty = torch.isneginf(LSE_ref)
+    assert empty.any() and (~empty).any()
+    compare(O, LSE, O_ref, LSE_ref, label=f"Sq={Sq} Skv={Skv} W={W}")
+
+
+def test_rows_without_keys_varlen_metadata(cuda_device):
+    # metadata rows with start == end (first row of a sequence given no key) and
+    # start > end (last row of a sequence); the bounds stay monotone along the
+    # rows, as every metadata builder produces them
+    lengths = [130, 1, 257, 64, 300]
+    S = sum(lengths)
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    W = 48
+    q, k, v = _rand_qkv(1, S, S, 16, 4, 77, cuda_device)
+    ref_meta = oracle_meta.build_metadata(S, S, W, cu)
+    fs, ls, ce = (ref_meta[n].copy() for n in ("full_starts", "local_starts", "causal_ends"))
+    for s in cu[1:-1]:
+        ce[s] = s                      # start == end at a sequence start
+    for e in cu[2:]:
+        if e - 1 not in cu:
+            fs[e - 1] = ls[e - 1] = e  # start > end at a sequence end
+            ce[e - 1] = e - 1
+    for arr in (fs, ls, ce):
+        assert (np.diff(arr.astype(np.int64)) >= 0).all()
+    ref_meta = dict(ref_meta, full_starts=fs, local_starts=ls, causal_ends=ce)
+    meta = varlen.SwitchAttentionMetadata(**{n: torch.from_numpy(a).to(cuda_device) for n, a in ref_meta.items()})
+    for p_full in (0.0, 0.4, 1.0):
+        mask = torch.rand(1, S, generator=torch.Generator().manual_seed(int(p_full * 10))) < p_full
+        full, local = lists_from_mask(mask)
+        fi, li = device_lists(full, local, cuda_device, 1)
+        O, LSE = varlen.switch_gqa_prefill_forward(q, k, v, fi, li, metadata=meta, window_size=W)
+        torch.cuda.synchronize()
+        O_ref, LSE_ref = oracle_subset(q, k, v, full, local, W, metadata=ref_meta)
+        assert torch.isneginf(LSE_ref).any()
+        compare(O, LSE, O_ref, LSE_ref, label=f"varlen empty rows p_full={p_full}")

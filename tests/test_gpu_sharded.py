@@ -71,3 +71,71 @@ def test_sharded_forward_one_rank_nccl(cuda_device):
         assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(16, 4), (8, 8), (12, 2)])
+def test_unit_moves_round_trip(cuda_device, Hq, Hkv):
+    # swa_gather_units / swa_scatter_units: a rank's unit slices out of row-major
+    # tensors and back, bit for bit (O rows of r * 256 bytes, LSE rows of r * 4
+    # bytes: the 16-byte and the 4-byte word paths), padding slots skipped
+    from switchattentionkernels_b200 import sharded
+
+    g = torch.Generator().manual_seed(Hq + Hkv)
+    B, S = 3, 257
+    o = torch.randn(B, S, Hq, 128, generator=g).bfloat16().to(cuda_device)
+    l = torch.randn(B, S, Hq, generator=g).to(cuda_device)
+    units = [5 % (B * Hkv), 0, B * Hkv - 1]
+    o_u = sharded.take_units(o, units, hkv=Hkv, slots=5)
+    l_u = sharded.take_units(l, units, hkv=Hkv, slots=5)
+    r = Hq // Hkv
+    for i, u in enumerate(units):
+        b, gg = divmod(u, Hkv)
+        assert torch.equal(o_u[i], o[b, :, gg * r:(gg + 1) * r]) and torch.equal(l_u[i], l[b, :, gg * r:(gg + 1) * r])
+    o2 = torch.zeros_like(o)
+    l2 = torch.zeros_like(l)
+    sharded._move_units(o_u, o2, units + [-1, -1], hkv=Hkv, to_rows=True)
+    sharded._move_units(l_u, l2, units + [-1, -1], hkv=Hkv, to_rows=True)
+    torch.cuda.synchronize()
+    o_v, o2_v = o.view(B, S, Hkv, r, 128), o2.view(B, S, Hkv, r, 128)
+    for u in range(B * Hkv):
+        b, gg = divmod(u, Hkv)
+        if u in units:
+            assert torch.equal(o2_v[b, :, gg], o_v[b, :, gg])
+        else:
+            assert not o2_v[b, :, gg].any()
+
+
+def test_unit_major_forward_equals_row_major_slices(cuda_device):
+    # a rank's units held unit-major ([n, S, r, 128] q, [n, S, 1, 128] k / v, the units'
+    # mask rows) through the ordinary forward: bit-equal to those units' slices of the
+    # row-major launch; the gather (one rank: scatter only) rebuilds the whole result
+    from switchattentionkernels_b200 import build_switch_query_indices_batched, sharded
+
+    q, k, v, mask = _inputs(cuda_device, seed=23)
+    B, S, Hq, _ = q.shape
+    Hkv, W = k.shape[2], 150
+    r = Hq // Hkv
+    full, local, counts = build_switch_query_indices_batched(mask.to(cuda_device))
+    ref_o, ref_l = _core.forward(q, k, v, full, local, window_size=W, query_counts=counts)
+    fl, ll = lists_from_mask(mask)
+    plan = plan_units(unit_costs(fl, ll, hkv=Hkv, skv=S, window=W), 3)
+    n_max = max(len(p) for p in plan)
+    o_all = torch.empty((3 * n_max, S, r, 128), dtype=torch.bfloat16, device=cuda_device)
+    l_all = torch.empty((3 * n_max, S, r), dtype=torch.float32, device=cuda_device)
+    for rank, units in enumerate(plan):
+        q_u, k_u, v_u = (sharded.take_units(t, units, hkv=Hkv) for t in (q, k, v))
+        m_u = mask[torch.tensor([u // Hkv for u in units])].to(cuda_device)
+        f_u, l_u, c_u = build_switch_query_indices_batched(m_u)
+        o_u, lse_u = _core.forward(q_u, k_u, v_u, f_u, l_u, window_size=W, query_counts=c_u)
+        torch.cuda.synchronize()
+        for i, u in enumerate(units):
+            b, g = divmod(u, Hkv)
+            assert torch.equal(o_u[i], ref_o[b, :, g * r:(g + 1) * r]), f"unit {u} O"
+            assert torch.equal(lse_u[i], ref_l[b, :, g * r:(g + 1) * r]), f"unit {u} LSE"
+        o_all[rank * n_max:rank * n_max + len(units)] = o_u
+        l_all[rank * n_max:rank * n_max + len(units)] = lse_u
+    out = torch.full_like(q, float("nan"))
+    lse = torch.full((B, S, Hq), float("nan"), device=cuda_device)
+    sharded.scatter_gathered(o_all, l_all, plan, hkv=Hkv, out=out, lse=lse)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)

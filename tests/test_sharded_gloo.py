@@ -57,6 +57,22 @@ def _worker(rank, world, port, mode, result_q):
                 lse[b, :, g * r:(g + 1) * r] = L[b, :, g * r:(g + 1) * r]
             return out, lse
 
+        if mode == "unit_major":
+            # a rank holds only its units, unit-major: [n, S, r, 128] q and [n, S, 1, 128]
+            # k / v with each unit's batch lists; the forward over them is the ordinary
+            # forward with B = n, Hq = r, Hkv = 1
+            plan = sharded.plan_units(costs, world)
+            mine = plan[rank]
+            n_max = max(len(x) for x in plan)
+            q_u, k_u, v_u = (sharded.take_units(t, mine, hkv=hkv, slots=n_max) for t in (q, k, v))
+            fl = [full[u // hkv] for u in mine] + [np.zeros(0, np.int32)] * (n_max - len(mine))
+            ll = [local[u // hkv] for u in mine] + [np.arange(q.shape[1], dtype=np.int32)] * (n_max - len(mine))
+            O_u, L_u = oracle_attn.prefill_dense(q_u, k_u, v_u, fl, ll, window=W)
+            out, lse = sharded.gather_units_to_rows(O_u.bfloat16(), L_u, plan, B=q.shape[0], hkv=hkv)
+            O, L = oracle_attn.prefill_dense(q, k, v, full, local, window=W)
+            ok = bool(torch.equal(out, O.bfloat16()) and torch.equal(lse, L))
+            result_q.put((rank, "ok" if ok else "mismatch", plan))
+            return
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before its launch")
         out, lse, plan = sharded.sharded_switch_gqa_prefill_forward(
@@ -122,3 +138,30 @@ def test_failing_rank_surfaces_as_error_not_hang():
     res = _run("fail")
     assert res[1][0].startswith("error:RuntimeError")
     assert res[0][0].startswith("error:"), res  # the surviving rank's collective times out and raises
+
+
+def test_unit_costs_with_metadata_match_oracle_counts():
+    # packed sequences: costs come from the per-row bounds, not from raw positions
+    from oracle import metadata as oracle_meta
+
+    rng = np.random.default_rng(5)
+    cu = np.array([0, 40, 41, 150, 200])
+    S = int(cu[-1])
+    md = oracle_meta.build_metadata(S, S, 16, cu)
+    fl, ll = [], []
+    for b in range(2):
+        m = rng.random(S) < 0.3
+        fl.append(np.nonzero(m)[0].astype(np.int32))
+        ll.append(np.nonzero(~m)[0].astype(np.int32))
+    costs = sharded.unit_costs(fl, ll, hkv=3, skv=S, window=16, metadata=md)
+    plain = sharded.unit_costs(fl, ll, hkv=3, skv=S, window=16)
+    for b in range(2):
+        n = oracle_attn.legal_key_counts([fl[b]], [ll[b]], window=16, skv=S, metadata=md)
+        assert (costs[3 * b:3 * b + 3] == n).all()
+    assert (costs < plain).all()  # full rows of later sequences no longer count earlier sequences' keys
+
+
+def test_unit_major_shards_compose_to_the_whole_result():
+    res = _run("unit_major")
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    assert sorted(u for p in res[0][1] for u in p) == list(range(6))
