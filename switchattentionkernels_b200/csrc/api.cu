@@ -404,11 +404,14 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
         ++p.n_q3;
       }
     }
-    const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Skv), static_cast<uint64_t>(B)};
-    const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Skv) * Hkv * 256};
-    const uint32_t kb[4] = {64, 1, 128, 1};
-    if (!swa::make_bf16_map_sw128(&p.k_map, k, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
-    if (!swa::make_bf16_map_sw128(&p.v_map, v, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+    // one box per 128-key K or V tile: dims (64 columns, key, column half, KV head,
+    // batch), box {64, 128, 2, 1, 1}, so the tile lands as its two 64-column halves
+    // of 128 swizzled rows each (16 KB apart), in one TMA instruction
+    const uint64_t kd[5] = {64, static_cast<uint64_t>(Skv), 2, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(B)};
+    const uint64_t ks[4] = {static_cast<uint64_t>(Hkv) * 256, 128, 256, static_cast<uint64_t>(Skv) * Hkv * 256};
+    const uint32_t kb[5] = {64, 128, 2, 1, 1};
+    if (!swa::make_bf16_map_sw128(&p.k_map, k, 5, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+    if (!swa::make_bf16_map_sw128(&p.v_map, v, 5, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
   }
   p.idx[0] = full_idx;
   p.idx[1] = local_idx;

@@ -53,7 +53,7 @@ namespace {
 
 constexpr int kThreads = 576;
 constexpr int kBK = 128;            // keys per K/V tile
-constexpr int kStages = 4;          // K/V ring depth (each stage: one K or one V tile)
+constexpr int kStages = 5;          // K/V ring depth (each stage: one K or one V tile)
 constexpr int kSchedSlots = 4;      // work-unit ring depth
 constexpr uint32_t kTileBytes = 128 * 128 * 2;   // 32 KB: a 128x128 BF16 tile (2 swizzled halves)
 constexpr uint32_t kHalfBytes = 128 * 64 * 2;    // 16 KB: 128 rows x 64 columns
@@ -89,13 +89,11 @@ struct SmemLayout {
   static constexpr int n_bars = b_drain + 1;
   static constexpr uint32_t units = bars + ((n_bars * 8 + 63) / 64) * 64;
   static constexpr uint32_t misc = units + kSchedSlots * sizeof(Unit);
-  // row-max exchange [2 parity][2 tile][2 half][128] floats (4 KB), then the row-sum
-  // exchange [2 tile][2 half][128] floats (2 KB)
-  static constexpr uint32_t xchg = misc + 64;
-  static constexpr uint32_t total = xchg + 4096 + 2048;
+  static constexpr uint32_t total = misc + 64;
 };
 
 constexpr uint32_t kSmemBytes = SmemLayout::total + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB a CTA may use");
 
 struct RowBounds {
   int lo, hi;
@@ -469,16 +467,15 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         auto load_kv = [&](int j, int kv) -> bool {
           const uint32_t s = kv_it % kStages;
           if (!mbar_wait(&kv_empty[s], ((kv_it / kStages) & 1) ^ 1, abort_flag)) return false;
-          // lanes 0 and 1 each issue one 64-column half; lane 0 arms the barrier first.
-          // (With the failure-detection test hook, CTA 0 never arms or loads its second
-          // ring entry: the MMA warp's bounded wait on it runs out.)
+          // one TMA box per tile (both 64-column halves), issued by lane 0 after it
+          // arms the barrier.  (With the failure-detection test hook, CTA 0 never arms
+          // or loads its second ring entry: the MMA warp's bounded wait on it runs out.)
           const bool withhold = p.test_withhold != 0 && blockIdx.x == 0 && kv_it == 1;
-          if (lane == 0 && !withhold) mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
-          __syncwarp();
-          if (lane < 2 && !withhold) {
-            uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes + lane * kHalfBytes;
+          if (lane == 0 && !withhold) {
+            mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
+            uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes;
             const CUtensorMap* map = kv == 0 ? &p.k_map : &p.v_map;
-            tma_load_4d(dst, map, &kv_full[s], lane * 64, u.g, u.j0 * 64 + j * kBK, u.b);
+            tma_load_5d(dst, map, &kv_full[s], 0, u.j0 * 64 + j * kBK, 0, u.g, u.b);
           }
           __syncwarp();
           ++kv_it;
@@ -548,33 +545,41 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     };
     // Descriptors are built once; a ring entry's descriptor is the base plus the
     // entry offset in the 14-bit start-address field (bytes >> 4).
-    const uint64_t q_desc[2] = {make_smem_desc_sw128(q_addr[0], 16, 1024), make_smem_desc_sw128(q_addr[1], 16, 1024)};
+    // The Q descriptors of all eight K = 16 steps of both tiles are fixed; a K ring
+    // entry's eight are made when its load is waited for, off the path from a P
+    // chunk to the next S MMA.
+    uint64_t qd[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) qd[i][kk] = make_smem_desc_sw128(q_addr[i], 16, 1024) + k128_step_offset(kk);
     const uint64_t k_desc0 = make_smem_desc_sw128(kv_addr, 16, 1024);
     const uint64_t v_desc0 = make_smem_desc_sw128(kv_addr, kHalfBytes, 1024);
-    auto issue_s = [&](int i, uint32_t kstage) {
-      umma_ss_k128_warp(tm_s[i], q_desc[i], k_desc0 + kstage * (kTileBytes >> 4), idesc_s);
-    };
-    // P V for one tile in two chunks: chunk c covers keys [32 c, +32) of each key
-    // half (keys 64 h + 32 c .. +31: P columns 64 h + 16 c .., V rows 2048-byte
-    // steps 4 h + 2 c ..), published by the softmax before it exponentiates chunk c + 1.
-    auto issue_pv = [&](int i, uint32_t vstage, bool accumulate) -> bool {
-      const uint64_t vb = v_desc0 + vstage * (kTileBytes >> 4);
+    uint64_t kd[8];
+    auto k_descs = [&](uint32_t kstage) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        if (!mbar_wait(&p_chunk[2 * i + c], p_use[i] & 1, abort_flag)) { ok = false; return false; }
-        tc_fence_after();
-        umma_ts_k32_warp(tm_o[i], tm_s[i] + 16 * c, vb + (2 * c) * 128, idesc_o, (accumulate || c > 0) ? 1u : 0u);
-        umma_ts_k32_warp(tm_o[i], tm_s[i] + 64 + 16 * c, vb + (4 + 2 * c) * 128, idesc_o, 1u);
-      }
-      ++p_use[i];
-      return true;
+      for (int kk = 0; kk < 8; ++kk) kd[kk] = k_desc0 + kstage * (kTileBytes >> 4) + k128_step_offset(kk);
     };
-    // S MMAs of one key step for tile i; after the unit's last one, Q_i is released
-    // to the producer (the commit arrives once these MMAs have read it).
-    auto issue_s_step = [&](int i, uint32_t kstage, bool last_of_unit) {
-      issue_s(i, kstage);
+    auto issue_s = [&](int i) { umma_ss8_warp(tm_s[i], qd[i], kd, idesc_s); };
+    // P V for one tile in two chunks: chunk c covers keys [64 c, 64 c + 64) (P columns
+    // 32 c .. 32 c + 31, V rows in 2048-byte steps of 16 keys from 4 c), published by
+    // the softmax before it exponentiates chunk c + 1.
+    // S MMAs of one key step for tile i (K ring entry of the last k_descs call); after
+    // the unit's last one, Q_i is released to the producer (the commit arrives once
+    // these MMAs have read it).
+    auto issue_s_step = [&](int i, bool last_of_unit) {
+      issue_s(i);
       tc_commit_warp(&s_full[i]);
       if (last_of_unit) tc_commit_warp(&q_empty[i]);
+    };
+    // P V chunk c of tile i (waits for the chunk's P).
+    auto issue_pv_chunk = [&](int i, int c, uint64_t vb, bool accumulate) -> bool {
+      if (!mbar_wait(&p_chunk[2 * i + c], p_use[i] & 1, abort_flag)) { ok = false; return false; }
+      tc_fence_after();
+      umma_ts_k32_warp(tm_o[i], tm_s[i] + 32 * c, vb + (4 * c) * 128, idesc_o, (accumulate || c > 0) ? 1u : 0u);
+      umma_ts_k32_warp(tm_o[i], tm_s[i] + 32 * c + 16, vb + (4 * c + 2) * 128, idesc_o, 1u);
+      if (c == 1) ++p_use[i];
+      return true;
     };
 
     Unit cur;
@@ -585,14 +590,15 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       ok = ok && mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag);
       if (ok) {
         ++q_use[0];
+        k_descs(ks);
         tc_fence_after();
-        issue_s_step(0, ks, cur.n == 1);
+        issue_s_step(0, cur.n == 1);
       }
       ok = ok && mbar_wait(&q_full[1], q_use[1] & 1, abort_flag);
       if (ok) {
         ++q_use[1];
         tc_fence_after();
-        issue_s_step(1, ks, cur.n == 1);
+        issue_s_step(1, cur.n == 1);
         tc_commit_warp(&kv_empty[ks]);
         ++kv_it;
       }
@@ -602,40 +608,48 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       // invariant: S_0(j), S_1(j) of `cur` are issued.  Inside a unit the order is
       // PV_0(j), S_0(j+1), PV_1(j), S_1(j+1); at a unit's last step both P V MMAs go
       // first, then the next unit's S MMAs (S_i(0) overwrites the columns that hold
-      // P_i of this step).
+      // P_i of this step).  The waits for V_j and K_{j+1} (normally landed long ago)
+      // come first, so that from the last P chunk of a tile to its next S MMA the
+      // warp only issues MMAs.
       const bool last = j == cur.n - 1;
       const uint32_t vs = kv_it % kStages;
       tr.ev(1, step);
       if (!mbar_wait(&kv_full[vs], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
       ++kv_it;
+      uint32_t ks = 0;
+      if (!last) {
+        ks = kv_it % kStages;
+        if (!mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
+        ++kv_it;
+        k_descs(ks);
+      }
+      tc_fence_after();
       tr.ev(2, step);
       if (j == 0) {
         if (!mbar_wait(&o_empty[0], (o_use[0] & 1) ^ 1, abort_flag)) { ok = false; break; }
         ++o_use[0];
       }
-      if (!issue_pv(0, vs, j > 0)) break;
+      const uint64_t vb = v_desc0 + vs * (kTileBytes >> 4);
+      if (!issue_pv_chunk(0, 0, vb, j > 0)) break;
       tr.ev(3, step);
-      uint32_t ks = 0;
+      if (!issue_pv_chunk(0, 1, vb, j > 0)) break;
       if (last) {
         tc_commit_warp(&o_full[0]);
       } else {
-        ks = kv_it % kStages;
-        if (!mbar_wait(&kv_full[ks], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
-        ++kv_it;
-        tc_fence_after();
-        tr.ev(4, step);
-        issue_s_step(0, ks, j + 1 == cur.n - 1);
+        issue_s_step(0, j + 1 == cur.n - 1);
       }
+      tr.ev(4, step);
       if (j == 0) {
         if (!mbar_wait(&o_empty[1], (o_use[1] & 1) ^ 1, abort_flag)) { ok = false; break; }
         ++o_use[1];
       }
-      if (!issue_pv(1, vs, j > 0)) break;
-      tr.ev(5, step);
+      if (!issue_pv_chunk(1, 0, vb, j > 0)) break;
+      if (!issue_pv_chunk(1, 1, vb, j > 0)) break;
       tc_commit_warp(&kv_empty[vs]);
       if (!last) {
-        issue_s_step(1, ks, j + 1 == cur.n - 1);
+        issue_s_step(1, j + 1 == cur.n - 1);
         tc_commit_warp(&kv_empty[ks]);
+        tr.ev(5, step);
         ++j;
       } else {
         tc_commit_warp(&o_full[1]);
@@ -650,14 +664,15 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (!mbar_wait(&kv_full[k0s], (kv_it / kStages) & 1, abort_flag)) { ok = false; break; }
         tr.ev(9, step);
         ++kv_it;
+        k_descs(k0s);
         tc_fence_after();
-        issue_s_step(0, k0s, cur.n == 1);
+        issue_s_step(0, cur.n == 1);
         tr.ev(17, step);
         if (!mbar_wait(&q_full[1], q_use[1] & 1, abort_flag)) { ok = false; break; }
         tr.ev(18, step);
         ++q_use[1];
         tc_fence_after();
-        issue_s_step(1, k0s, cur.n == 1);
+        issue_s_step(1, cur.n == 1);
         tc_commit_warp(&kv_empty[k0s]);
       }
       tr.ev(6, step);
@@ -670,20 +685,21 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    // Four warpgroups: tile = (warp - 2) / 8, column half = ((warp - 2) / 4) % 2.
-    // Thread (tile, half, t) owns keys [64 * half, 64 * half + 64) of row t of its
-    // tile.  A warp may only access the TMEM lane quarter (warp % 4), so each group
-    // of four consecutive warps covers lanes 0..127.  The two threads of a row
-    // exchange their partial row maxima through shared memory every key step (named
-    // barrier 1 + tile over the tile's 256 threads) and their partial row sums once
-    // per unit, at the epilogue.
+    // Warps 2-17: tile = (warp - 2) / 8.  A warp may only access its TMEM lane
+    // quarter warp % 4; the two warps of a tile with the same quarter take its lanes
+    // 0..15 and 16..31 (block hb).  Within a warp, thread l (< 16) and thread l + 16
+    // share row t = 32 q + 16 hb + l (16-lane TMEM loads): thread half 0 holds keys
+    // [0, 32) and [64, 96) of every key tile, half 1 keys [32, 64) and [96, 128).
+    // The row max of a key step and the row sum of a unit are exchanged between the
+    // two threads of a row with one warp shuffle: no shared memory, no barrier.
     const int grp = (warp - 2) >> 2;             // 0..3
     const int tile = grp >> 1;
-    const int half = grp & 1;
-    const int lane_base = (warp & 3) * 32;
-    const int t = lane_base + lane;              // row within the tile = TMEM lane
+    const int hb = grp & 1;
+    const int half = lane >> 4;
+    const int lane_base = (warp & 3) * 32 + 16 * hb;
+    const int t = lane_base + (lane & 15);       // row within the tile = TMEM lane
     const uint32_t tm_s = tmem + 128 * tile + (static_cast<uint32_t>(lane_base) << 16);
-    const uint32_t tm_o = tmem + 256 + 128 * tile + 64 * half + (static_cast<uint32_t>(lane_base) << 16);
+    const uint32_t tm_o = tmem + 256 + 128 * tile + (static_cast<uint32_t>(lane_base) << 16);
     const int R = 128 * tile + t;                  // row within the unit
     const int slot_in_unit = R / p.rp;
     const int head_in_group_off = R % p.rp;
@@ -691,10 +707,6 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     const float sl2 = p.scale_log2;
     const float m_init = -1073741824.0f * sl2;     // reference initial row max (-2^30), scaled
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    float* xmax = reinterpret_cast<float*>(smem + SmemLayout::xchg);          // [2 parity][2 tile][2 half][128]
-    float* xsum = reinterpret_cast<float*>(smem + SmemLayout::xchg + 4096);   // [2 tile][2 half][128]
-    static_assert(SmemLayout::total - SmemLayout::xchg == 4096 + 2048, "exchange buffer sizes");
-    const int bar_id = 1 + tile;
     uint32_t s_use = 0, o_use = 0;
     bool ok = true;
     Tracer tr(t == 0 && half == 0 ? 1 + tile : -1);
@@ -716,40 +728,46 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       if (u.n == 0) {
         if (valid_row) {
           const uint32_t nan_pair = 0x7FC07FC0u;
-          uint4* dst = reinterpret_cast<uint4*>(p.out + orow * 128 + 64 * half);
+          const uint4 nan4 = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
+          uint4* dst0 = reinterpret_cast<uint4*>(p.out + orow * 128 + 32 * half);
+          uint4* dst1 = reinterpret_cast<uint4*>(p.out + orow * 128 + 64 + 32 * half);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) dst[c] = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
+          for (int c = 0; c < 4; ++c) {
+            dst0[c] = nan4;
+            dst1[c] = nan4;
+          }
           if (half == 0) p.lse[orow] = -INFINITY;
         }
         continue;
       }
       float m = m_init;
-      float l = 0.0f;   // partial row sum over this thread's key half
+      float l = 0.0f;   // partial row sum over this thread's keys
       for (int j = 0; j < u.n; ++j) {
         tr.ev(10, s_use + 1);
         if (!mbar_wait(&s_full[tile], s_use & 1, abort_flag)) { ok = false; break; }
         tr.ev(11, s_use + 1);
         tc_fence_after();
         uint32_t sr[64];
-        tmem_ld_x32(tm_s + 64 * half, sr + 0);
-        tmem_ld_x32(tm_s + 64 * half + 32, sr + 32);
+        tmem_ld_16x2_x32(tm_s, sr + 0);        // keys 32 half + [0, 32)
+        tmem_ld_16x2_x32(tm_s + 64, sr + 32);  // keys 64 + 32 half + [0, 32)
         tmem_ld_wait();
         reg_fence32(sr + 0);
         reg_fence32(sr + 32);
         float* s = reinterpret_cast<float*>(sr);
-        const int k0 = u.j0 * 64 + j * kBK + 64 * half;
-        const bool need_mask = !(rb.lo <= k0 && k0 + 64 <= rb.hi);
-        // legal keys of this row in [k0, k0 + 64) form [k0 + a, k0 + b): two 32-bit
-        // masks, then one predicated select per entry
-        auto key_mask = [&](int word) -> uint32_t {
-          const int a = min(max(rb.lo - k0, 0), 64);
-          const int b = max(min(rb.hi - k0, 64), a);
-          const uint64_t hi_bits = b >= 64 ? ~0ull : ((1ull << b) - 1);
-          const uint64_t valid = hi_bits & ~((a >= 64) ? ~0ull : ((1ull << a) - 1));
-          return static_cast<uint32_t>(valid >> (32 * word));
+        const int k0 = u.j0 * 64 + j * kBK;
+        const bool need_mask = !(rb.lo <= k0 && k0 + kBK <= rb.hi);
+        // legal keys among the 32 keys from `base`: one 32-bit mask, then one
+        // predicated select per entry
+        auto key_mask = [&](int base) -> uint32_t {
+          const int a = min(max(rb.lo - base, 0), 32);
+          const int b = max(min(rb.hi - base, 32), a);
+          const uint32_t hi_bits = b >= 32 ? ~0u : ((1u << b) - 1u);
+          const uint32_t lo_bits = a >= 32 ? ~0u : ((1u << a) - 1u);
+          return hi_bits & ~lo_bits;
         };
+        const int kb0 = k0 + 32 * half, kb1 = k0 + 64 + 32 * half;
         if (need_mask) {
-          const uint32_t v0 = key_mask(0), v1 = key_mask(1);
+          const uint32_t v0 = key_mask(kb0), v1 = key_mask(kb1);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             s[e] = select_or_neg_inf(v0, 1u << e, s[e]);
@@ -757,14 +775,10 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           }
         }
         tr.ev(12, s_use + 1);
-        // partial max, exchanged with the partner thread of the same row
+        // partial max, exchanged with the thread of the same row (lane ^ 16)
         const float pmax = row_max64(s);
-        tr.ev(14, s_use + 1);
-        float* xm = xmax + (s_use & 1) * 512 + tile * 256;
-        xm[half * 128 + t] = pmax;
-        named_bar_sync(bar_id, 256);
+        const float m_tile = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16)) * sl2;
         tr.ev(15, s_use + 1);
-        const float m_tile = fmaxf(pmax, xm[(half ^ 1) * 128 + t]) * sl2;
         ++s_use;
         bool rescale = false;
         float alpha = 1.0f;
@@ -777,38 +791,39 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           rescale = true;
         }
         if (__any_sync(0xffffffffu, rescale)) {
-          // this thread's half of the O row (P V of earlier key tiles, all complete)
-          // *= alpha, before any P of this key step is published
+          // this thread's columns of the O row (P V of earlier key tiles, all
+          // complete) *= alpha, before any P of this key step is published
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t orr[16];
-            tmem_ld_x16(tm_o + 16 * c, orr);
+            const uint32_t ta = tm_o + (c >> 1) * 64 + (c & 1) * 32;  // columns [32 c', +32) of the two halves
+            tmem_ld_16x2_x16(ta, orr);
             tmem_ld_wait();
             reg_fence16(orr);
 #pragma unroll
             for (int e = 0; e < 16; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st_x16(tm_o + 16 * c, orr);
+            tmem_st_16x2_x16(ta, orr);
           }
         }
         const uint64_t negm2 = f2_pack(-m, -m);
         uint64_t acc[4] = {0, 0, 0, 0};
-        // two chunks of 32 keys; each is published as soon as it is in TMEM, so the
-        // P V MMAs of chunk 0 run while chunk 1 is exponentiated.  Chunk 1's scores
-        // are read from TMEM again (keys 32..63 of this half, which no P store
-        // reaches: P of key half h goes to columns 64 h .. 64 h + 31), so the 32
-        // registers that held them are free while chunk 0 is exponentiated.
+        // chunk c = keys [64 c, 64 c + 64) of the tile (this thread: 32 of them),
+        // P pairs into columns 32 c + 16 half .. + 15, published as soon as it is in
+        // TMEM so the P V MMAs of chunk 0 run while chunk 1 is exponentiated.
+        // Chunk 1's scores are read from TMEM again (columns 64..127, which chunk
+        // 0's P does not reach), so their registers are free meanwhile.
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
           uint32_t sr1[32];
           const float* sc = s;
           if (c == 1) {
-            tmem_ld_x32(tm_s + 64 * half + 32, sr1);
+            tmem_ld_16x2_x32(tm_s + 64, sr1);
             tmem_ld_wait();
             reg_fence32(sr1);
             float* s1 = reinterpret_cast<float*>(sr1);
             if (need_mask) {
-              const uint32_t v1 = key_mask(1);
+              const uint32_t v1 = key_mask(kb1);
 #pragma unroll
               for (int e = 0; e < 32; ++e) s1[e] = select_or_neg_inf(v1, 1u << e, s1[e]);
             }
@@ -830,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
             acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
             pk[qq] = pack_bf16x2(p0, p1);
           }
-          tmem_st_x16(tm_s + 64 * half + 16 * c, pk);
+          tmem_st_16x2_x16(tm_s + 32 * c, pk);
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(&p_chunk[2 * tile + c]);
@@ -846,17 +861,16 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       }
       if (!ok) break;
       // epilogue: O / l -> BF16 written straight from registers with coalesced
-      // stores: each thread packs its 64 columns (eight 16-byte chunks), the eight
-      // lanes of a group transpose their 8 x 8 chunks with three xor butterflies
-      // (lane L then holds chunk L % 8 of the group's eight rows), so one store
-      // instruction writes four whole 128-byte row halves.  LSE in log2 units.
+      // stores: each thread packs its 64 columns (eight 16-byte chunks: columns
+      // 32 half + 8 j for j < 4, 64 + 32 half + 8 (j - 4) for j >= 4), the eight lanes
+      // of a lane group transpose their 8 x 8 chunks with three xor butterflies (lane
+      // L then holds chunk L % 8 of the group's eight rows), so one store instruction
+      // writes two 64-byte pieces of four rows.  LSE in log2 units.
       tr.ev(20, s_use);
-      xsum[tile * 256 + half * 128 + t] = l;
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
       if (!mbar_wait(&o_full[tile], o_use & 1, abort_flag)) { ok = false; break; }
       ++o_use;
       tr.ev(21, s_use);
-      named_bar_sync(bar_id, 256);
-      l += xsum[tile * 256 + (half ^ 1) * 128 + t];
       // A row whose key range is empty (metadata start >= end, or a local row at
       // t >= Skv + W - 1) has row sum 0 in the reference (swiattn_gqa_prefill.py:201-206,
       // swiattn_gqa_prefill_varlen.py:236-241): O = 0/0 and LSE = log2(0) + m.
@@ -864,11 +878,11 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       const float inv_l = no_keys ? __int_as_float(0x7FC00000) : 1.0f / l;
       if (half == 0 && valid_row) p.lse[orow] = no_keys ? -INFINITY : lg2_approx(l) + m;
       tc_fence_after();
-      uint32_t ch[8][4];  // ch[j]: chunk j (columns 8 j .. 8 j + 7 of this half) as BF16 pairs
+      uint32_t ch[8][4];  // ch[j]: chunk j of this thread's columns as BF16 pairs
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t orr[32];
-        tmem_ld_x32(tm_o + 32 * c, orr);
+        tmem_ld_16x2_x32(tm_o + 64 * c, orr);
         tmem_ld_wait();
         reg_fence32(orr);
 #pragma unroll
@@ -898,23 +912,17 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         }
       }
       const int64_t my_row = valid_row ? orow : -1;
+      const int my_chunk = lane & 7;
+      const int col = my_chunk < 4 ? 32 * half + 8 * my_chunk : 64 + 32 * half + 8 * (my_chunk - 4);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int src = (lane & ~7) + j;  // lane holding row j of this group
         const int64_t grow = __shfl_sync(0xffffffffu, my_row, src);
         if (grow >= 0)
-          *reinterpret_cast<uint4*>(p.out + grow * 128 + 64 * half + 8 * (lane & 7)) =
-              make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
+          *reinterpret_cast<uint4*>(p.out + grow * 128 + col) = make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
       }
       tr.ev(22, s_use);
     }
-    // Abort path only: this warp left the loop on a timed-out (or flagged) wait.  Its
-    // partner warps of the tile may sit in the row-exchange or epilogue barrier that
-    // this warp will not reach; one arrival completes that phase for them, and after
-    // any phase of that barrier the next blocking step of every softmax warp is a
-    // bounded mbarrier wait, which sees the abort flag.  An arrival that no warp
-    // waits for is harmless: the barrier is not used again before the CTA exits.
-    if (__any_sync(0xffffffffu, *abort_flag != 0)) named_bar_arrive(bar_id, 256);
   }
 
   // ------------------------------------------------------------------ teardown
@@ -947,6 +955,15 @@ cudaError_t launch_prefill(const PrefillParams& params, int num_sms, cudaStream_
 }
 
 uint32_t prefill_smem_bytes() { return kSmemBytes; }
+
+#ifdef SWA_TRACE
+// Points the cycle tracer of CTA 0 at a device buffer of 5 x 2 x 8192 uint64
+// (one region per recorder) or, with nullptr, turns it off.
+extern "C" int swa_dev_trace_set(void* buf) {
+  unsigned long long* ptr = static_cast<unsigned long long*>(buf);
+  return static_cast<int>(cudaMemcpyToSymbol(g_swa_trace, &ptr, sizeof(ptr)));
+}
+#endif
 
 #ifdef SWA_CYCLES
 // Copies the per-CTA cycle counts of the last launch (n <= 1024) to host memory.

@@ -122,6 +122,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
 // L2 policy that keeps lines resident ahead of streaming data (evict-last).
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t pol;
@@ -219,6 +228,32 @@ __device__ __forceinline__ void umma_ss_k128_warp(uint32_t d_tmem, uint64_t a_de
       "l"(a_desc), "l"(b_desc), "r"(idesc)
       : "memory");
 }
+
+// Eight back-to-back SS MMAs over K = 128 with all sixteen descriptors given in
+// registers (a[k], b[k]: step k's operands), so the first MMA issues right after
+// the elect and the issuing warp does no address arithmetic on the critical path.
+// The first step overwrites D.
+__device__ __forceinline__ void umma_ss8_warp(uint32_t d_tmem, const uint64_t* a, const uint64_t* b, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p0, p1;\n\t"
+      "setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %9, %17, p0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %10, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %11, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %12, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %13, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %14, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %15, %17, p1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %16, %17, p1;\n\t}" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]),
+      "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(idesc)
+      : "memory");
+}
+
+// Start-address offsets (descriptor units of 16 bytes) of the eight K = 16 steps of a
+// 128-column K-major tile stored as two 64-column swizzled halves 16 KB apart.
+__host__ __device__ constexpr uint32_t k128_step_offset(int k) { return (k >> 2) * 1024 + (k & 3) * 2; }
 
 // As umma_ss_k128_warp with an N = 64 B operand whose two 64-column halves lie
 // 8192 bytes apart (a 64-row swizzled tile); A's halves lie 16384 bytes apart.
@@ -359,6 +394,36 @@ __device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t* r) {
                : "memory");
 }
 
+// 16-lane forms (".16x32bx2"): the warp accesses 16 TMEM lanes (the lane field of
+// taddr: its quarter's lane 0 or 16); threads 0-15 get columns [c, c + n) of lanes
+// 0..15, threads 16-31 columns [c + n, c + 2n) of the same lanes (second access at
+// the immediate column offset n).  So the two threads t and t + 16 of a warp share
+// one row and hold adjacent column ranges of it.
+__device__ __forceinline__ void tmem_ld_16x2_x32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], 32;"
+      : SWA_R8(0), SWA_R8(8), SWA_R8(16), SWA_R8(24)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_16x2_x16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16], 16;"
+      : SWA_R8(0), SWA_R8(8)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st_16x2_x16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 16, "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      SWA_W8(0), SWA_W8(8)
+      : "memory");
+}
+
 #undef SWA_R8
 #undef SWA_W8
 
@@ -386,6 +451,21 @@ __device__ __forceinline__ void named_bar_arrive(int id, int count) {
 __device__ __forceinline__ void reg_fence16(uint32_t* r) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// Register reallocation between warpgroups: every warp of a warpgroup executes the
+// same call.  dealloc lowers this warpgroup's per-thread registers to N (returning
+// the rest to the CTA's pool); alloc raises them to N, waiting until the pool has
+// them.  The pool is what the CTA was launched with (threads x registers per
+// thread at launch), so the warpgroups' final counts must add up to at most that.
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------

@@ -29,7 +29,7 @@ struct __align__(64) PrefillParams {
   // positions x rp heads in one TMA box (L < n_q3; n_q3 = log2(128 / rp), rp <= 64)
   CUtensorMap q_runs[kMaxQRunMaps];
   int n_q3;
-  CUtensorMap k_map;  // 4-D {128, Hkv, Skv, B}, box {64, 1, 128, 1}, 128B swizzle
+  CUtensorMap k_map;  // 5-D {64, Skv, 2, Hkv, B} (column half as a dimension), box {64, 128, 2, 1, 1}, 128B swizzle
   CUtensorMap v_map;
   const int32_t* idx[2];       // routed positions per branch: [B, idx_stride]
   int idx_stride[2];
