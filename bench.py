@@ -76,6 +76,9 @@ def parse_args():
                     help="instead of the default line: every rank computes its own 4 sequences (weak scaling)")
     ap.add_argument("--steady-seconds", type=float, default=2.0,
                     help="length of the back-to-back steady-state block after the timed steps")
+    ap.add_argument("--workload", type=int, choices=[3, 5], default=CONFIG_ID,
+                    help="default line's workload: 3 (the headline) or 5 (two 131072-token sequences, Hkv 4)")
+    ap.add_argument("--p-full", type=float, default=None, help="with --workload 5: routing density p_full")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the N=1 extras (standard-layout kernel, backward and decode steps)")
     ap.add_argument("--backward", action="store_true",
@@ -196,14 +199,17 @@ def unit_flops(mask: np.ndarray, window: int, hq: int, skv: int) -> float:
     return workloads.effective_flops(mask, window, skv, hq)
 
 
-def config3_dict(world: int) -> dict:
+def config3_dict(world: int, cfg_id: int = CONFIG_ID, p_full: float | None = None) -> dict:
     """``config`` of the default line: the same keys and values in both arms."""
-    cfg = workloads.CONFIGS[CONFIG_ID]
+    cfg = workloads.CONFIGS[cfg_id]
+    p = cfg.p_full if p_full is None else p_full
+    gib = (cfg.B * cfg.S * (cfg.Hq + 2 * cfg.Hkv) * 128 * 2) / 2**30
     return {"workload": cfg.name, "B": cfg.B, "S": cfg.S, "Hq": cfg.Hq, "Hkv": cfg.Hkv, "head_dim": 128,
-            "window": cfg.window, "p_full": cfg.p_full, "routing": "markov(switch=0.02)",
+            "window": cfg.window, "p_full": p,
+            "routing": "markov(switch=0.02)" if cfg.markov_switch is not None else "bernoulli",
             "units": cfg.B * cfg.Hkv,
             "parallelism": f"(batch, KV group) units sharded over {world} rank(s), LPT on legal entries",
-            "l2": "inputs larger than L2 (q/k/v 1.5 GiB)"}
+            "l2": f"inputs larger than L2 (q/k/v {gib:.1f} GiB)"}
 
 
 # --------------------------------------------------------------------------- CPU baseline (oracle)
@@ -734,7 +740,7 @@ def run_default(args, world, rank, local_rank):
         return t.tolist()
 
     # every rank draws the same batch and keeps its own units
-    w = workloads.make_inputs(CONFIG_ID, device=dev, on_device=True)
+    w = workloads.make_inputs(args.workload, device=dev, on_device=True, p_full=args.p_full)
     q, k, v, mask_cpu, W = w["q"], w["k"], w["v"], w["mask"], w["window"]
     B, S, Hq, D = q.shape
     Hkv = k.shape[2]
@@ -787,7 +793,39 @@ def run_default(args, world, rank, local_rank):
     clock_info = clocks.stop()
     pf_avg = statistics.fmean([a.elapsed_time(b) for a, b in pf_events]) if pf_events else 0.0
 
-    # the same step with a replicated result: all-gather of every rank's O / LSE + scatter
+    # the same step with a replicated result, fused: the kernel's epilogue writes every
+    # row into every rank's row-major buffer (symmetric memory, over NVLink)
+    rep = sharded.ReplicaBuffers(B, S, Hq, device=dev)
+    f_events = []
+
+    def step_fused(record=False):
+        if n == 0:
+            rep.barrier()
+            rep.barrier()
+            return
+        full, local, counts = build_switch_query_indices_batched(mask_u)
+        e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) if record else None
+        rep.barrier()  # nobody still reads the buffers' previous contents
+        if e:
+            e[0].record(stream)
+        sharded.forward_units_replicated(q_u, k_u, v_u, full, local, counts, mine, rep, hkv=Hkv, window_size=W,
+                                         barrier=False)
+        if e:
+            e[1].record(stream)
+            f_events.append(e)
+        rep.barrier()  # every rank's rows have landed everywhere
+
+    for _ in range(2):
+        step_fused()
+    torch.cuda.synchronize()
+    barrier()
+    fu_ms = time_steps(lambda: step_fused(record=True), K, stream)
+    barrier()
+    fu_kernel = statistics.fmean([a.elapsed_time(b) for a, b in f_events]) if f_events else 0.0
+    del rep
+
+    # the same with the replication after the launch: NCCL all-gather of every rank's
+    # unit-major O / LSE + the scatter kernel
     out_all = torch.empty((B, S, Hq, D), dtype=torch.bfloat16, device=dev)
     lse_all = torch.empty((B, S, Hq), dtype=torch.float32, device=dev)
     gbufs = {}
@@ -891,7 +929,7 @@ def run_default(args, world, rank, local_rank):
 
     # N = 1 extras: the row-major layout of the single-GPU API, one backward and one decode step
     extras = {}
-    if not multi and not args.no_extras:
+    if not multi and not args.no_extras and args.workload == CONFIG_ID:
         from switchattentionkernels_b200.backward import switch_gqa_prefill_backward
         from switchattentionkernels_b200.decode import switch_gqa_decode_forward
 
@@ -961,14 +999,14 @@ def run_default(args, world, rank, local_rank):
         del dq_, dk_, dv_
 
     e2e_ms = e2e["ms"] if e2e else 0.0
-    mx = reduce([ms, g_ms, coll_ms, scat_ms, st_ms, e2e_ms, pf_avg], dist.ReduceOp.MAX)
+    mx = reduce([ms, g_ms, coll_ms, scat_ms, st_ms, e2e_ms, pf_avg, fu_ms, fu_kernel], dist.ReduceOp.MAX)
     sm = reduce([flops_rank, pf_avg, float(e2e["h2d"] if e2e else 0), float(e2e["d2h"] if e2e else 0)],
                 dist.ReduceOp.SUM)
-    ms_max, g_ms_max, coll_max, scat_max, st_max, e2e_max, pf_max = mx
+    ms_max, g_ms_max, coll_max, scat_max, st_max, e2e_max, pf_max, fu_max, fu_kernel_max = mx
     flops_sum, pf_sum, h2d_sum, d2h_sum = sm
 
     cpu = None
-    if rank == 0 and not multi and not args.no_cpu_baseline:
+    if rank == 0 and not multi and not args.no_cpu_baseline and args.workload == CONFIG_ID:
         # rank 0 at N=1 only: the CPU restatement on a bounded sample of the same workload
         cpu_inputs = {"q_cpu": q.cpu(), "k_cpu": k.cpu(), "v_cpu": v.cpu(), "mask": mask_np, "window": W}
         cpu = cpu_oracle_sample(cpu_inputs, args.cpu_seconds)
@@ -981,17 +1019,23 @@ def run_default(args, world, rank, local_rank):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": WU,
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic", "config": config3_dict(world),
+            "dtype": "bf16", "data": "synthetic", "config": config3_dict(world, args.workload, w["p_full"]),
             "units_per_rank": [len(p) for p in plan],
             "layout": "each rank holds its units unit-major: q [units, S, Hq/Hkv, 128], k / v [units, S, 1, 128]",
             "effective_tflop_per_step": flops_total / 1e12,
             "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_burst, "unit": UNIT,
-                         "frac": achieved / peak_burst, "traffic": profile_traffic(config3_dict(1)["workload"]),
+                         "frac": achieved / peak_burst, "traffic": profile_traffic(config3_dict(1)["workload"]) if args.workload == CONFIG_ID else None,
                          "kernel": "switch_prefill_kernel", "kernel_ms": pf_max,
                          "peak_source": f"{peak_src} bf16_tflops (burst)",
                          "frac_of_sustained": achieved / peak_sustained},
-            "gather": {"value": flops_total / (g_ms_max * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": g_ms_max,
+            "gather": {"value": flops_total / (fu_max * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": fu_max,
+                       "kernel_ms": fu_kernel_max,
+                       "bytes_to_peers_rank0": (world - 1) * n * S * r * (D * 2 + 4),
+                       "what": "replicated result: the prefill epilogue stores every O/LSE row into every rank's "
+                               "row-major buffer (symmetric memory, peer stores over NVLink) during the "
+                               "attention itself; a device barrier of all ranks before and after each step"},
+            "gather_nccl": {"value": flops_total / (g_ms_max * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": g_ms_max,
                        "all_gather_ms": coll_max, "scatter_ms": scat_max,
                        "bytes_received_per_rank": recv,
                        "all_gather_gbs_per_rank": recv / (coll_max * 1e-3) / 1e9 if recv and coll_max > 0 else None,

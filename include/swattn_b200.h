@@ -194,6 +194,30 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Prefill over a rank's unit-major inputs with its output replicated in
+ * row-major form (multi-GPU driver; no counterpart in the reference, which has
+ * no distributed code -- its per-(batch, head) grid, swiattn_gqa_prefill.py:69,
+ * admits the (batch, KV group) split).  The launch is swa_prefill_forward with
+ * Hkv = 1 over B units: q [B, Sq, Hq, 128], k/v [B, Skv, 1, 128], -1 padded
+ * [B, *_stride] index lists with counts [B, 2] (batch-major, as swa_compact_mask
+ * writes them), metadata as there.  Unit b of the launch is global unit
+ * unit_gid[b] (device int32 [B]) = b_g * rep_hkv + g_g of a [Bg, Sq, rep_hkv * Hq,
+ * 128] problem, and every output row is stored into each of the n_rep (1..8)
+ * row-major buffers rep_out[t] (bf16 [Bg, Sq, rep_hkv * Hq, 128]) and
+ * rep_lse[t] (fp32 [Bg, Sq, rep_hkv * Hq]) at its global position: this GPU's
+ * memory or a peer's (peer pointers from symmetric / IPC-mapped memory, written
+ * over NVLink by the kernel's epilogue).  out / lse (the unit-major result) may
+ * be NULL.  Rows of other units in the replicas are left untouched; making the
+ * peers' writes visible (a barrier after the launch on every rank) is the
+ * caller's.  Workspace and status as swa_prefill_forward. */
+int swa_prefill_forward_replicated(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                                   const int32_t* local_idx, int full_stride, int local_stride,
+                                   const int32_t* counts, const int32_t* full_starts, const int32_t* local_starts,
+                                   const int32_t* causal_ends, const int32_t* unit_gid, int B, int Sq, int Skv, int Hq,
+                                   int head_dim, int window, float scale_log2, int rep_hkv, int n_rep,
+                                   void* const* rep_out, float* const* rep_lse, void* out, float* lse,
+                                   int32_t* workspace, size_t workspace_bytes, void* stream);
+
 /* Unit-major <-> row-major moves of the multi-GPU driver (no counterpart in the
  * reference, which has no distributed code; its per-(batch, head) grid,
  * swiattn_gqa_prefill.py:69, admits the (batch, KV group) split these serve).

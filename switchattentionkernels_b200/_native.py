@@ -47,6 +47,7 @@ EXPORTED = (
     "swa_backward_workspace_bytes",
     "swa_scatter_units",
     "swa_gather_units",
+    "swa_prefill_forward_replicated",
 )
 
 _lock = threading.Lock()
@@ -129,6 +130,18 @@ def _declare(lib) -> None:
         _p, _p,                # out, lse
         _i, _i, _i, _i, _i,    # B, Smax, Hq, Hkv, head_dim
         _i, _f,                # window, scale_log2
+        _p, _sz, _p,           # workspace, workspace_bytes, stream
+    ]
+    lib.swa_prefill_forward_replicated.restype = _i
+    lib.swa_prefill_forward_replicated.argtypes = [
+        _p, _p, _p,            # q, k, v (unit-major)
+        _p, _p, _i, _i,        # full_idx, local_idx, full_stride, local_stride
+        _p, _p, _p, _p,        # counts [B, 2], full_starts, local_starts, causal_ends
+        _p,                    # unit_gid
+        _i, _i, _i, _i, _i,    # B, Sq, Skv, Hq, head_dim
+        _i, _f,                # window, scale_log2
+        _i, _i, _p, _p,        # rep_hkv, n_rep, rep_out[], rep_lse[]
+        _p, _p,                # out, lse (nullable)
         _p, _sz, _p,           # workspace, workspace_bytes, stream
     ]
     for name in ("swa_scatter_units", "swa_gather_units"):

@@ -344,23 +344,48 @@ int swa_prefill_backward(const void* q, const void* k, const void* v, const void
   return SWA_OK;
 }
 
-int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
-                        const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
-                        const int32_t* counts, int counts_batch_major, int count_full, int count_local,
-                        const int32_t* full_starts,
-                        const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
-                        void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
-                        float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
-                        void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Row-major output replicas of a prefill launch (null: none).
+struct Replicas {
+  int n;
+  int hkv;
+  const int32_t* unit_gid;
+  void* const* out;
+  float* const* lse;
+};
+
+int prefill_forward_impl(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                         const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                         const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                         const int32_t* full_starts, const int32_t* local_starts, const int32_t* causal_ends,
+                         const int32_t* bg_list, int n_bg, void* out, float* lse, int B, int Sq, int Skv, int Hq,
+                         int Hkv, int head_dim, int window, float scale_log2, const int32_t* gate,
+                         int32_t* workspace, size_t workspace_bytes, void* stream, const Replicas* rep) {
   if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
   if (B <= 0 || Sq <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
   if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
   if (window <= 0) return fail(SWA_E_INVALID, "window_size must be positive");
   if (!(scale_log2 > 0.0f)) return fail(SWA_E_INVALID, "softmax scale must be positive");
-  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || lse == nullptr)
+  const bool replicated = rep != nullptr && rep->n > 0;
+  if (q == nullptr || k == nullptr || v == nullptr || ((out == nullptr || lse == nullptr) && !replicated))
     return fail(SWA_E_INVALID, "null tensor pointer");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (out != nullptr && !aligned16(out)))
     return fail(SWA_E_INVALID, "q/k/v/out must be 16-byte aligned");
+  if ((out == nullptr) != (lse == nullptr)) return fail(SWA_E_INVALID, "out and lse are both given or both null");
+  if (replicated) {
+    if (rep->n > swa::kMaxReplicas) return fail(SWA_E_INVALID, "at most 8 replicas");
+    if (Hkv != 1) return fail(SWA_E_INVALID, "replicated outputs need a unit-major launch (Hkv == 1)");
+    if (rep->hkv <= 0 || rep->unit_gid == nullptr || rep->out == nullptr || rep->lse == nullptr)
+      return fail(SWA_E_INVALID, "replicas need unit ids, the global KV head count and output pointers");
+    for (int t = 0; t < rep->n; ++t)
+      if (rep->out[t] == nullptr || rep->lse[t] == nullptr || !aligned16(rep->out[t]))
+        return fail(SWA_E_INVALID, "replica outputs must be non-null and 16-byte aligned");
+    if (static_cast<int64_t>(B) * Sq * Hq >= (int64_t(1) << 31))
+      return fail(SWA_E_UNSUPPORTED, "tensor too large for 32-bit row indices");
+  }
   if (workspace == nullptr || workspace_bytes < 16) return fail(SWA_E_INVALID, "workspace must hold 16 bytes");
   if (counts == nullptr && B != 1) return fail(SWA_E_INVALID, "device counts are required when B > 1");
   if (full_cap < 0 || local_cap < 0 || (full_cap > 0 && full_idx == nullptr) ||
@@ -446,6 +471,15 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
   p.nhb = r / rp;
   p.boxh = rp < 128 ? rp : 128;
   p.test_withhold = g_test_withhold.load();
+  if (replicated) {
+    p.n_rep = rep->n;
+    p.rep_hkv = rep->hkv;
+    p.unit_gid = rep->unit_gid;
+    for (int t = 0; t < rep->n; ++t) {
+      p.rep_out[t] = static_cast<__nv_bfloat16*>(rep->out[t]);
+      p.rep_lse[t] = rep->lse[t];
+    }
+  }
 
   const int64_t per_level = static_cast<int64_t>(p.n_bg) * p.nhb;
   const int64_t items =
@@ -459,6 +493,39 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
   e = swa::launch_prefill(p, ctas, s);
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return SWA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int swa_prefill_forward(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                        const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                        const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                        const int32_t* full_starts,
+                        const int32_t* local_starts, const int32_t* causal_ends, const int32_t* bg_list, int n_bg,
+                        void* out, float* lse, int B, int Sq, int Skv, int Hq, int Hkv, int head_dim, int window,
+                        float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
+                        void* stream) {
+  return prefill_forward_impl(q, k, v, full_idx, local_idx, full_stride, local_stride, full_cap, local_cap, counts,
+                              counts_batch_major, count_full, count_local, full_starts, local_starts, causal_ends,
+                              bg_list, n_bg, out, lse, B, Sq, Skv, Hq, Hkv, head_dim, window, scale_log2, gate,
+                              workspace, workspace_bytes, stream, nullptr);
+}
+
+int swa_prefill_forward_replicated(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                                   const int32_t* local_idx, int full_stride, int local_stride,
+                                   const int32_t* counts, const int32_t* full_starts, const int32_t* local_starts,
+                                   const int32_t* causal_ends, const int32_t* unit_gid, int B, int Sq, int Skv, int Hq,
+                                   int head_dim, int window, float scale_log2, int rep_hkv, int n_rep,
+                                   void* const* rep_out, float* const* rep_lse, void* out, float* lse,
+                                   int32_t* workspace, size_t workspace_bytes, void* stream) {
+  if (n_rep <= 0) return fail(SWA_E_INVALID, "n_rep must be at least 1");
+  const Replicas rep{n_rep, rep_hkv, unit_gid, rep_out, rep_lse};
+  return prefill_forward_impl(q, k, v, full_idx, local_idx, full_stride, local_stride, full_stride, local_stride,
+                              counts, 1, 0, 0, full_starts, local_starts, causal_ends, nullptr, 0, out, lse, B, Sq,
+                              Skv, Hq, 1, head_dim, window, scale_log2, nullptr, workspace, workspace_bytes, stream,
+                              &rep);
 }
 
 }  // extern "C"

@@ -16,8 +16,8 @@
 //                          ahead) and publishes them through a shared-memory ring;
 //                          TMA Q gather (boxes of consecutive routed positions, see
 //                          q_tile_boxes; the next unit's boxes are prefetched into L2
-//                          one unit ahead) and the K/V tile ring (4 entries of 128
-//                          keys x 128 dims, K and V tiles alternating)
+//                          one unit ahead) and the K/V tile ring (5 entries of 128
+//                          keys x 128 dims, one TMA box each, K and V alternating)
 //   warp 1      MMA      : one elected lane issues tcgen05.mma in groups of eight
 //                          (S) or two (P V chunk) instructions:
 //                          S_i = Q_i K^T (SS, K-major) and O_i += P_i V (TS: P in TMEM,
@@ -25,15 +25,17 @@
 //                          continuous stream over key steps: PV_0(j), S_0(j+1),
 //                          PV_1(j), S_1(j+1); at a unit's last step both P V groups
 //                          go first, then the next unit's S MMAs.
-//   warps 2-17  softmax  : four warpgroups; tile = (warp - 2) / 8 (rows 0..127 or
-//                          128..255 of the unit, TMEM lane = row), key half =
-//                          ((warp - 2) / 4) % 2 (keys [64 h, 64 h + 64) of each key
-//                          tile and O columns [64 h, 64 h + 64)); then the O/LSE
-//                          epilogue of the tile.
-// TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs)
-// of key half h overwrites columns 64 h .. 64 h + 31 of S_i (scores that half has
-// already consumed) and is consumed by the next PV MMA.  P is published in two
-// chunks (keys [32 c, +32) of each key half, c = 0, 1).
+//   warps 2-17  softmax  : tile = (warp - 2) / 8 (rows 0..127 or 128..255 of the
+//                          unit, TMEM lane = row); the two warps of a tile on one
+//                          TMEM lane quarter take its lanes 0-15 and 16-31, and within
+//                          a warp threads l and l + 16 share a row (16-lane TMEM
+//                          loads: keys [0, 32) + [64, 96) and [32, 64) + [96, 128) of
+//                          each key tile), exchanging row max and row sum by warp
+//                          shuffle; then the O/LSE epilogue of the tile.
+// TMEM (512 columns): S0 | S1 | O0 | O1, 128 FP32 columns each; P_i (BF16 pairs) of
+// keys [64 c, 64 c + 64) overwrites columns 32 c .. 32 c + 31 of S_i (scores the
+// threads already hold) and is consumed by the next PV MMA.  P is published in two
+// chunks (c = 0, 1).
 // Key tiles of a unit start at the 64-aligned key at or below its first legal key.
 //
 // Numerics follow the reference: FP32 scores, log2-domain online softmax with
@@ -152,6 +154,17 @@ __device__ __forceinline__ int branch_count(const PrefillParams& p, int branch, 
 
 __device__ __forceinline__ int load_pos(const PrefillParams& p, int branch, int b, int slot) {
   return p.idx[branch][static_cast<int64_t>(b) * p.idx_stride[branch] + slot];
+}
+
+// Row of (batch b of this launch, position, head of the launch) in the replicated
+// row-major outputs: batch b is global unit unit_gid[b] = b_g * rep_hkv + g_g, and
+// the launch's Hq heads are that unit's KV group (launches over unit-major inputs,
+// Hkv == 1).
+__device__ __forceinline__ int64_t replica_row(const PrefillParams& p, int b, int qpos, int head) {
+  const int gid = p.unit_gid[b];
+  const int bg = gid / p.rep_hkv, gg = gid - bg * p.rep_hkv;
+  const int hq_g = p.rep_hkv * p.Hq;
+  return (static_cast<int64_t>(bg) * p.Sq + qpos) * hq_g + static_cast<int64_t>(gg) * p.Hq + head;
 }
 
 // Decode work item `it` into a unit; returns false for an empty item.
@@ -729,14 +742,20 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (valid_row) {
           const uint32_t nan_pair = 0x7FC07FC0u;
           const uint4 nan4 = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
-          uint4* dst0 = reinterpret_cast<uint4*>(p.out + orow * 128 + 32 * half);
-          uint4* dst1 = reinterpret_cast<uint4*>(p.out + orow * 128 + 64 + 32 * half);
+          for (int t = -1; t < p.n_rep; ++t) {
+            __nv_bfloat16* ob = t < 0 ? p.out : p.rep_out[t];
+            float* lb = t < 0 ? p.lse : p.rep_lse[t];
+            if (ob == nullptr) continue;
+            const int64_t row = t < 0 ? orow : replica_row(p, u.b, qpos, head);
+            uint4* dst0 = reinterpret_cast<uint4*>(ob + row * 128 + 32 * half);
+            uint4* dst1 = reinterpret_cast<uint4*>(ob + row * 128 + 64 + 32 * half);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            dst0[c] = nan4;
-            dst1[c] = nan4;
+            for (int c = 0; c < 4; ++c) {
+              dst0[c] = nan4;
+              dst1[c] = nan4;
+            }
+            if (half == 0) lb[row] = -INFINITY;
           }
-          if (half == 0) p.lse[orow] = -INFINITY;
         }
         continue;
       }
@@ -876,7 +895,12 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       // swiattn_gqa_prefill_varlen.py:236-241): O = 0/0 and LSE = log2(0) + m.
       const bool no_keys = rb.hi <= rb.lo;
       const float inv_l = no_keys ? __int_as_float(0x7FC00000) : 1.0f / l;
-      if (half == 0 && valid_row) p.lse[orow] = no_keys ? -INFINITY : lg2_approx(l) + m;
+      const int64_t rrow = (p.n_rep > 0 && valid_row) ? replica_row(p, u.b, qpos, head) : -1;
+      if (half == 0 && valid_row) {
+        const float lse_v = no_keys ? -INFINITY : lg2_approx(l) + m;
+        if (p.lse != nullptr) p.lse[orow] = lse_v;
+        for (int t = 0; t < p.n_rep; ++t) p.rep_lse[t][rrow] = lse_v;
+      }
       tc_fence_after();
       uint32_t ch[8][4];  // ch[j]: chunk j of this thread's columns as BF16 pairs
 #pragma unroll
@@ -911,7 +935,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           }
         }
       }
-      const int64_t my_row = valid_row ? orow : -1;
+      const int64_t my_row = (valid_row && p.out != nullptr) ? orow : -1;
       const int my_chunk = lane & 7;
       const int col = my_chunk < 4 ? 32 * half + 8 * my_chunk : 64 + 32 * half + 8 * (my_chunk - 4);
 #pragma unroll
@@ -921,8 +945,24 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (grow >= 0)
           *reinterpret_cast<uint4*>(p.out + grow * 128 + col) = make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
       }
+      if (p.n_rep > 0) {
+        // the same chunks into every row-major replica (this GPU's or a peer's
+        // memory, written over NVLink), at the row's global position
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int src = (lane & ~7) + j;
+          const int64_t grow = __shfl_sync(0xffffffffu, rrow, src);
+          if (grow >= 0) {
+            const uint4 val = make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
+            for (int t = 0; t < p.n_rep; ++t) *reinterpret_cast<uint4*>(p.rep_out[t] + grow * 128 + col) = val;
+          }
+        }
+      }
       tr.ev(22, s_use);
     }
+    // replicas in peer memory: make this thread's stores visible system-wide before
+    // the kernel completes (the caller's barrier then publishes them to the peers)
+    if (p.n_rep > 0) __threadfence_system();
   }
 
   // ------------------------------------------------------------------ teardown

@@ -22,6 +22,7 @@ enum : int32_t {
 };
 
 constexpr int kMaxQRunMaps = 7;
+constexpr int kMaxReplicas = 8;  // row-major output copies one prefill launch can write
 
 struct __align__(64) PrefillParams {
   CUtensorMap q_map;  // 2-D {128, B*Sq*Hq}, box {64, boxh}, 128B swizzle
@@ -53,6 +54,16 @@ struct __align__(64) PrefillParams {
   int nhb;   // head blocks per KV group = (Hq/Hkv) / rp
   int boxh;  // rows per Q TMA box = min(rp, 128)
   int test_withhold;  // failure-detection test hook: CTA 0 withholds its second K/V tile load
+  // Replicated row-major outputs (multi-GPU driver; launches with Hkv == 1 over
+  // unit-major inputs): batch b of the launch is global unit unit_gid[b] =
+  // b_g * rep_hkv + g_g, and every output row is also stored to rep_out[t] /
+  // rep_lse[t] (t < n_rep; [Bg, Sq, rep_hkv * Hq, 128] / [Bg, Sq, rep_hkv * Hq]),
+  // this GPU's memory or a peer's.  `out` / `lse` may then be null (not written).
+  int n_rep;
+  int rep_hkv;
+  const int32_t* unit_gid;
+  __nv_bfloat16* rep_out[kMaxReplicas];
+  float* rep_lse[kMaxReplicas];
 };
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);

@@ -13,16 +13,20 @@ of batch b).  Two ways to run a rank's share:
   ``B = n`` sequences of ``r`` query heads over one KV head -- the shape in which
   a head-sharded model layer produces them, and the only bytes a rank needs.
 
-Only when the caller asks for a replicated result does one all-gather move O
-(BF16) and LSE (FP32) of every unit to every rank (NCCL over NVLink for CUDA
-tensors), followed by one scatter kernel into the ``[B, S, Hq, ...]`` layout
-(``gather_units_to_rows``).
+Only when the caller asks for a replicated result is there communication:
+either the prefill kernel's epilogue stores every O / LSE row into every rank's
+row-major ``[B, S, Hq, ...]`` buffer over NVLink as it is produced
+(``forward_units_replicated`` with ``ReplicaBuffers`` in symmetric memory: the
+transfer overlaps the attention itself), or one NCCL all-gather of O (BF16) and
+LSE (FP32) after the launch followed by one scatter kernel into the row-major
+layout (``gather_units_to_rows``; any backend that implements ``all_gather``).
 
 The reference has no distributed code; this driver implements the sharding
 that its per-(batch, head) grid (``swiattn_gqa_prefill.py:69``) admits.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Sequence
 
 import numpy as np
@@ -276,3 +280,106 @@ def sharded_switch_gqa_prefill_forward(q, k, v, full_query_indices, local_query_
     if gather and world > 1:
         gather_units(out, lse, plan, hkv=hkv, group=group)
     return out, lse, plan
+
+
+class ReplicaBuffers:
+    """Row-major O ``[B, S, Hq, 128]`` (BF16) and LSE ``[B, S, Hq]`` (FP32) of one
+    sharded problem, on every rank of ``group``, in symmetric memory.
+
+    Every rank's kernel writes its units' rows into all ranks' buffers directly
+    (peer pointers over NVLink), so after ``forward_units_replicated`` every rank
+    holds the whole result.  Allocated once per problem shape and reused across
+    calls; ``out`` / ``lse`` are this rank's buffers.
+    """
+
+    def __init__(self, B: int, S: int, Hq: int, *, device, group=None):
+        device = torch.device(device)
+        self.shape = (B, S, Hq)
+        single = not dist.is_initialized() or dist.get_world_size(group) == 1
+        self._h_out = None
+        if single:
+            # one rank: plain device buffers, nothing to share
+            self.out = torch.empty((B, S, Hq, 128), dtype=torch.bfloat16, device=device)
+            self.lse = torch.empty((B, S, Hq), dtype=torch.float32, device=device)
+            self.world = 1
+            out_ptrs, lse_ptrs = [self.out.data_ptr()], [self.lse.data_ptr()]
+        else:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            if group is None:
+                group = dist.group.WORLD
+            self.out = symm_mem.empty((B, S, Hq, 128), dtype=torch.bfloat16, device=device)
+            self.lse = symm_mem.empty((B, S, Hq), dtype=torch.float32, device=device)
+            self._h_out = symm_mem.rendezvous(self.out, group)
+            self._h_lse = symm_mem.rendezvous(self.lse, group)
+            self.world = int(self._h_out.world_size)
+            if self.world > 8:
+                raise ValueError("at most 8 ranks can share replicated outputs")
+            out_ptrs = list(self._h_out.buffer_ptrs)
+            lse_ptrs = list(self._h_lse.buffer_ptrs)
+        self._rep_out = (ctypes.c_void_p * self.world)(*out_ptrs)
+        self._rep_lse = (ctypes.c_void_p * self.world)(*lse_ptrs)
+
+    def barrier(self) -> None:
+        """Device-side barrier of all ranks on the current stream: every rank's
+        earlier writes into the buffers are complete and visible afterwards (a
+        no-op with one rank: stream order suffices)."""
+        if self._h_out is not None:
+            self._h_out.barrier(channel=0)
+
+
+def forward_units_replicated(q_u, k_u, v_u, full_u, local_u, counts_u, units: Sequence[int], rep: ReplicaBuffers, *,
+                             hkv: int, window_size: int = 1024, sm_scale: float | None = None, metadata=None,
+                             out=None, lse=None, barrier: bool = True, status_out=None):
+    """This rank's units (unit-major, see ``take_units``) through the prefill
+    kernel, every output row written into all ranks' ``rep`` buffers.
+
+    ``full_u`` / ``local_u`` / ``counts_u``: the units' -1 padded index lists and
+    ``[n, 2]`` counts (``build_switch_query_indices_batched`` of the units' mask
+    rows).  ``units``: the global unit ids ``b * hkv + g`` of the n units, in order.
+    ``out`` / ``lse``: optional unit-major outputs (not written when None).  With
+    ``barrier`` (the default) the call starts with a device barrier of all ranks
+    (nobody still reads the buffers' previous contents) and ends with one (every
+    rank's rows have landed); without it those are the caller's.
+    """
+    _core.validate_qkv(q_u, k_u, v_u)
+    n, S, r, D = q_u.shape
+    if k_u.shape[2] != 1 or k_u.shape[0] != n or len(units) != n:
+        raise ValueError("unit-major inputs: q [n, S, Hq/Hkv, 128], k / v [n, S, 1, 128], one unit id per row")
+    B, S_rep, Hq = rep.shape
+    if S_rep != S or Hq != hkv * r:
+        raise ValueError("replica buffers do not match the problem")
+    dev = q_u.device
+    _core._check_status_out(status_out, dev)
+    if counts_u.dtype != torch.int32 or tuple(counts_u.shape) != (n, 2) or counts_u.device != dev:
+        raise ValueError("counts_u must be an int32 [n, 2] tensor on the device of q_u")
+    f = full_u.to(dtype=torch.int32).contiguous()
+    l = local_u.to(dtype=torch.int32).contiguous()
+    scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * _core.LOG2E
+    if not scale > 0:
+        raise ValueError("sm_scale must be positive")
+    fs = ls = ce = None
+    if metadata is not None:
+        _core._check_metadata(metadata, q_u, S, k_u.shape[1])
+        fs, ls, ce = metadata.full_starts, metadata.local_starts, metadata.causal_ends
+    gid = _device_ids(units, dev)
+    ws = torch.zeros(4, dtype=torch.int32, device=dev)
+    lib = _native.load()
+    if barrier:
+        rep.barrier()
+    with torch.cuda.device(dev):
+        rc = lib.swa_prefill_forward_replicated(
+            _native.ptr(q_u), _native.ptr(k_u), _native.ptr(v_u),
+            _native.ptr(f) if f.shape[1] else None, _native.ptr(l) if l.shape[1] else None,
+            int(f.shape[1]), int(l.shape[1]), _native.ptr(counts_u.contiguous()),
+            _native.ptr(fs), _native.ptr(ls), _native.ptr(ce), _native.ptr(gid),
+            n, S, k_u.shape[1], r, D, int(window_size), float(scale), hkv, rep.world,
+            ctypes.cast(rep._rep_out, ctypes.c_void_p), ctypes.cast(rep._rep_lse, ctypes.c_void_p),
+            _native.ptr(out), _native.ptr(lse),
+            _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
+    _native.check(rc, "forward_units_replicated")
+    if barrier:
+        rep.barrier()
+    if status_out is not None or _core.CHECK_DEVICE_STATUS:
+        _core.publish_status(ws[1:2], status_out)
+    return rep.out, rep.lse

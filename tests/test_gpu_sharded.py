@@ -139,3 +139,115 @@ def test_unit_major_forward_equals_row_major_slices(cuda_device):
     sharded.scatter_gathered(o_all, l_all, plan, hkv=Hkv, out=out, lse=lse)
     torch.cuda.synchronize()
     assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)
+
+
+class _LocalReplicas:
+    """Stand-in for ReplicaBuffers on one GPU: several row-major buffers of this
+    device (the kernel path is the same; the peer pointers come from symmetric
+    memory in the multi-GPU case)."""
+
+    def __init__(self, B, S, Hq, dev, copies):
+        import ctypes
+
+        self.shape = (B, S, Hq)
+        self.outs = [torch.full((B, S, Hq, 128), float("nan"), dtype=torch.bfloat16, device=dev) for _ in range(copies)]
+        self.lses = [torch.full((B, S, Hq), float("nan"), device=dev) for _ in range(copies)]
+        self.world = copies
+        self._rep_out = (ctypes.c_void_p * copies)(*[t.data_ptr() for t in self.outs])
+        self._rep_lse = (ctypes.c_void_p * copies)(*[t.data_ptr() for t in self.lses])
+        self.out, self.lse = self.outs[0], self.lses[0]
+
+    def barrier(self):
+        pass
+
+
+def test_replicated_epilogue_writes_every_copy(cuda_device):
+    # each "rank" of a 3-rank plan runs its unit-major units through the replicating
+    # launch; every row-major copy must equal the row-major forward bit for bit
+    from switchattentionkernels_b200 import build_switch_query_indices_batched, sharded
+
+    q, k, v, mask = _inputs(cuda_device, seed=24)
+    B, S, Hq, _ = q.shape
+    Hkv, W = k.shape[2], 170
+    full, local, counts = build_switch_query_indices_batched(mask.to(cuda_device))
+    ref_o, ref_l = _core.forward(q, k, v, full, local, window_size=W, query_counts=counts)
+    fl, ll = lists_from_mask(mask)
+    plan = plan_units(unit_costs(fl, ll, hkv=Hkv, skv=S, window=W), 3)
+    rep = _LocalReplicas(B, S, Hq, cuda_device, copies=3)
+    for units in plan:
+        q_u, k_u, v_u = (sharded.take_units(t, units, hkv=Hkv) for t in (q, k, v))
+        m_u = mask[torch.tensor([u // Hkv for u in units])].to(cuda_device)
+        f_u, l_u, c_u = build_switch_query_indices_batched(m_u)
+        o_u = torch.empty_like(q_u)
+        lse_u = torch.empty(q_u.shape[:3], device=cuda_device)
+        sharded.forward_units_replicated(q_u, k_u, v_u, f_u, l_u, c_u, units, rep, hkv=Hkv, window_size=W,
+                                         out=o_u, lse=lse_u, barrier=False)
+        torch.cuda.synchronize()
+        for i, u in enumerate(units):
+            b, g = divmod(u, Hkv)
+            r = Hq // Hkv
+            assert torch.equal(o_u[i], ref_o[b, :, g * r:(g + 1) * r]), f"unit {u}: unit-major O"
+            assert torch.equal(lse_u[i], ref_l[b, :, g * r:(g + 1) * r]), f"unit {u}: unit-major LSE"
+    for t in range(3):
+        assert torch.equal(rep.outs[t], ref_o), f"copy {t}: O"
+        assert torch.equal(rep.lses[t], ref_l), f"copy {t}: LSE"
+
+
+def _replica_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from switchattentionkernels_b200 import build_switch_query_indices_batched, sharded
+
+        q, k, v, mask = _inputs(dev, seed=25)
+        B, S, Hq, _ = q.shape
+        Hkv, W = k.shape[2], 260
+        fl, ll = lists_from_mask(mask)
+        plan = plan_units(unit_costs(fl, ll, hkv=Hkv, skv=S, window=W), world)
+        units = plan[rank]
+        q_u, k_u, v_u = (sharded.take_units(t, units, hkv=Hkv) for t in (q, k, v))
+        m_u = mask[torch.tensor([u // Hkv for u in units])].to(dev)
+        f_u, l_u, c_u = build_switch_query_indices_batched(m_u)
+        rep = sharded.ReplicaBuffers(B, S, Hq, device=dev)
+        for _ in range(2):  # the buffers are reused across calls
+            out, lse = sharded.forward_units_replicated(q_u, k_u, v_u, f_u, l_u, c_u, units, rep, hkv=Hkv,
+                                                        window_size=W)
+        full, local, counts = build_switch_query_indices_batched(mask.to(dev))
+        ref_o, ref_l = _core.forward(q, k, v, full, local, window_size=W, query_counts=counts)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(out, ref_o) and torch.equal(lse, ref_l))
+        result_q.put((rank, "ok" if ok else "mismatch"))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        result_q.put((rank, "error:" + type(e).__name__ + ":" + str(e)[:300]))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def test_replicated_outputs_two_gpus():
+    # every rank's kernel writes its units' rows into both ranks' symmetric-memory
+    # buffers over NVLink; each rank must end with the whole row-major result
+    import multiprocessing as mp_std
+    import socket
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp_std.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_replica_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    assert res == [(0, "ok"), (1, "ok")], res
