@@ -15,9 +15,9 @@
 //   warp 0      producer : takes work units from the global counter (one unit
 //                          ahead) and publishes them through a shared-memory ring;
 //                          TMA Q gather (boxes of consecutive routed positions, see
-//                          q_tile_boxes; the next unit's boxes are prefetched into L2
-//                          one unit ahead) and the K/V tile ring (5 entries of 128
-//                          keys x 128 dims, one TMA box each, K and V alternating)
+//                          q_tile_boxes) and the K/V tile ring (5 entries of 128
+//                          keys x 128 dims, one TMA box each, K and V alternating);
+//                          K/V loads evict-last in L2, Q loads and O stores evict-first
 //   warp 1      MMA      : one elected lane issues tcgen05.mma in groups of eight
 //                          (S) or two (P V chunk) instructions:
 //                          S_i = Q_i K^T (SS, K-major) and O_i += P_i V (TS: P in TMEM,
@@ -60,6 +60,11 @@ constexpr int kSchedSlots = 4;      // work-unit ring depth
 constexpr uint32_t kTileBytes = 128 * 128 * 2;   // 32 KB: a 128x128 BF16 tile (2 swizzled halves)
 constexpr uint32_t kHalfBytes = 128 * 64 * 2;    // 16 KB: 128 rows x 64 columns
 constexpr float kRescaleThreshold = 8.0f;
+// L2 use: K/V tiles are read by every unit of their (b, g) group, Q rows and O rows
+// are touched once.  The K/V loads carry an evict-last L2 policy, the Q loads and
+// O stores evict-first, so the streams of Q and O do not push the groups' K/V
+// prefixes out of L2 (config 3: DRAM traffic per launch 5.72 -> 4.34 GB; the Q L2
+// prefetch one unit ahead that this replaced added 1.1 GB of re-reads).
 
 struct Unit {
   int valid;    // 0 = no more work
@@ -239,17 +244,18 @@ __device__ __forceinline__ void read_unit(const volatile Unit* src, Unit& u) {
 }
 
 // TMA boxes of Q tile i (rows 128 i .. 128 i + 127) of unit u, issued by the
-// producer warp's lanes: loads into `qdst` (completing on `bar`) or, with
-// qdst == nullptr, L2 prefetches.  With rp <= 64 a tile holds spt = 128 / rp
-// routed positions (slots); each slot s is covered by the largest aligned
-// power-of-two block of slots containing it whose positions are consecutive, and
-// such a block of 2^L slots is one box of 2^L positions x rp heads (3-D map
-// q_runs[L - 1]), or of rp rows (2-D map) for a single slot.  Blocks of
-// consecutive positions contain sub-blocks of consecutive positions, so these
-// maximal blocks partition the slots and every row is loaded exactly once.
+// producer warp's lanes into `qdst`, completing on `bar` (evict-first L2 policy:
+// every Q row is read once).  With rp <= 64 a tile holds spt = 128 / rp routed
+// positions (slots); each slot s is covered by the largest aligned power-of-two
+// block of slots containing it whose positions are consecutive, and such a block
+// of 2^L slots is one box of 2^L positions x rp heads (3-D map q_runs[L - 1]), or
+// of rp rows (2-D map) for a single slot.  Blocks of consecutive positions contain
+// sub-blocks of consecutive positions, so these maximal blocks partition the slots
+// and every row is loaded exactly once.
 __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit& u, int i, int lane, uint8_t* qdst,
                                              uint64_t* bar) {
   const int head0 = u.g * (p.Hq / p.Hkv) + u.hb * p.rp;
+  const uint64_t pol = l2_policy_evict_first();
   if (p.rp > 64) {
     // at most one position per tile: boxes of boxh rows (rp = 128: one box per half;
     // rp = 256: tile i holds heads [128 i, 128 i + 128) of the unit's position)
@@ -261,11 +267,7 @@ __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit&
       const int slot_abs = min(u.pb * p.pc + row0 / p.rp, u.count - 1);
       const int pos = min(max(load_pos(p, u.branch, u.b, slot_abs), 0), p.Sq - 1);
       const int row = (u.b * p.Sq + pos) * p.Hq + head0 + row0 % p.rp;
-      if (qdst != nullptr) {
-        tma_load_2d(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, bar, half * 64, row);
-      } else {
-        tma_prefetch_l2_2d(&p.q_map, half * 64, row, l2_policy_evict_last());
-      }
+      tma_load_2d_hint(qdst + half * kHalfBytes + bx * p.boxh * 128, &p.q_map, bar, half * 64, row, pol);
     }
     return;
   }
@@ -291,16 +293,10 @@ __device__ __forceinline__ void q_tile_boxes(const PrefillParams& p, const Unit&
     for (int half = 0; half < 2; ++half) {
       if (lev == 0) {
         const int row = (u.b * p.Sq + pos) * p.Hq + head0;
-        if (qdst != nullptr) {
-          tma_load_2d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_map, bar, half * 64, row);
-        } else {
-          tma_prefetch_l2_2d(&p.q_map, half * 64, row, l2_policy_evict_last());
-        }
-      } else if (qdst != nullptr) {
-        tma_load_3d(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_runs[lev - 1], bar, half * 64, head0,
-                    u.b * p.Sq + pos);
+        tma_load_2d_hint(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_map, bar, half * 64, row, pol);
       } else {
-        tma_prefetch_l2_3d(&p.q_runs[lev - 1], half * 64, head0, u.b * p.Sq + pos, l2_policy_evict_last());
+        tma_load_3d_hint(qdst + half * kHalfBytes + s * p.rp * 128, &p.q_runs[lev - 1], bar, half * 64, head0,
+                         u.b * p.Sq + pos, pol);
       }
     }
   }
@@ -352,6 +348,9 @@ __device__ __forceinline__ float row_max64(const float* s) {
   return fmax3(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[5]), fmaxf(u[6], u[7]));
 }
 
+// kRep: the launch also writes the replicated row-major outputs (p.n_rep > 0); a
+// separate instantiation, so the plain launch carries none of that code.
+template <bool kRep>
 __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __grid_constant__ PrefillParams p) {
   if (p.gate != nullptr && *p.gate != 0) return;  // index validation failed: write nothing
 #ifdef SWA_CYCLES
@@ -468,12 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       }
       __syncwarp();
       if (!u.valid) break;
-      if (un.valid && un.n > 0) {
-        // Prefetch the next unit's Q boxes into L2 so its gather (issued once this
-        // unit's last S MMAs have freed the Q buffers) hits L2.
-        q_tile_boxes(p, un, 0, lane, nullptr, nullptr);
-        q_tile_boxes(p, un, 1, lane, nullptr, nullptr);
-      }
       tr.ev(62, k);
       bool ok = true;
       if (u.n > 0) {
@@ -488,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
             mbar_arrive_expect_tx(&kv_full[s], kTileBytes);
             uint8_t* dst = smem + SmemLayout::kv + s * kTileBytes;
             const CUtensorMap* map = kv == 0 ? &p.k_map : &p.v_map;
-            tma_load_5d(dst, map, &kv_full[s], 0, u.j0 * 64 + j * kBK, 0, u.g, u.b);
+            tma_load_5d_hint(dst, map, &kv_full[s], 0, u.j0 * 64 + j * kBK, 0, u.g, u.b, l2_policy_evict_last());
           }
           __syncwarp();
           ++kv_it;
@@ -742,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (valid_row) {
           const uint32_t nan_pair = 0x7FC07FC0u;
           const uint4 nan4 = make_uint4(nan_pair, nan_pair, nan_pair, nan_pair);
-          for (int t = -1; t < p.n_rep; ++t) {
+          for (int t = -1; t < (kRep ? p.n_rep : 0); ++t) {
             __nv_bfloat16* ob = t < 0 ? p.out : p.rep_out[t];
             float* lb = t < 0 ? p.lse : p.rep_lse[t];
             if (ob == nullptr) continue;
@@ -895,11 +888,13 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       // swiattn_gqa_prefill_varlen.py:236-241): O = 0/0 and LSE = log2(0) + m.
       const bool no_keys = rb.hi <= rb.lo;
       const float inv_l = no_keys ? __int_as_float(0x7FC00000) : 1.0f / l;
-      const int64_t rrow = (p.n_rep > 0 && valid_row) ? replica_row(p, u.b, qpos, head) : -1;
+      const int64_t rrow = (kRep && valid_row) ? replica_row(p, u.b, qpos, head) : -1;
       if (half == 0 && valid_row) {
         const float lse_v = no_keys ? -INFINITY : lg2_approx(l) + m;
-        if (p.lse != nullptr) p.lse[orow] = lse_v;
-        for (int t = 0; t < p.n_rep; ++t) p.rep_lse[t][rrow] = lse_v;
+        if (!kRep || p.lse != nullptr) p.lse[orow] = lse_v;
+        if constexpr (kRep) {
+          for (int t = 0; t < p.n_rep; ++t) p.rep_lse[t][rrow] = lse_v;
+        }
       }
       tc_fence_after();
       uint32_t ch[8][4];  // ch[j]: chunk j of this thread's columns as BF16 pairs
@@ -935,17 +930,19 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
           }
         }
       }
-      const int64_t my_row = (valid_row && p.out != nullptr) ? orow : -1;
+      const int64_t my_row = (valid_row && (!kRep || p.out != nullptr)) ? orow : -1;
       const int my_chunk = lane & 7;
       const int col = my_chunk < 4 ? 32 * half + 8 * my_chunk : 64 + 32 * half + 8 * (my_chunk - 4);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int src = (lane & ~7) + j;  // lane holding row j of this group
         const int64_t grow = __shfl_sync(0xffffffffu, my_row, src);
-        if (grow >= 0)
-          *reinterpret_cast<uint4*>(p.out + grow * 128 + col) = make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
+        if (grow >= 0) {
+          const uint4 val = make_uint4(ch[j][0], ch[j][1], ch[j][2], ch[j][3]);
+          st_global_v4_hint(p.out + grow * 128 + col, val, l2_policy_evict_first());
+        }
       }
-      if (p.n_rep > 0) {
+      if constexpr (kRep) {
         // the same chunks into every row-major replica (this GPU's or a peer's
         // memory, written over NVLink), at the row's global position
 #pragma unroll
@@ -962,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     }
     // replicas in peer memory: make this thread's stores visible system-wide before
     // the kernel completes (the caller's barrier then publishes them to the peers)
-    if (p.n_rep > 0) __threadfence_system();
+    if constexpr (kRep) __threadfence_system();
   }
 
   // ------------------------------------------------------------------ teardown
@@ -981,16 +978,23 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_sms, cudaStream_t stream) {
-  static bool attr_set[64] = {};
+  static bool attr_set[2][64] = {};
+  const bool rep = params.n_rep > 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(switch_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (dev < 64 && !attr_set[rep][dev]) {
+    cudaError_t e = rep ? cudaFuncSetAttribute(switch_prefill_kernel<true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
+                        : cudaFuncSetAttribute(switch_prefill_kernel<false>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[rep][dev] = true;
   }
-  switch_prefill_kernel<<<num_sms, kThreads, kSmemBytes, stream>>>(params);
+  if (rep) {
+    switch_prefill_kernel<true><<<num_sms, kThreads, kSmemBytes, stream>>>(params);
+  } else {
+    switch_prefill_kernel<false><<<num_sms, kThreads, kSmemBytes, stream>>>(params);
+  }
   return cudaGetLastError();
 }
 

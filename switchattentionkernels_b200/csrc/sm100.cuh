@@ -34,10 +34,9 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // CTA frees its tensor memory and the kernel returns with an error code recorded
 // in global memory.  No legitimate wait in these kernels lasts longer than one
 // work unit (well under 10 ms), so one second is a wide margin.  Named barriers
-// (bar.sync) have no time limit: a kernel whose warps also meet in one gives
-// every warp that leaves on an abort a bar.arrive on it (named_bar_arrive), so
-// partner warps already waiting there are released and reach their next bounded
-// mbarrier wait, which sees the flag.
+// (bar.sync) have no time limit, so a kernel that uses one (the decode step's
+// four math warps) places it where every warp arrives whether or not it left its
+// loop on an abort; the prefill kernel uses none.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 // ---------------------------------------------------------------------------
@@ -104,15 +103,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                                            int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3) {
   asm volatile(
@@ -122,13 +112,47 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                                            int c2, int c3, int c4) {
+// The same tile loads with an L2 cache policy (createpolicy) for the lines they read.
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                                 uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                                 int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                                 int c2, int c3, int c4, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+      "l"(policy)
+      : "memory");
+}
+
+// L2 policy for data read or written once (evict-first).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 16-byte global store with an L2 cache policy.
+__device__ __forceinline__ void st_global_v4_hint(void* ptr, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w), "l"(policy)
+               : "memory");
 }
 
 // L2 policy that keeps lines resident ahead of streaming data (evict-last).
@@ -136,23 +160,6 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
-}
-
-// Bring a box of a tiled tensor into L2 (no shared-memory destination), with an
-// L2 cache policy.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1, uint64_t policy) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "l"(policy)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2,
-                                                   uint64_t policy) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "l"(policy)
-               : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -199,33 +206,6 @@ __device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           smem_u32(bar))
-      : "memory");
-}
-
-// Eight back-to-back SS MMAs over K = 128 (two 64-column swizzled halves, four
-// 16-element steps each) with a single elected issuing lane.  a_desc / b_desc are
-// the descriptors of the first step; step kk adds ((kk / 4) * 16384 + (kk % 4) * 32)
-// bytes to both start addresses (start-address field = bytes >> 4, no carry out of
-// its 14 bits for shared-memory addresses).  The first step overwrites D.
-__device__ __forceinline__ void umma_ss_k128_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                  uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .pred e, p0, p1;\n\t.reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n\t"
-      "setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
-      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\tadd.s64 a4, %1, 1024;\n\t"
-      "add.s64 a5, %1, 1026;\n\tadd.s64 a6, %1, 1028;\n\tadd.s64 a7, %1, 1030;\n\t"
-      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\tadd.s64 b4, %2, 1024;\n\t"
-      "add.s64 b5, %2, 1026;\n\tadd.s64 b6, %2, 1028;\n\tadd.s64 b7, %2, 1030;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc)
       : "memory");
 }
 
@@ -442,30 +422,9 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Arrive on a named barrier without waiting (counts this warp's threads toward
-// the current phase of barrier `id` over `count` threads).
-__device__ __forceinline__ void named_bar_arrive(int id, int count) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void reg_fence16(uint32_t* r) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
-}
-
-// Register reallocation between warpgroups: every warp of a warpgroup executes the
-// same call.  dealloc lowers this warpgroup's per-thread registers to N (returning
-// the rest to the CTA's pool); alloc raises them to N, waiting until the pool has
-// them.  The pool is what the CTA was launched with (threads x registers per
-// thread at launch), so the warpgroups' final counts must add up to at most that.
-template <uint32_t N>
-__device__ __forceinline__ void reg_dealloc() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-
-template <uint32_t N>
-__device__ __forceinline__ void reg_alloc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------
