@@ -79,6 +79,8 @@ def parse_args():
     ap.add_argument("--workload", type=int, choices=[3, 5], default=CONFIG_ID,
                     help="default line's workload: 3 (the headline) or 5 (two 131072-token sequences, Hkv 4)")
     ap.add_argument("--p-full", type=float, default=None, help="with --workload 5: routing density p_full")
+    ap.add_argument("--p-sweep", type=str, default=None,
+                    help="with --workload 5: comma-separated p_full values, one line each from one process")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the N=1 extras (standard-layout kernel, backward and decode steps)")
     ap.add_argument("--backward", action="store_true",
@@ -996,7 +998,30 @@ def run_default(args, world, rank, local_rank):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hpk, "unit": "GB/s", "frac": gbs / hpk,
                          "peak_source": hsrc},
             "gpu_launches_per_step": 2}
-        del dq_, dk_, dv_
+        # the same batch with an FP8 e4m3 cache, per-(sequence, KV head) scales
+        ks_ = dk_.float().abs().amax(dim=(1, 3)) / 448.0
+        vs_ = dv_.float().abs().amax(dim=(1, 3)) / 448.0
+        dk8 = (dk_.float() / ks_[:, None, :, None]).to(torch.float8_e4m3fn)
+        dv8 = (dv_.float() / vs_[:, None, :, None]).to(torch.float8_e4m3fn)
+        del dk_, dv_
+
+        def step_dec8():
+            switch_gqa_decode_forward(dq_, dk8, dv8, dl, dr, window_size=DECODE_W, k_scale=ks_, v_scale=vs_)
+
+        for _ in range(2):
+            step_dec8()
+        torch.cuda.synchronize()
+        d8_ms = time_steps(step_dec8, nd, stream)
+        gbs8 = kv_bytes / 2 / (d8_ms * 1e-3) / 1e9
+        extras["decode_fp8"] = {
+            "metric": "decode step over an FP8 e4m3 KV cache: legal K/V bytes read per second",
+            "value": gbs8, "unit": "GB/s", "ms_per_step": d8_ms, "steps": nd,
+            "tokens_per_s": DECODE_B / (d8_ms * 1e-3), "speedup_vs_bf16_cache": d_ms / d8_ms,
+            "workload": "the decode batch above, K/V quantised per (sequence, KV head)",
+            "roofline": {"bound": "hbm", "achieved": gbs8, "peak": hpk, "unit": "GB/s", "frac": gbs8 / hpk,
+                         "peak_source": hsrc},
+            "gpu_launches_per_step": 2}
+        del dq_, dk8, dv8
 
     e2e_ms = e2e["ms"] if e2e else 0.0
     mx = reduce([ms, g_ms, coll_ms, scat_ms, st_ms, e2e_ms, pf_avg, fu_ms, fu_kernel], dist.ReduceOp.MAX)
@@ -1080,6 +1105,12 @@ def main():
             return run_cp(args, world, rank, local_rank)
         if args.replicas:
             return run_replicas(args, world, rank, local_rank)
+        if args.p_sweep:
+            for pv in args.p_sweep.split(","):
+                args.p_full = float(pv)
+                run_default(args, world, rank, local_rank)
+                torch.cuda.empty_cache()
+            return 0
         return run_default(args, world, rank, local_rank)
     finally:
         if world > 1:

@@ -140,6 +140,19 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
                        int head_dim, int window, float scale_log2, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* The decode step over an FP8 KV cache (no counterpart in the reference): as
+ * swa_decode_forward with k_cache / v_cache [B, Smax, Hkv, 128] in FP8 e4m3 (one
+ * byte per element) and per-(sequence, KV head) FP32 scales k_scale, v_scale
+ * [B, Hkv]: the attention uses K = k_cache * k_scale and V = v_cache * v_scale.
+ * Half the cache bytes of the BF16 step, which is HBM-bound.  The products run
+ * in FP16 (the e4m3 values convert exactly; q is converted from BF16 and must
+ * lie within the FP16 range; P is rounded to FP16).  Same workspace as
+ * swa_decode_workspace_bytes(B, Smax, Hq, Hkv). */
+int swa_decode_forward_fp8(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                           const float* v_scale, const int32_t* seq_lens, const uint8_t* route, void* out, float* lse,
+                           int B, int Smax, int Hq, int Hkv, int head_dim, int window, float scale_log2,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* Capacity-bucket preparation and validation of one index list per batch row
  * (replaces _prepare_indices, swiattn_gqa_prefill_varlen.py:271-304).
  *   idx [B, N]; trailing_pad = 0: all N entries are routed rows (the reference

@@ -48,6 +48,7 @@ EXPORTED = (
     "swa_scatter_units",
     "swa_gather_units",
     "swa_prefill_forward_replicated",
+    "swa_decode_forward_fp8",
 )
 
 _lock = threading.Lock()
@@ -127,6 +128,15 @@ def _declare(lib) -> None:
     lib.swa_decode_forward.restype = _i
     lib.swa_decode_forward.argtypes = [
         _p, _p, _p, _p, _p,    # q, k_cache, v_cache, seq_lens, route
+        _p, _p,                # out, lse
+        _i, _i, _i, _i, _i,    # B, Smax, Hq, Hkv, head_dim
+        _i, _f,                # window, scale_log2
+        _p, _sz, _p,           # workspace, workspace_bytes, stream
+    ]
+    lib.swa_decode_forward_fp8.restype = _i
+    lib.swa_decode_forward_fp8.argtypes = [
+        _p, _p, _p, _p, _p,    # q, k_cache, v_cache, k_scale, v_scale
+        _p, _p,                # seq_lens, route
         _p, _p,                # out, lse
         _i, _i, _i, _i, _i,    # B, Smax, Hq, Hkv, head_dim
         _i, _f,                # window, scale_log2

@@ -197,10 +197,14 @@ size_t swa_decode_workspace_bytes(int B, int Smax, int Hq, int Hkv) {
   return decode_ws_bytes(B, Hkv, decode_split(B, Smax, Hq, Hkv, nsm));
 }
 
-int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_lens,
-                       const uint8_t* route, void* out, float* lse, int B, int Smax, int Hq, int Hkv,
-                       int head_dim, int window, float scale_log2, void* workspace, size_t workspace_bytes,
-                       void* stream) {
+}  // extern "C"
+
+namespace {
+
+int decode_forward_impl(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                        const float* v_scale, bool fp8, const int32_t* seq_lens, const uint8_t* route, void* out,
+                        float* lse, int B, int Smax, int Hq, int Hkv, int head_dim, int window, float scale_log2,
+                        void* workspace, size_t workspace_bytes, void* stream) {
   if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
   if (B <= 0 || Smax <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
   if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
@@ -213,6 +217,7 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
     return fail(SWA_E_INVALID, "q/k/v/out/workspace must be 16-byte aligned");
   if (static_cast<int64_t>(B) * Smax * Hkv >= (int64_t(1) << 31))
     return fail(SWA_E_UNSUPPORTED, "KV cache too large for 32-bit row indices");
+  if (fp8 && (k_scale == nullptr || v_scale == nullptr)) return fail(SWA_E_INVALID, "FP8 cache needs k/v scales");
   int nsm = 0;
   int rc = device_sms(&nsm);
   if (rc != SWA_OK) return rc;
@@ -220,11 +225,23 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
   if (workspace_bytes < decode_ws_bytes(B, Hkv, d)) return fail(SWA_E_INVALID, "workspace too small");
 
   swa::DecodeParams p{};
-  const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Smax), static_cast<uint64_t>(B)};
-  const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Smax) * Hkv * 256};
-  const uint32_t kb[4] = {64, 1, 64, 1};
-  if (!swa::make_bf16_map_sw128(&p.k_map, k_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
-  if (!swa::make_bf16_map_sw128(&p.v_map, v_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  if (fp8) {
+    // bytes: 128 per (key, KV head); one box = 64 keys x 128 bytes
+    const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Smax), static_cast<uint64_t>(B)};
+    const uint64_t ks[3] = {128, static_cast<uint64_t>(Hkv) * 128, static_cast<uint64_t>(Smax) * Hkv * 128};
+    const uint32_t kb[4] = {128, 1, 64, 1};
+    if (!swa::make_u8_map_sw128(&p.k_map, k_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+    if (!swa::make_u8_map_sw128(&p.v_map, v_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  } else {
+    const uint64_t kd[4] = {128, static_cast<uint64_t>(Hkv), static_cast<uint64_t>(Smax), static_cast<uint64_t>(B)};
+    const uint64_t ks[3] = {256, static_cast<uint64_t>(Hkv) * 256, static_cast<uint64_t>(Smax) * Hkv * 256};
+    const uint32_t kb[4] = {64, 1, 64, 1};
+    if (!swa::make_bf16_map_sw128(&p.k_map, k_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "k tensor map");
+    if (!swa::make_bf16_map_sw128(&p.v_map, v_cache, 4, kd, ks, kb)) return fail(SWA_E_TMA, "v tensor map");
+  }
+  p.fp8 = fp8 ? 1 : 0;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
   const size_t parts = static_cast<size_t>(B) * Hkv * d.nhb * d.splits;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.status = reinterpret_cast<int32_t*>(ws);
@@ -251,6 +268,26 @@ int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, 
   e = swa::launch_decode(p, s);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return SWA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int swa_decode_forward(const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_lens,
+                       const uint8_t* route, void* out, float* lse, int B, int Smax, int Hq, int Hkv,
+                       int head_dim, int window, float scale_log2, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return decode_forward_impl(q, k_cache, v_cache, nullptr, nullptr, false, seq_lens, route, out, lse, B, Smax, Hq,
+                             Hkv, head_dim, window, scale_log2, workspace, workspace_bytes, stream);
+}
+
+int swa_decode_forward_fp8(const void* q, const void* k_cache, const void* v_cache, const float* k_scale,
+                           const float* v_scale, const int32_t* seq_lens, const uint8_t* route, void* out, float* lse,
+                           int B, int Smax, int Hq, int Hkv, int head_dim, int window, float scale_log2,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_forward_impl(q, k_cache, v_cache, k_scale, v_scale, true, seq_lens, route, out, lse, B, Smax, Hq,
+                             Hkv, head_dim, window, scale_log2, workspace, workspace_bytes, stream);
 }
 
 size_t swa_backward_workspace_bytes(int B, int Hq, int full_stride, int local_stride) {

@@ -38,6 +38,13 @@ constexpr int kDecStages = 2;
 constexpr int kDecTileKeys = 64;
 constexpr int kDecHalfBytes = kDecTileKeys * 128;        // 64 keys x 64 dims x 2 B
 constexpr int kDecStageBytes = 4 * kDecHalfBytes;        // K h0, K h1, V h0, V h1
+// FP8 cache: a stage is the K and V tiles as bytes (64 keys x 128 B each); each math
+// warp converts its 16 keys of a stage to FP16 in a 16-bit tile of the BF16 layout
+// (K then V, 2 x 16 KB) right after the stage's rows arrive, so the two FP8 stages
+// and that tile fill the same 64 KB as the two BF16 stages.
+constexpr int kDecStageBytes8 = 2 * kDecTileKeys * 128;
+constexpr int kDecConvOffset = kDecStages * kDecStageBytes8;
+static_assert(kDecConvOffset + 2 * 2 * kDecHalfBytes <= kDecStages * kDecStageBytes, "FP8 stages + FP16 tile");
 constexpr int kDecThreads = 160;                         // 4 math warps + 1 producer warp
 constexpr int kDecQBytes = 2 * 16 * 128;                 // 16 rows x 2 halves x 128 B
 
@@ -62,6 +69,9 @@ __device__ __forceinline__ DecRange split_range(const DecodeParams& p, int b, in
   return DecRange{s0, min(L, s0 + p.split_keys)};
 }
 
+// kFp8: the K/V cache holds FP8 e4m3 with per-(b, KV head) scales; the products
+// then run in FP16 (Q, the converted K/V and P), exact for the e4m3 inputs.
+template <bool kFp8>
 __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __grid_constant__ DecodeParams p) {
   const int split = blockIdx.x;
   const int g = blockIdx.y / p.nhb;
@@ -105,6 +115,12 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
     uint4 val = make_uint4(0, 0, 0, 0);
     if (hb * 16 + row < p.r)
       val = *reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(b) * p.Hq + head0 + row) * 128 + 8 * c);
+    if constexpr (kFp8) {  // BF16 -> FP16 (the FP16 products of the FP8 path)
+      uint32_t w[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = pack_f16x2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xFFFF0000u));
+      val = make_uint4(w[0], w[1], w[2], w[3]);
+    }
     *reinterpret_cast<uint4*>(smem + DecSmem::q + swz(16, row, c)) = val;
   }
   __syncthreads();
@@ -118,13 +134,20 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
       for (; t < ntiles; ++t) {
         const int s = t % kDecStages;
         if (!mbar_wait(&empty[s], ((t / kDecStages) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], kDecStageBytes);
-        uint8_t* dst = smem + DecSmem::stages + s * kDecStageBytes;
         const int key0 = rg.s0 + t * kDecTileKeys;
-        tma_load_4d(dst, &p.k_map, &full[s], 0, g, key0, b);
-        tma_load_4d(dst + kDecHalfBytes, &p.k_map, &full[s], 64, g, key0, b);
-        tma_load_4d(dst + 2 * kDecHalfBytes, &p.v_map, &full[s], 0, g, key0, b);
-        tma_load_4d(dst + 3 * kDecHalfBytes, &p.v_map, &full[s], 64, g, key0, b);
+        if constexpr (kFp8) {
+          mbar_arrive_expect_tx(&full[s], kDecStageBytes8);
+          uint8_t* dst = smem + DecSmem::stages + s * kDecStageBytes8;
+          tma_load_4d(dst, &p.k_map, &full[s], 0, g, key0, b);
+          tma_load_4d(dst + kDecTileKeys * 128, &p.v_map, &full[s], 0, g, key0, b);
+        } else {
+          mbar_arrive_expect_tx(&full[s], kDecStageBytes);
+          uint8_t* dst = smem + DecSmem::stages + s * kDecStageBytes;
+          tma_load_4d(dst, &p.k_map, &full[s], 0, g, key0, b);
+          tma_load_4d(dst + kDecHalfBytes, &p.k_map, &full[s], 64, g, key0, b);
+          tma_load_4d(dst + 2 * kDecHalfBytes, &p.v_map, &full[s], 0, g, key0, b);
+          tma_load_4d(dst + 3 * kDecHalfBytes, &p.v_map, &full[s], 64, g, key0, b);
+        }
       }
       if (*abort_flag) {
         // let the loads already issued land before the CTA's shared memory is released
@@ -152,14 +175,46 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
     float o[16][4];
 #pragma unroll
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    const float sl2 = p.scale_log2;
+    const float sl2 = kFp8 ? p.scale_log2 * p.k_scale[b * p.Hkv + g] : p.scale_log2;
     const int klo = p.route[b] != 0 ? 0 : max(0, min(max(p.seq_lens[b], 0), p.Smax) - p.window);
     const int khi = rg.s1;
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % kDecStages;
       if (!mbar_wait(&full[s], (t / kDecStages) & 1, abort_flag)) break;
-      const uint32_t kb = smem_u32(smem + DecSmem::stages + s * kDecStageBytes);
-      const uint32_t vb = kb + 2 * kDecHalfBytes;
+      uint32_t kb, vb;
+      if constexpr (kFp8) {
+        // this warp's 16 keys of the K and V byte tiles (row k at k * 128, 16-byte
+        // chunk c at c ^ (k & 7)) -> FP16 in the 16-bit tile layout; the FP8 stage is
+        // free again as soon as every warp has converted its rows
+        const uint8_t* src8 = smem + DecSmem::stages + s * kDecStageBytes8;
+        uint8_t* conv = smem + DecSmem::stages + kDecConvOffset;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int idx = lane + 32 * i;
+          const int tsr = idx >> 7;                  // 0 = K, 1 = V
+          const int key = 16 * warp + ((idx & 127) >> 3);
+          const int c = idx & 7;                     // 16 dims per byte chunk
+          const uint4 v8 = *reinterpret_cast<const uint4*>(src8 + tsr * kDecTileKeys * 128 + key * 128 +
+                                                           ((c ^ (key & 7)) << 4));
+          const uint32_t w[4] = {v8.x, v8.y, v8.z, v8.w};
+          uint32_t h[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            h[2 * e] = e4m3x2_to_f16x2(static_cast<uint16_t>(w[e] & 0xFFFFu));
+            h[2 * e + 1] = e4m3x2_to_f16x2(static_cast<uint16_t>(w[e] >> 16));
+          }
+          uint8_t* dst = conv + tsr * 2 * kDecHalfBytes;
+          *reinterpret_cast<uint4*>(dst + swz(kDecTileKeys, key, 2 * c)) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(dst + swz(kDecTileKeys, key, 2 * c + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        kb = smem_u32(conv);
+        vb = kb + 2 * kDecHalfBytes;
+      } else {
+        kb = smem_u32(smem + DecSmem::stages + s * kDecStageBytes);
+        vb = kb + 2 * kDecHalfBytes;
+      }
       // S = Q K^T for this warp's 16 keys (two n tiles of 8)
       float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -169,8 +224,13 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
         const int c = 2 * ks + (mat & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(kb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
-        mma_bf16(sc[0], qa[ks], b0, b1);
-        mma_bf16(sc[1], qa[ks], b2, b3);
+        if constexpr (kFp8) {
+          mma_f16(sc[0], qa[ks], b0, b1);
+          mma_f16(sc[1], qa[ks], b2, b3);
+        } else {
+          mma_bf16(sc[0], qa[ks], b0, b1);
+          mma_bf16(sc[1], qa[ks], b2, b3);
+        }
       }
       // mask, online softmax (rows qr, qr + 8)
       const int key0 = rg.s0 + t * kDecTileKeys + 16 * warp;
@@ -204,8 +264,13 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
           pv[e] = (mh == -INFINITY) ? 0.0f : ex2_approx(sc[n][e] - mh);
           l[e >> 1] += pv[e];
         }
-        pa[2 * n] = pack_bf16x2(pv[0], pv[1]);
-        pa[2 * n + 1] = pack_bf16x2(pv[2], pv[3]);
+        if constexpr (kFp8) {
+          pa[2 * n] = pack_f16x2(pv[0], pv[1]);
+          pa[2 * n + 1] = pack_f16x2(pv[2], pv[3]);
+        } else {
+          pa[2 * n] = pack_bf16x2(pv[0], pv[1]);
+          pa[2 * n + 1] = pack_bf16x2(pv[2], pv[3]);
+        }
       }
       // O of earlier tiles to the new running maximum
 #pragma unroll
@@ -224,11 +289,16 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
         const int c = nd + (mat >> 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(vb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
-        mma_bf16(o[nd], a, b0, b1);
-        mma_bf16(o[nd + 1], a, b2, b3);
+        if constexpr (kFp8) {
+          mma_f16(o[nd], a, b0, b1);
+          mma_f16(o[nd + 1], a, b2, b3);
+        } else {
+          mma_bf16(o[nd], a, b0, b1);
+          mma_bf16(o[nd + 1], a, b2, b3);
+        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (!kFp8 && lane == 0) mbar_arrive(&empty[s]);
     }
     // row sums over the quad
 #pragma unroll
@@ -256,6 +326,7 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
 #pragma unroll
       for (int w = 0; w < 4; ++w) mc = fmaxf(mc, ml[(w * 16 + row) * 2]);
       f[h] = (m[h] == -INFINITY) ? 0.0f : ex2_approx(m[h] - mc);
+      if constexpr (kFp8) f[h] *= p.v_scale[b * p.Hkv + g];  // O of the FP8 values -> O of K/V x scale
       if (warp == 0 && (lane & 3) == 0) {
         float lc = 0.0f;
 #pragma unroll
@@ -335,17 +406,24 @@ __global__ void __launch_bounds__(128) switch_decode_combine_kernel(const __grid
 uint32_t decode_smem_bytes() { return kDecSmemBytes; }
 
 cudaError_t launch_decode(const DecodeParams& params, cudaStream_t stream) {
-  static bool attr_set[64] = {};
+  static bool attr_set[2][64] = {};
+  const int f8 = params.fp8 != 0 ? 1 : 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(switch_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
+  if (dev < 64 && !attr_set[f8][dev]) {
+    cudaError_t e = f8 ? cudaFuncSetAttribute(switch_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kDecSmemBytes)
+                       : cudaFuncSetAttribute(switch_decode_kernel<false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[f8][dev] = true;
   }
   const dim3 grid(params.splits, params.Hkv * params.nhb, params.B);
-  switch_decode_kernel<<<grid, kDecThreads, kDecSmemBytes, stream>>>(params);
+  if (f8) {
+    switch_decode_kernel<true><<<grid, kDecThreads, kDecSmemBytes, stream>>>(params);
+  } else {
+    switch_decode_kernel<false><<<grid, kDecThreads, kDecSmemBytes, stream>>>(params);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   switch_decode_combine_kernel<<<dim3(params.Hkv * params.nhb, params.B), 128, 0, stream>>>(params);

@@ -70,8 +70,13 @@ cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream
 
 // Decode step: one query token per sequence against its KV cache.
 struct __align__(64) DecodeParams {
-  CUtensorMap k_map;  // 4-D {128, Hkv, Smax, B}, box {64, 1, 64, 1}, 128B swizzle
+  // BF16 cache: 4-D {128, Hkv, Smax, B}, box {64, 1, 64, 1}, 128B swizzle.
+  // FP8 cache (fp8 != 0): bytes, 4-D {128, Hkv, Smax, B}, box {128, 1, 64, 1}.
+  CUtensorMap k_map;
   CUtensorMap v_map;
+  int fp8;                  // K/V cache in FP8 e4m3 with per-(b, KV head) scales
+  const float* k_scale;     // [B, Hkv] (fp8 only): K = k_cache * k_scale
+  const float* v_scale;     // [B, Hkv] (fp8 only): V = v_cache * v_scale
   const __nv_bfloat16* q;   // [B, Hq, 128]
   const int32_t* seq_lens;  // [B] cached keys including the new token
   const uint8_t* route;     // [B] non-zero = full attention

@@ -48,6 +48,27 @@ inline bool make_bf16_map_sw128(CUtensorMap* map, const void* base, int rank, co
   return r == CUDA_SUCCESS;
 }
 
+// Byte (FP8) tensor map with 128-byte swizzle; dims/strides as make_bf16_map_sw128.
+inline bool make_u8_map_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                              const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (fn == nullptr) return false;
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_bytes[i];
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<cuuint32_t>(rank), const_cast<void*>(base), gdim,
+                  gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 2-D int32 tensor map without swizzle (rows of dims[0] elements, row stride
 // `row_bytes`), e.g. 16-byte records copied into shared memory as they lie.
 inline bool make_i32_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes,

@@ -17,9 +17,22 @@ from . import _core, _native
 from ._core import LOG2E
 
 
+def _scales(x, B: int, Hkv: int, dev, name: str) -> torch.Tensor:
+    """FP32 ``[B, Hkv]`` contiguous scales on ``dev`` from a number, ``[Hkv]`` or ``[B, Hkv]``."""
+    t = torch.as_tensor(x, dtype=torch.float32, device=dev)
+    if t.ndim == 0:
+        t = t.expand(B, Hkv)
+    elif t.ndim == 1 and t.shape[0] == Hkv:
+        t = t.unsqueeze(0).expand(B, Hkv)
+    if tuple(t.shape) != (B, Hkv):
+        raise ValueError(f"{name} must be a number, [Hkv] or [B, Hkv]")
+    return t.contiguous()
+
+
 def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                               seq_lens: torch.Tensor, route_full: torch.Tensor, *, window_size: int = 1024,
-                              sm_scale: float | None = None, status_out: torch.Tensor | None = None):
+                              sm_scale: float | None = None, status_out: torch.Tensor | None = None,
+                              k_scale: torch.Tensor | float | None = None, v_scale: torch.Tensor | float | None = None):
     """Attention of each sequence's new token over its KV cache.
 
     ``q``: BF16 ``[B, Hq, 128]`` (or ``[B, 1, Hq, 128]``); ``k_cache`` / ``v_cache``:
@@ -31,15 +44,26 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     ``status_out``: optional int32 device tensor whose element 0 receives the
     launch's status word on the current stream (no host sync); non-zero
     (``STATUS_TIMEOUT``) means the outputs are undefined.
+
+    FP8 cache: ``k_cache`` / ``v_cache`` of dtype ``torch.float8_e4m3fn`` with
+    ``k_scale`` / ``v_scale`` (FP32 ``[B, Hkv]``, ``[Hkv]`` or a number): the
+    attention uses ``k_cache * k_scale`` and ``v_cache * v_scale``.  Half the bytes
+    of the BF16 step; the products run in FP16, so ``q`` must lie within the FP16
+    range.
     """
     squeeze = q.ndim == 4
     if squeeze:
         if q.shape[1] != 1:
             raise ValueError("decode takes one query token per sequence")
         q = q[:, 0]
+    fp8 = isinstance(k_cache, torch.Tensor) and k_cache.dtype == torch.float8_e4m3fn
+    cache_dtype = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    if not isinstance(q, torch.Tensor) or q.dtype != torch.bfloat16 or not q.is_cuda:
+        raise TypeError("q must be a device-resident bfloat16 tensor")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if not isinstance(t, torch.Tensor) or t.dtype != cache_dtype or not t.is_cuda:
+            raise TypeError(f"{name} must be a device-resident bfloat16 tensor, or float8_e4m3fn for both caches")
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
-        if not isinstance(t, torch.Tensor) or t.dtype != torch.bfloat16 or not t.is_cuda:
-            raise TypeError(f"{name} must be a device-resident bfloat16 tensor")
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
     if q.ndim != 3 or k_cache.ndim != 4 or v_cache.shape != k_cache.shape:
@@ -64,6 +88,13 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     scale = (sm_scale if sm_scale is not None else (1.0 / D) ** 0.5) * LOG2E
     if not scale > 0:
         raise ValueError("sm_scale must be positive")
+    if fp8:
+        if k_scale is None or v_scale is None:
+            raise ValueError("an FP8 KV cache needs k_scale and v_scale")
+        k_scale = _scales(k_scale, B, Hkv, dev, "k_scale")
+        v_scale = _scales(v_scale, B, Hkv, dev, "v_scale")
+    elif k_scale is not None or v_scale is not None:
+        raise ValueError("k_scale / v_scale apply to an FP8 KV cache only")
     _core._check_status_out(status_out, dev)
     lib = _native.load()
     out = torch.empty_like(q)
@@ -75,10 +106,17 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
                                lib.swa_last_error_string().decode(errors="replace"))
         ws = torch.empty((nbytes + 15) // 16 * 4, dtype=torch.int32, device=dev)
         route = route_full.contiguous().view(torch.uint8)
-        rc = lib.swa_decode_forward(_native.ptr(q), _native.ptr(k_cache), _native.ptr(v_cache),
-                                    _native.ptr(seq_lens.contiguous()), _native.ptr(route), _native.ptr(out),
-                                    _native.ptr(lse), B, Smax, Hq, Hkv, D, int(window_size), float(scale),
-                                    _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
+        if fp8:
+            rc = lib.swa_decode_forward_fp8(_native.ptr(q), _native.ptr(k_cache), _native.ptr(v_cache),
+                                            _native.ptr(k_scale), _native.ptr(v_scale),
+                                            _native.ptr(seq_lens.contiguous()), _native.ptr(route), _native.ptr(out),
+                                            _native.ptr(lse), B, Smax, Hq, Hkv, D, int(window_size), float(scale),
+                                            _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
+        else:
+            rc = lib.swa_decode_forward(_native.ptr(q), _native.ptr(k_cache), _native.ptr(v_cache),
+                                        _native.ptr(seq_lens.contiguous()), _native.ptr(route), _native.ptr(out),
+                                        _native.ptr(lse), B, Smax, Hq, Hkv, D, int(window_size), float(scale),
+                                        _native.ptr(ws), ws.numel() * 4, _native.stream_ptr(dev))
     _native.check(rc, "switch_gqa_decode_forward")
     if status_out is not None or _core.CHECK_DEVICE_STATUS:
         _core.publish_status(ws[0:1], status_out)

@@ -94,3 +94,56 @@ def test_decode_arguments(cuda_device):
         switch_gqa_decode_forward(q.float(), k, k, lens, route)
     O, L = switch_gqa_decode_forward(q.unsqueeze(1), k, k, lens, route)
     assert O.shape == (2, 1, 8, 128) and L.shape == (2, 1, 8)
+
+
+def _fp8_cache(k, v, seed):
+    """FP8 e4m3 caches with per-(b, KV head) scales (amax / 448, as a quantiser would
+    choose them) and the dequantised FP32 values the oracle sees."""
+    g = torch.Generator().manual_seed(seed)
+    B, _, Hkv, _ = k.shape
+    ks = (k.float().abs().amax(dim=(1, 3)) / 448.0) * (0.5 + torch.rand(B, Hkv, generator=g))
+    vs = (v.float().abs().amax(dim=(1, 3)) / 448.0) * (0.5 + torch.rand(B, Hkv, generator=g))
+    k8 = (k.float() / ks[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    v8 = (v.float() / vs[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    kd = k8.float() * ks[:, None, :, None]
+    vd = v8.float() * vs[:, None, :, None]
+    return k8, v8, ks, vs, kd, vd
+
+
+@pytest.mark.parametrize("B,Smax,Hq,Hkv,W", [
+    (1, 1, 8, 2, 16), (3, 100, 8, 2, 1), (5, 1000, 32, 8, 200), (2, 3000, 32, 1, 512), (7, 777, 6, 3, 64),
+    (33, 700, 32, 8, 128), (2, 20000, 32, 4, 2048),
+])
+def test_decode_fp8_cache_matches_oracle(cuda_device, B, Smax, Hq, Hkv, W):
+    # FP8 e4m3 K/V with per-(b, KV head) scales: the oracle attends over the
+    # dequantised cache; the kernel's FP16 products keep the prefill tolerances
+    q, k, v, lens, route = _case(cuda_device, B, Smax, Hq, Hkv, seed=B * 31 + Smax + W)
+    k8, v8, ks, vs, kd, vd = _fp8_cache(k, v, seed=B + W)
+    O, L = switch_gqa_decode_forward(q.to(cuda_device), k8.to(cuda_device), v8.to(cuda_device),
+                                     lens.to(cuda_device), route.to(cuda_device), window_size=W,
+                                     k_scale=ks.to(cuda_device), v_scale=vs.to(cuda_device))
+    torch.cuda.synchronize()
+    Oref, Lref = oracle_attn.decode_rows(q, kd, vd, lens.numpy(), route.numpy(), window=W)
+    _check(O, L, Oref, Lref, f"fp8 B={B} Smax={Smax} Hq={Hq} Hkv={Hkv} W={W}")
+
+
+def test_decode_fp8_scale_forms_and_bf16_agreement(cuda_device):
+    # one number, [Hkv] and [B, Hkv] scales give the same result; with power-of-two
+    # scales the dequantised cache is exact in BF16, and the BF16 step on it agrees
+    q, k, v, lens, route = _case(cuda_device, 4, 1500, 16, 4, seed=12)
+    k8 = (k.float() * 4).clamp(-448, 448).to(torch.float8_e4m3fn)
+    v8 = (v.float() * 4).clamp(-448, 448).to(torch.float8_e4m3fn)
+    dev = cuda_device
+    args = (q.to(dev), k8.to(dev), v8.to(dev), lens.to(dev), route.to(dev))
+    outs = [switch_gqa_decode_forward(*args, window_size=200, k_scale=s, v_scale=s)
+            for s in (0.25, torch.full((4,), 0.25), torch.full((4, 4), 0.25))]
+    torch.cuda.synchronize()
+    for O, L in outs[1:]:
+        assert torch.equal(O, outs[0][0]) and torch.equal(L, outs[0][1])
+    kb = (k8.float() * 0.25).bfloat16().to(dev)
+    vb = (v8.float() * 0.25).bfloat16().to(dev)
+    Ob, Lb = switch_gqa_decode_forward(q.to(dev), kb, vb, lens.to(dev), route.to(dev), window_size=200)
+    torch.cuda.synchronize()
+    _check(outs[0][0], outs[0][1], Ob.float().cpu(), Lb.cpu(), "fp8 vs bf16 on the same values")
+    with pytest.raises(ValueError):
+        switch_gqa_decode_forward(*args, window_size=200)  # scales are required
