@@ -15,8 +15,14 @@
 //   warps 0-3 math   : warp w takes keys [16 w, 16 w + 16) of every tile:
 //                      S = Q K^T and O += P V with mma.sync m16n8k16 (BF16 in,
 //                      FP32 accumulate; the 16-row M dimension holds the
-//                      head block), online softmax in the log2 domain, P
-//                      rounded to BF16 before P V as in the prefill path.
+//                      head block), online softmax in the log2 domain (the
+//                      running max raised, and O rescaled, only when it grows
+//                      by more than 8), P rounded to BF16 before P V as in the
+//                      prefill path.
+//   FP8 e4m3 cache (switch_decode_kernel<true>): 64-key K and V byte tiles in a
+//   4-entry ring; the math warps load their fragments from the bytes and
+//   convert them to FP16 in registers (FP16 products, k_scale folded into the
+//   score scale, v_scale into the merge).
 //   The four warps' (max, sum, O) are merged in shared memory; the split's
 //   partial goes to the workspace and a second kernel merges the splits and
 //   writes O (BF16) and LSE (FP32, log2 units).
@@ -38,21 +44,23 @@ constexpr int kDecStages = 2;
 constexpr int kDecTileKeys = 64;
 constexpr int kDecHalfBytes = kDecTileKeys * 128;        // 64 keys x 64 dims x 2 B
 constexpr int kDecStageBytes = 4 * kDecHalfBytes;        // K h0, K h1, V h0, V h1
-// FP8 cache: a stage is the K and V tiles as bytes (64 keys x 128 B each); each math
-// warp converts its 16 keys of a stage to FP16 in a 16-bit tile of the BF16 layout
-// (K then V, 2 x 16 KB) right after the stage's rows arrive, so the two FP8 stages
-// and that tile fill the same 64 KB as the two BF16 stages.
+// FP8 cache: a stage is the K and V tiles as bytes (64 keys x 128 B each, 128B
+// swizzle), 16 KB; four of them fill the 64 KB of the two BF16 stages.  The math
+// warps read their MMA fragments straight from the byte tiles (ldmatrix on the
+// bytes as 16-bit elements) and convert them in registers.
 constexpr int kDecStageBytes8 = 2 * kDecTileKeys * 128;
-constexpr int kDecConvOffset = kDecStages * kDecStageBytes8;
-static_assert(kDecConvOffset + 2 * 2 * kDecHalfBytes <= kDecStages * kDecStageBytes, "FP8 stages + FP16 tile");
+constexpr float kDecRescale = 8.0f;  // log2 units: running-max growth that forces an O rescale
+constexpr int kDecStages8 = 4;
+constexpr int kDecMaxStages = 4;
+static_assert(kDecStages8 * kDecStageBytes8 <= kDecStages * kDecStageBytes, "FP8 stages in the BF16 stage region");
 constexpr int kDecThreads = 160;                         // 4 math warps + 1 producer warp
 constexpr int kDecQBytes = 2 * 16 * 128;                 // 16 rows x 2 halves x 128 B
 
 struct DecSmem {
   static constexpr uint32_t stages = 0;
   static constexpr uint32_t q = stages + kDecStages * kDecStageBytes;
-  static constexpr uint32_t bars = q + kDecQBytes;       // full[4], empty[4]
-  static constexpr uint32_t misc = bars + 2 * kDecStages * 8;
+  static constexpr uint32_t bars = q + kDecQBytes;       // full[kDecMaxStages], empty[kDecMaxStages]
+  static constexpr uint32_t misc = bars + 2 * kDecMaxStages * 8;
   static constexpr uint32_t ml = misc + 16;              // [4 warps][16 rows][2] floats
   static constexpr uint32_t total = ml + 4 * 16 * 2 * 4;
 };
@@ -94,13 +102,14 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kSt = kFp8 ? kDecStages8 : kDecStages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + DecSmem::bars);
-  uint64_t* empty = full + kDecStages;
+  uint64_t* empty = full + kDecMaxStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + DecSmem::misc);
   float* ml = reinterpret_cast<float*>(smem + DecSmem::ml);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDecStages; ++s) {
+    for (int s = 0; s < kSt; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
     }
@@ -108,19 +117,14 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
     fence_barrier_init();
   }
   // Q head block into shared memory (two 64-dim halves, 128B swizzle): thread t
-  // copies 16-byte chunks; rows of heads past r are zero
+  // copies 16-byte chunks; rows of heads past r are zero.  The FP8 path builds its
+  // Q fragments from global memory instead.
   const int head0 = g * p.r + hb * 16;
-  for (int i = threadIdx.x; i < 16 * 16; i += kDecThreads) {
+  for (int i = threadIdx.x; !kFp8 && i < 16 * 16; i += kDecThreads) {
     const int row = i >> 4, c = i & 15;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (hb * 16 + row < p.r)
       val = *reinterpret_cast<const uint4*>(p.q + (static_cast<int64_t>(b) * p.Hq + head0 + row) * 128 + 8 * c);
-    if constexpr (kFp8) {  // BF16 -> FP16 (the FP16 products of the FP8 path)
-      uint32_t w[4] = {val.x, val.y, val.z, val.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) w[e] = pack_f16x2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xFFFF0000u));
-      val = make_uint4(w[0], w[1], w[2], w[3]);
-    }
     *reinterpret_cast<uint4*>(smem + DecSmem::q + swz(16, row, c)) = val;
   }
   __syncthreads();
@@ -132,8 +136,8 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
       tma_prefetch_desc(&p.v_map);
       int t = 0;
       for (; t < ntiles; ++t) {
-        const int s = t % kDecStages;
-        if (!mbar_wait(&empty[s], ((t / kDecStages) & 1) ^ 1, abort_flag)) break;
+        const int s = t % kSt;
+        if (!mbar_wait(&empty[s], ((t / kSt) & 1) ^ 1, abort_flag)) break;
         const int key0 = rg.s0 + t * kDecTileKeys;
         if constexpr (kFp8) {
           mbar_arrive_expect_tx(&full[s], kDecStageBytes8);
@@ -151,25 +155,45 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
       }
       if (*abort_flag) {
         // let the loads already issued land before the CTA's shared memory is released
-        for (int u = max(0, t - kDecStages); u < t; ++u) {
+        for (int u = max(0, t - kSt); u < t; ++u) {
           volatile int dummy = 0;
-          mbar_wait(&full[u % kDecStages], (u / kDecStages) & 1, &dummy);
+          mbar_wait(&full[u % kSt], (u / kSt) & 1, &dummy);
         }
       }
     }
   } else {
     // ------------------------------------------------------------ math warps
     const uint32_t q_base = smem_u32(smem + DecSmem::q);
-    uint32_t qa[8][4];  // A fragments of the 16 x 128 Q block, one per 16-dim k step
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int mat = lane >> 3;
-      const int row = (mat & 1) * 8 + (lane & 7);
-      const int c = 2 * ks + (mat >> 1);
-      ldsm_x4(q_base + swz(16, row, c), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
-    }
     const int qr = lane >> 2;          // rows qr and qr + 8 of the head block
     const int qc = 2 * (lane & 3);     // columns qc, qc + 1 of each 8-wide n tile
+    uint32_t qa[8][4];  // A fragments of the 16 x 128 Q block, one per 16-dim k step
+    if constexpr (kFp8) {
+      // FP16, with the k slots of each 16-dim step in the order the byte tiles give
+      // the K fragments: slots (2j, 2j + 1) = dims (4j, 4j + 1), slots (2j + 8,
+      // 2j + 9) = dims (4j + 2, 4j + 3), j = lane % 4
+      const int j = lane & 3;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int row = qr + 8 * hr;
+          uint2 w = make_uint2(0, 0);
+          if (hb * 16 + row < p.r)
+            w = *reinterpret_cast<const uint2*>(p.q + (static_cast<int64_t>(b) * p.Hq + head0 + row) * 128 +
+                                                16 * ks + 4 * j);
+          qa[ks][hr] = pack_f16x2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u));
+          qa[ks][2 + hr] = pack_f16x2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xFFFF0000u));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int mat = lane >> 3;
+        const int row = (mat & 1) * 8 + (lane & 7);
+        const int c = 2 * ks + (mat >> 1);
+        ldsm_x4(q_base + swz(16, row, c), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+      }
+    }
     float m[2] = {-INFINITY, -INFINITY};
     float l[2] = {0.0f, 0.0f};
     float o[16][4];
@@ -179,55 +203,42 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
     const int klo = p.route[b] != 0 ? 0 : max(0, min(max(p.seq_lens[b], 0), p.Smax) - p.window);
     const int khi = rg.s1;
     for (int t = 0; t < ntiles; ++t) {
-      const int s = t % kDecStages;
-      if (!mbar_wait(&full[s], (t / kDecStages) & 1, abort_flag)) break;
-      uint32_t kb, vb;
-      if constexpr (kFp8) {
-        // this warp's 16 keys of the K and V byte tiles (row k at k * 128, 16-byte
-        // chunk c at c ^ (k & 7)) -> FP16 in the 16-bit tile layout; the FP8 stage is
-        // free again as soon as every warp has converted its rows
-        const uint8_t* src8 = smem + DecSmem::stages + s * kDecStageBytes8;
-        uint8_t* conv = smem + DecSmem::stages + kDecConvOffset;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int idx = lane + 32 * i;
-          const int tsr = idx >> 7;                  // 0 = K, 1 = V
-          const int key = 16 * warp + ((idx & 127) >> 3);
-          const int c = idx & 7;                     // 16 dims per byte chunk
-          const uint4 v8 = *reinterpret_cast<const uint4*>(src8 + tsr * kDecTileKeys * 128 + key * 128 +
-                                                           ((c ^ (key & 7)) << 4));
-          const uint32_t w[4] = {v8.x, v8.y, v8.z, v8.w};
-          uint32_t h[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            h[2 * e] = e4m3x2_to_f16x2(static_cast<uint16_t>(w[e] & 0xFFFFu));
-            h[2 * e + 1] = e4m3x2_to_f16x2(static_cast<uint16_t>(w[e] >> 16));
-          }
-          uint8_t* dst = conv + tsr * 2 * kDecHalfBytes;
-          *reinterpret_cast<uint4*>(dst + swz(kDecTileKeys, key, 2 * c)) = make_uint4(h[0], h[1], h[2], h[3]);
-          *reinterpret_cast<uint4*>(dst + swz(kDecTileKeys, key, 2 * c + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        kb = smem_u32(conv);
-        vb = kb + 2 * kDecHalfBytes;
-      } else {
-        kb = smem_u32(smem + DecSmem::stages + s * kDecStageBytes);
-        vb = kb + 2 * kDecHalfBytes;
-      }
+      const int s = t % kSt;
+      if (!mbar_wait(&full[s], (t / kSt) & 1, abort_flag)) break;
+      const uint32_t kb = kFp8 ? smem_u32(smem + DecSmem::stages + s * kDecStageBytes8)
+                               : smem_u32(smem + DecSmem::stages + s * kDecStageBytes);
+      const uint32_t vb = kFp8 ? kb + kDecTileKeys * 128 : kb + 2 * kDecHalfBytes;
       // S = Q K^T for this warp's 16 keys (two n tiles of 8)
       float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if constexpr (kFp8) {
+        // one ldmatrix.x4 on the byte tile (8 keys x 16 bytes per matrix): matrices
+        // (keys 0-7, step ks), (0-7, ks + 1), (8-15, ks), (8-15, ks + 1) of this warp's
+        // keys; lane l gets bytes 4 (l % 4) .. + 3 of key l / 4, i.e. dims 4j .. 4j + 3
+        // of the step, two FP16 pairs = the B fragment in the permuted k order of qa
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int mat = lane >> 3;
-        const int key = 16 * warp + (mat >> 1) * 8 + (lane & 7);
-        const int c = 2 * ks + (mat & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
-        if constexpr (kFp8) {
-          mma_f16(sc[0], qa[ks], b0, b1);
-          mma_f16(sc[1], qa[ks], b2, b3);
-        } else {
+        for (int ks = 0; ks < 8; ks += 2) {
+          const int mat = lane >> 3;
+          const int key = 16 * warp + (mat >> 1) * 8 + (lane & 7);
+          const int c = ks + (mat & 1);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(kb + key * 128 + ((c ^ (key & 7)) << 4), r0, r1, r2, r3);
+          mma_f16(sc[0], qa[ks], e4m3x2_to_f16x2(static_cast<uint16_t>(r0)),
+                  e4m3x2_to_f16x2(static_cast<uint16_t>(r0 >> 16)));
+          mma_f16(sc[1], qa[ks], e4m3x2_to_f16x2(static_cast<uint16_t>(r2)),
+                  e4m3x2_to_f16x2(static_cast<uint16_t>(r2 >> 16)));
+          mma_f16(sc[0], qa[ks + 1], e4m3x2_to_f16x2(static_cast<uint16_t>(r1)),
+                  e4m3x2_to_f16x2(static_cast<uint16_t>(r1 >> 16)));
+          mma_f16(sc[1], qa[ks + 1], e4m3x2_to_f16x2(static_cast<uint16_t>(r3)),
+                  e4m3x2_to_f16x2(static_cast<uint16_t>(r3 >> 16)));
+        }
+      } else {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int mat = lane >> 3;
+          const int key = 16 * warp + (mat >> 1) * 8 + (lane & 7);
+          const int c = 2 * ks + (mat & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
           mma_bf16(sc[0], qa[ks], b0, b1);
           mma_bf16(sc[1], qa[ks], b2, b3);
         }
@@ -244,15 +255,34 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
           sc[n][e] = x;
           mx[e >> 1] = fmaxf(mx[e >> 1], x);
         }
-      float alpha[2];
+      // The running max is only raised (and O, l rescaled) when the tile's max
+      // exceeds it by more than kDecRescale: the (max, sum, O) triple stays
+      // consistent, so the merged result is the same, and P stays below 2^kDecRescale.
+      bool grow[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
         mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-        const float mn = fmaxf(m[h], mx[h]);
-        alpha[h] = (mn == -INFINITY) ? 1.0f : ex2_approx(m[h] - mn);
-        m[h] = mn;
-        l[h] *= alpha[h];
+        grow[h] = mx[h] > m[h] + kDecRescale;  // false while both are -inf
+      }
+      if (__any_sync(0xffffffffu, grow[0] || grow[1])) {
+        float alpha[2] = {1.0f, 1.0f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (grow[h]) {
+            alpha[h] = ex2_approx(m[h] - mx[h]);  // 0 for the first legal tile (m = -inf)
+            m[h] = mx[h];
+            l[h] *= alpha[h];
+          }
+        }
+        // O of earlier tiles to the new running maximum
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][0] *= alpha[0];
+          o[n][1] *= alpha[0];
+          o[n][2] *= alpha[1];
+          o[n][3] *= alpha[1];
+        }
       }
       uint32_t pa[4];
 #pragma unroll
@@ -272,33 +302,48 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
           pa[2 * n + 1] = pack_bf16x2(pv[2], pv[3]);
         }
       }
-      // O of earlier tiles to the new running maximum
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][0] *= alpha[0];
-        o[n][1] *= alpha[0];
-        o[n][2] *= alpha[1];
-        o[n][3] *= alpha[1];
-      }
       // O += P V: P (16 rows x 16 keys) as the A fragment, V via transposed ldmatrix
       const uint32_t a[4] = {pa[0], pa[1], pa[2], pa[3]};
+      if constexpr (kFp8) {
+        // ldmatrix.x4.trans on the byte tile: matrices (keys 0-7, 16-dim chunk cc),
+        // (8-15, cc), (0-7, cc + 1), (8-15, cc + 1); lane l gets keys 2j, 2j + 1 (j =
+        // l % 4) of dims 16 cc + 2 (l / 4) and + 1 as bytes [k0 d0, k0 d1, k1 d0, k1 d1].
+        // The (k0, k1) byte pairs of d0 and of d1 are the B fragments of two MMAs whose
+        // n slots are the even and the odd dims of the chunk: o[2 cc] and o[2 cc + 1]
+        // (output column of o[n][e]: out_col below).
 #pragma unroll
-      for (int nd = 0; nd < 16; nd += 2) {
-        const int mat = lane >> 3;
-        const int key = 16 * warp + (mat & 1) * 8 + (lane & 7);
-        const int c = nd + (mat >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
-        if constexpr (kFp8) {
-          mma_f16(o[nd], a, b0, b1);
-          mma_f16(o[nd + 1], a, b2, b3);
-        } else {
+        for (int cc = 0; cc < 8; cc += 2) {
+          const int mat = lane >> 3;
+          const int key = 16 * warp + (mat & 1) * 8 + (lane & 7);
+          const int c = cc + (mat >> 1);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(vb + key * 128 + ((c ^ (key & 7)) << 4), r0, r1, r2, r3);
+          const uint32_t rr[4] = {r0, r1, r2, r3};
+          uint32_t ev[4], od[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            ev[e] = e4m3x2_to_f16x2(static_cast<uint16_t>(__byte_perm(rr[e], 0, 0x0020)));
+            od[e] = e4m3x2_to_f16x2(static_cast<uint16_t>(__byte_perm(rr[e], 0, 0x0031)));
+          }
+          mma_f16(o[2 * cc], a, ev[0], ev[1]);
+          mma_f16(o[2 * cc + 1], a, od[0], od[1]);
+          mma_f16(o[2 * cc + 2], a, ev[2], ev[3]);
+          mma_f16(o[2 * cc + 3], a, od[2], od[3]);
+        }
+      } else {
+#pragma unroll
+        for (int nd = 0; nd < 16; nd += 2) {
+          const int mat = lane >> 3;
+          const int key = 16 * warp + (mat & 1) * 8 + (lane & 7);
+          const int c = nd + (mat >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vb + swz(kDecTileKeys, key, c), b0, b1, b2, b3);
           mma_bf16(o[nd], a, b0, b1);
           mma_bf16(o[nd + 1], a, b2, b3);
         }
       }
       __syncwarp();
-      if (!kFp8 && lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
     // row sums over the quad
 #pragma unroll
@@ -342,12 +387,16 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
     float* acc = reinterpret_cast<float*>(smem + DecSmem::stages);
     for (int i = threadIdx.x; i < 16 * 128; i += 128) acc[i] = 0.0f;
     named_bar_sync(1, 128);
+    // output column of accumulator o[n][e] (e = 0, 1; e = 2, 3 the same for row qr + 8):
+    // BF16 path 8 n + qc + e; FP8 path chunk n / 2, parity n % 2 (even / odd dims):
+    // 16 (n / 2) + 2 qc + 2 e + n % 2
+    auto out_col = [&](int n, int e) { return kFp8 ? 16 * (n >> 1) + 2 * qc + 2 * e + (n & 1) : 8 * n + qc + e; };
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
-      atomicAdd(&acc[qr * 128 + 8 * n + qc], o[n][0] * f[0]);
-      atomicAdd(&acc[qr * 128 + 8 * n + qc + 1], o[n][1] * f[0]);
-      atomicAdd(&acc[(qr + 8) * 128 + 8 * n + qc], o[n][2] * f[1]);
-      atomicAdd(&acc[(qr + 8) * 128 + 8 * n + qc + 1], o[n][3] * f[1]);
+      atomicAdd(&acc[qr * 128 + out_col(n, 0)], o[n][0] * f[0]);
+      atomicAdd(&acc[qr * 128 + out_col(n, 1)], o[n][1] * f[0]);
+      atomicAdd(&acc[(qr + 8) * 128 + out_col(n, 0)], o[n][2] * f[1]);
+      atomicAdd(&acc[(qr + 8) * 128 + out_col(n, 1)], o[n][3] * f[1]);
     }
     named_bar_sync(1, 128);
     const int rows = min(16, p.r - hb * 16);  // head rows that exist
