@@ -174,27 +174,53 @@ __device__ __forceinline__ int64_t replica_row(const PrefillParams& p, int b, in
 
 // Decode work item `it` into a unit; returns false for an empty item.
 //
-// Full-branch items are ordered (b, g)-major: all units of one (batch, KV group),
-// longest first, then the next group.  The CTAs running at one time then stream
-// the K/V prefix of one or two groups (16 MB each at S = 32K), which stays in L2
-// while every unit of the group reads it; ordered by length across all groups,
-// they streamed the prefixes of every group at once and re-read K/V from DRAM.
-// The tail stays short: the last full units of a group are its shortest, and the
-// local-branch units (all about W keys) come after every full unit.
-__device__ bool decode_item(const PrefillParams& p, int it, int nf, int maxnpb0, int maxnpb1, Unit& u) {
-  const int per_level = p.n_bg * p.nhb;
+// Items are ordered (b, g)-major: all full-branch units of one (batch, KV group),
+// longest first, then its local-branch units (last positions first), then the
+// next group.  The CTAs running at one time then stream the K/V of a few groups
+// (16 MB each at S = 32K), which stays in L2 while every unit of those groups,
+// full and local, reads it.  Ordered by length across all groups, the full units
+// streamed the prefixes of every group at once; with every local unit after every
+// full unit, the local units read each group's K/V from DRAM a second time
+// (config 3, B = 4: 2x the K/V bytes).  The tail stays short: the local units of
+// the last kTailGroups groups (all about W keys) come after every full unit,
+// position-block-major over those groups, and fill the CTAs while the last long
+// full units finish (config 3: with 4 such groups a launch took 4 % more cycles
+// than with 8; each group kept for the tail reads its K/V a second time).
+constexpr int kTailGroups = 8;
+
+__device__ bool decode_item(const PrefillParams& p, int it, int maxnpb0, int maxnpb1, Unit& u) {
+  const int per0 = maxnpb0 * p.nhb;  // full-branch items of one group
+  const int per1 = maxnpb1 * p.nhb;  // local-branch items of one group
+  const int n_early = max(p.n_bg - kTailGroups, 0);
+  const int early_items = n_early * (per0 + per1);
   int branch, pb, rem;
-  if (it < nf) {
-    branch = 0;
-    const int per_bg = maxnpb0 * p.nhb;
-    const int within = it % per_bg;
-    pb = maxnpb0 - 1 - within / p.nhb;  // longest full-causal units of the group first
-    rem = (it / per_bg) * p.nhb + within % p.nhb;
+  if (it < early_items) {
+    const int grp = it / (per0 + per1);
+    int w = it - grp * (per0 + per1);
+    if (w < per0) {
+      branch = 0;
+      pb = maxnpb0 - 1 - w / p.nhb;  // longest full-causal units of the group first
+    } else {
+      w -= per0;
+      branch = 1;
+      pb = maxnpb1 - 1 - w / p.nhb;
+    }
+    rem = grp * p.nhb + w % p.nhb;
   } else {
-    it -= nf;
-    branch = 1;
-    pb = maxnpb1 - 1 - it / per_level;
-    rem = it % per_level;
+    it -= early_items;
+    const int n_late = p.n_bg - n_early;
+    if (it < n_late * per0) {
+      branch = 0;
+      const int grp = n_early + it / per0;
+      const int w = it % per0;
+      pb = maxnpb0 - 1 - w / p.nhb;
+      rem = grp * p.nhb + w % p.nhb;
+    } else {
+      it -= n_late * per0;
+      branch = 1;
+      pb = maxnpb1 - 1 - it / (n_late * p.nhb);
+      rem = n_early * p.nhb + it % (n_late * p.nhb);
+    }
   }
   const int bgi = rem / p.nhb;
   const int hb = rem % p.nhb;
@@ -427,8 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       maxnpb1 = max(maxnpb1, (min(branch_count(p, 1, b), p.idx_cap[1]) + p.pc - 1) / p.pc);
     }
     const int per_level = p.n_bg * p.nhb;
-    const int nf = maxnpb0 * per_level;
-    const int total = nf + maxnpb1 * per_level;
+    const int total = (maxnpb0 + maxnpb1) * per_level;
     auto fetch = [&](Unit& u) {
       u.valid = 0;
       while (true) {
@@ -436,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (lane == 0) it = atomicAdd(p.counter, 1);
         it = __shfl_sync(0xffffffffu, it, 0);
         if (it >= total) break;
-        if (decode_item(p, it, nf, maxnpb0, maxnpb1, u)) break;
+        if (decode_item(p, it, maxnpb0, maxnpb1, u)) break;
       }
     };
     uint32_t kv_it = 0;
