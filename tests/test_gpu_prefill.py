@@ -94,6 +94,18 @@ def test_large_gqa_groups(cuda_device, Hq, Hkv, S):
     _run(q, k, v, mask, 64, f"Hq={Hq} Hkv={Hkv}")
 
 
+@pytest.mark.parametrize("B,Hq,Hkv", [(3, 48, 4), (5, 16, 2), (2, 96, 6)])
+def test_many_groups_unit_order(cuda_device, B, Hq, Hkv):
+    # more (batch, KV group) groups than the kernel keeps for the tail, so the
+    # local units of the first groups run between full units; 48/4 also gives
+    # three head blocks per group; rows with no full row, all full rows and mixed
+    S = 640
+    q, k, v = _rand_qkv(B, S, S, Hq, Hkv, 40 + B + Hq, cuda_device)
+    dens = torch.tensor([[0.0], [1.0], [0.3], [0.6], [0.05]])[:B]
+    mask = torch.rand(B, S, generator=torch.Generator().manual_seed(B * Hkv)) < dens
+    _run(q, k, v, mask, 96, f"B={B} Hq={Hq} Hkv={Hkv}")
+
+
 def test_batched_padded_lists(cuda_device):
     B, S = 3, 900
     q, k, v = _rand_qkv(B, S, S, 8, 2, 33, cuda_device)
