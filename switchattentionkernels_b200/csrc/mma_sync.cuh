@@ -44,12 +44,15 @@ __device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, uint32_t b0
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Two FP8 e4m3 values (low byte first) -> two FP16 values (low half first);
-// exact: every e4m3 value is an FP16 value.
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(v));
-  return d;
+// Four FP8 e4m3 values (bytes 0-3) -> two FP16 pairs: lo = (byte 0, byte 1),
+// hi = (byte 2, byte 3); exact.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
 }
 
 // FP16 pair from two floats (lo in the low half), round to nearest.
