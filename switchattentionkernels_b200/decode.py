@@ -37,7 +37,9 @@ def switch_gqa_decode_forward(q: torch.Tensor, k_cache: torch.Tensor, v_cache: t
 
     ``q``: BF16 ``[B, Hq, 128]`` (or ``[B, 1, Hq, 128]``); ``k_cache`` / ``v_cache``:
     BF16 ``[B, Smax, Hkv, 128]`` with the new token's K/V already at row
-    ``seq_lens[b] - 1``; ``seq_lens``: int32 ``[B]`` (``1 <= L <= Smax``);
+    ``seq_lens[b] - 1``; ``seq_lens``: int32 ``[B]`` (``1 <= L <= Smax``; a
+    sequence with ``L = 0`` has no key and gets O = NaN, LSE = -inf, as a prefill
+    row whose key range is empty);
     ``route_full``: bool ``[B]``, True = full causal attention, False = the
     sliding window of the last ``window_size`` keys.  Returns ``(O, LSE)``:
     BF16 ``[B, Hq, 128]`` and FP32 ``[B, Hq]`` (log2 units), shaped like ``q``.

@@ -80,6 +80,24 @@ def test_decode_equals_the_prefill_row_at_the_last_position(cuda_device):
     _check(O, L, Op[:, -1].float().cpu(), Lp[:, -1].cpu(), "decode vs prefill row")
 
 
+@pytest.mark.parametrize("W", [64, 5000])
+def test_decode_sequence_without_keys(cuda_device, W):
+    # a sequence with no cached key (L = 0) has a row sum of 0: O = NaN and LSE = -inf,
+    # as the prefill writes a row whose key range is empty; the other sequences are
+    # unaffected (one of them spans many splits, merged by the last CTA to finish)
+    dev = cuda_device
+    q, k, v, _, route = _case(dev, 3, 6000, 32, 4, seed=91 + W)
+    lens = torch.tensor([0, 6000, 37], dtype=torch.int32)
+    route[:] = torch.tensor([True, True, False])
+    O, L = switch_gqa_decode_forward(q.to(dev), k.to(dev), v.to(dev), lens.to(dev), route.to(dev), window_size=W)
+    torch.cuda.synchronize()
+    O = O.float().cpu()
+    L = L.cpu()
+    assert torch.isnan(O[0]).all() and torch.isneginf(L[0]).all()
+    Oref, Lref = oracle_attn.decode_rows(q[1:], k[1:], v[1:], lens[1:].numpy(), route[1:].numpy(), window=W)
+    _check(O[1:], L[1:], Oref, Lref, f"L = 0 beside others, W={W}")
+
+
 def test_decode_arguments(cuda_device):
     dev = cuda_device
     q = torch.zeros(2, 8, 128, dtype=torch.bfloat16, device=dev)
