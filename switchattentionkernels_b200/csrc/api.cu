@@ -227,6 +227,7 @@ int decode_forward_impl(const void* q, const void* k_cache, const void* v_cache,
   int rc = device_sms(&nsm);
   if (rc != SWA_OK) return rc;
   const DecodeSplit d = decode_split(B, Smax, Hq, Hkv, nsm);
+  if (B > 65535) return fail(SWA_E_UNSUPPORTED, "decode grid: at most 65535 sequences");
   if (workspace_bytes < decode_ws_bytes(B, Hkv, d)) return fail(SWA_E_INVALID, "workspace too small");
 
   swa::DecodeParams p{};
