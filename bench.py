@@ -491,9 +491,44 @@ def run_cp(args, world, rank, local_rank):
 
     md = cp.cp_metadata(S, rows, device=dev, window_size=W, cu_seqlens=cu)
 
-    def step():
+    # K/V exchange: symmetric memory and peer stores (one rank: nothing to exchange)
+    kvx = cp.KVExchange(S, Hkv, device=dev) if world > 1 else None
+
+    def step(exchange=kvx):
         cp.context_parallel_switch_gqa_prefill_forward(ql, kl, vl, fl, ll, total_len=S, cu_seqlens=cu,
-                                                       window_size=W, validate=False, plan=plan, metadata=md)
+                                                       window_size=W, validate=False, plan=plan, metadata=md,
+                                                       kv_exchange=exchange)
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        z.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(z) / n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    extra = {}
+    if kvx is not None:
+        # the same step with the NCCL all-gather + reorder, and each exchange alone
+        for _ in range(2):
+            step(None)
+        extra["kv_exchange_nccl"] = {"ms_per_step": timed(lambda: step(None), args.steps)}
+        extra["kv_exchange_nccl"]["value"] = flops_total / (extra["kv_exchange_nccl"]["ms_per_step"] * 1e-3) / 1e12
+        sent = 2 * kl.numel() * kl.element_size() * (world - 1)  # this rank's K and V to every peer
+        ex_ms = timed(lambda: kvx.exchange(kl, vl, plan), args.steps)
+        nc_ms = timed(lambda: cp.cp_gather_kv(kl, vl, plan), args.steps)
+        extra["kv_exchange"] = {"what": "every rank stores its K/V chunks into every rank's symmetric-memory "
+                                        "buffer (one copy kernel per chunk, plain peer stores), between two "
+                                        "device barriers",
+                                "ms": ex_ms, "bytes_to_peers_rank0": sent, "gbs_per_rank": sent / (ex_ms * 1e6),
+                                "nccl_all_gather_and_reorder_ms": nc_ms,
+                                "reference_nvlink_peer_copy_gbs": 770.0}
 
     for _ in range(args.warmup):
         step()
@@ -528,12 +563,15 @@ def run_cp(args, world, rank, local_rank):
             "config": {"workload": cfg.name, "tokens": S, "sequences": int(cu.numel() - 1), "Hq": Hq, "Hkv": Hkv,
                        "window": W, "p_full": cfg.p_full,
                        "parallelism": f"context parallel over {world} ranks: cost-balanced zigzag rows, "
-                                      "K/V all-gather (NCCL)",
+                                      + ("K/V exchanged by peer stores through symmetric memory" if world > 1
+                                         else "no exchange"),
                        "rows_per_rank_max": plan.capacity,
                        "effective_tflop_per_step": flops_total / 1e12},
             "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst, "peak_source": peak_src,
-            "gpu_launches": args.steps,  # the prefill kernel, once per step and rank
+            # the prefill kernel, plus at N > 1 four exchange copy kernels (two chunks of K and V), per step
+            "gpu_launches": args.steps * (5 if world > 1 else 1),
             "clocks": clock_info,
+            **extra,
         }), flush=True)
     return 0
 

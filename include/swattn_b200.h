@@ -243,6 +243,16 @@ int swa_prefill_forward_replicated(const void* q, const void* k, const void* v, 
  * src -> unit-major dst (a rank's unit slices).  chunk_bytes, row_bytes and the
  * pointers must be multiples of 4; 16 gives 16-byte vector moves.  At most 65535
  * slots. */
+/* Context-parallel K/V exchange (no counterpart in the reference; the reference's
+ * metadata path addresses a gathered key axis, swiattn_gqa_prefill_varlen.py:179-182):
+ * copy `bytes` bytes from src (this GPU) to each of the n_dst (<= 8) destinations
+ * dsts[i] (this GPU's or a peer's memory, e.g. every rank's symmetric-memory K/V
+ * buffer at the chunk's token offset), each 16-byte word loaded once and stored to
+ * every destination with plain stores.  bytes, src and every dsts[i] must be
+ * multiples of 16.  Ordering against the peers is the caller's (a device barrier
+ * of all ranks before and after). */
+int swa_broadcast_bytes(const void* src, size_t bytes, void* const* dsts, int n_dst, void* stream);
+
 int swa_scatter_units(const void* src, const int32_t* unit_of_slot, int n_slots, int S, int hkv, int chunk_bytes,
                       int row_bytes, void* dst, void* stream);
 int swa_gather_units(const void* src, const int32_t* unit_of_slot, int n_slots, int S, int hkv, int chunk_bytes,

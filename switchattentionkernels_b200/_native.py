@@ -45,6 +45,7 @@ EXPORTED = (
     "swa_decode_forward",
     "swa_prefill_backward",
     "swa_backward_workspace_bytes",
+    "swa_broadcast_bytes",
     "swa_scatter_units",
     "swa_gather_units",
     "swa_prefill_forward_replicated",
@@ -158,6 +159,8 @@ def _declare(lib) -> None:
         fn = getattr(lib, name)
         fn.restype = _i
         fn.argtypes = [_p, _p, _i, _i, _i, _i, _i, _p, _p]  # src, unit_of_slot, n_slots, S, hkv, chunk, row, dst, stream
+    lib.swa_broadcast_bytes.restype = _i
+    lib.swa_broadcast_bytes.argtypes = [_p, _sz, _p, _i, _p]  # src, bytes, dsts[], n_dst, stream
 
 
 def load():

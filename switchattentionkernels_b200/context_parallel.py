@@ -10,10 +10,15 @@ restarts at every sequence start, the chunks can instead be cut at equal
 quantiles of a per-row cost (``row_costs``, e.g. ``cp_row_costs`` of the routing
 mask), which gives every rank the same number of legal (row, key) entries.
 
-Each rank owns Q, K and V of its rows.  K and V are exchanged once -- an
-all-gather of the shards (NCCL over NVLink for CUDA tensors) followed by one
-pass of chunk copies into token order -- and every rank then runs the prefill
-kernel on its own query rows against the whole token axis.  The
+Each rank owns Q, K and V of its rows.  K and V are exchanged once, in one of
+two ways: ``KVExchange`` -- every rank's K/V buffer of the whole token axis in
+symmetric memory, each rank writing its two chunks straight into every rank's
+buffer at their token offsets with one copy kernel of plain peer stores over
+NVLink, between two device barriers of all ranks -- or, for any backend,
+``cp_gather_kv``: an all-gather of the shards (NCCL over NVLink for CUDA
+tensors) followed by one pass of chunk copies into token order.  Every rank
+then runs the prefill kernel on its own query rows against the whole token
+axis.  The
 per-row key bounds (``full_starts`` / ``local_starts`` / ``causal_ends``) are those
 of the rows' global positions, so a local row's legal keys are exactly the ones
 it has without the split.
@@ -33,7 +38,9 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import _core
+import ctypes
+
+from . import _core, _native
 from .metadata import SwitchAttentionMetadata, build_switch_attention_metadata
 
 
@@ -149,6 +156,85 @@ def cp_gather_kv(k: torch.Tensor, v: torch.Tensor, plan: ContextParallelPlan, *,
     return out[0], out[1]
 
 
+class KVExchange:
+    """K and V of the whole token axis (``[1, S, Hkv, D]`` each) on every rank of
+    ``group``, in symmetric memory, filled by ``exchange``: each rank stores its
+    two zigzag chunks into every rank's buffers at the chunks' token offsets
+    (``swa_broadcast_bytes``: every word read once, stored to all ranks, plain
+    stores to the peers' memory over NVLink), with a device barrier of all ranks
+    before (nobody still reads the previous contents) and after (every chunk has
+    landed).  No staging buffer, no collective, no reorder pass.  Allocated once
+    per shape and reused; ``k`` / ``v`` are this rank's buffers, which the prefill
+    kernel then reads from this GPU's own memory.  One rank: plain device buffers.
+    """
+
+    def __init__(self, total_len: int, hkv: int, *, device, group=None, head_dim: int = 128,
+                 dtype=torch.bfloat16):
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("KVExchange needs CUDA tensors (use cp_gather_kv on other backends)")
+        shape = (1, total_len, hkv, head_dim)
+        self.shape = shape
+        self.group = group
+        self.world = 1 if not dist.is_initialized() else dist.get_world_size(group)
+        self.rank = 0 if not dist.is_initialized() else dist.get_rank(group)
+        self._handles = None
+        if self.world == 1:
+            self.k = torch.empty(shape, dtype=dtype, device=device)
+            self.v = torch.empty(shape, dtype=dtype, device=device)
+            kp, vp = [self.k.data_ptr()], [self.v.data_ptr()]
+        else:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            g = group if group is not None else dist.group.WORLD
+            if self.world > 8:
+                raise ValueError("KVExchange: at most 8 ranks")
+            self.k = symm_mem.empty(shape, dtype=dtype, device=device)
+            self.v = symm_mem.empty(shape, dtype=dtype, device=device)
+            hk = symm_mem.rendezvous(self.k, g)
+            hv = symm_mem.rendezvous(self.v, g)
+            self._handles = (hk, hv)
+            kp, vp = list(hk.buffer_ptrs), list(hv.buffer_ptrs)
+        self._ptrs = (kp, vp)
+        self._row_bytes = hkv * head_dim * torch.empty((), dtype=dtype).element_size()
+
+    def barrier(self) -> None:
+        """Device-side barrier of all ranks on the current stream (no-op for one rank)."""
+        if self._handles is not None:
+            self._handles[0].barrier(channel=0)
+
+    def exchange(self, k: torch.Tensor, v: torch.Tensor, plan: ContextParallelPlan):
+        """This rank's K/V rows (``[1, L_r, Hkv, D]``, ``plan.rows(rank)``) into every
+        rank's buffers; returns this rank's ``(k, v)`` of the whole token axis."""
+        if plan.world != self.world or plan.total_len != self.shape[1]:
+            raise ValueError("the plan was made for a different world size or token count")
+        rows = plan.rows(self.rank)
+        for t in (k, v):
+            if (t.ndim != 4 or t.shape[0] != 1 or t.shape[1] != rows.size or tuple(t.shape[2:]) != self.shape[2:]
+                    or t.dtype != self.k.dtype or t.device != self.k.device):
+                raise ValueError(f"K/V shards must be [1, {rows.size}, {self.shape[2]}, {self.shape[3]}] "
+                                 f"{self.k.dtype} on {self.k.device}")
+        lib = _native.load()
+        b = plan.bounds
+        r, n = self.rank, 2 * self.world
+        first = int(b[r + 1] - b[r])
+        chunks = ((int(b[r]), int(b[r + 1]), 0), (int(b[n - 1 - r]), int(b[n - r]), first))
+        self.barrier()
+        stream = _native.stream_ptr(self.k.device)
+        with torch.cuda.device(self.k.device):
+            for t, ptrs in ((k.contiguous(), self._ptrs[0]), (v.contiguous(), self._ptrs[1])):
+                for lo, hi, off in chunks:
+                    if hi == lo:
+                        continue
+                    nbytes = (hi - lo) * self._row_bytes
+                    dsts = (ctypes.c_void_p * len(ptrs))(*[p + lo * self._row_bytes for p in ptrs])
+                    rc = lib.swa_broadcast_bytes(ctypes.c_void_p(t.data_ptr() + off * self._row_bytes), nbytes,
+                                                 dsts, len(ptrs), stream)
+                    _native.check(rc, "swa_broadcast_bytes")
+        self.barrier()
+        return self.k, self.v
+
+
 def cp_metadata(total_len: int, rows: np.ndarray, *, device, window_size: int,
                 cu_seqlens: torch.Tensor | None = None) -> SwitchAttentionMetadata:
     """Key bounds of the local query ``rows`` (global row ids) against the whole token axis."""
@@ -166,7 +252,8 @@ def context_parallel_switch_gqa_prefill_forward(q, k, v, full_query_indices, loc
                                                 cu_seqlens=None, window_size: int = 1024, sm_scale=None,
                                                 group=None, validate: bool = True, row_costs=None,
                                                 plan: ContextParallelPlan | None = None,
-                                                metadata: SwitchAttentionMetadata | None = None):
+                                                metadata: SwitchAttentionMetadata | None = None,
+                                                kv_exchange: KVExchange | None = None):
     """Switch Attention prefill of this rank's rows of a context-parallel packed batch.
 
     ``q`` / ``k`` / ``v``: ``[1, L_r, H, 128]`` -- the rows ``plan.rows(rank)`` of the
@@ -180,6 +267,9 @@ def context_parallel_switch_gqa_prefill_forward(q, k, v, full_query_indices, loc
     batch, so a caller running several layers builds it once).
     Returns ``(O, LSE)`` of the local rows, ``[1, L_r, Hq, 128]`` BF16 and
     ``[1, L_r, Hq]`` FP32 (log2 units), equal to those rows of the unsplit forward.
+    ``kv_exchange``: a ``KVExchange`` of this batch's shape and group, which
+    exchanges K/V by peer stores through symmetric memory; without it, the NCCL
+    all-gather of ``cp_gather_kv``.
     Every rank takes part in the K/V exchange, also one that holds no rows.
     """
     world = dist.get_world_size(group)
@@ -191,7 +281,10 @@ def context_parallel_switch_gqa_prefill_forward(q, k, v, full_query_indices, loc
     rows = plan.rows(rank)
     if q.ndim != 4 or q.shape[0] != 1 or q.shape[1] != rows.size:
         raise ValueError(f"Q shard must have shape [1, {rows.size}, Hq, D] on rank {rank}")
-    k_full, v_full = cp_gather_kv(k, v, plan, group=group)
+    if kv_exchange is not None:
+        k_full, v_full = kv_exchange.exchange(k, v, plan)
+    else:
+        k_full, v_full = cp_gather_kv(k, v, plan, group=group)
     if rows.size == 0:
         return torch.empty_like(q), torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
     md = metadata

@@ -90,8 +90,58 @@ int check_args(const void* src, void* dst, const int32_t* unit_of_slot, int n_sl
   return SWA_OK;
 }
 
+struct BroadcastDsts {
+  uint4* p[8];
+  int n;
+};
+
+// Each 16-byte word of src is loaded once and stored to every destination (this
+// GPU's memory or a peer's over NVLink: plain st.global).
+__global__ void __launch_bounds__(256) broadcast_kernel(const uint4* __restrict__ src, size_t words, BroadcastDsts d) {
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < words;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = src[i];
+    for (int t = 0; t < d.n; ++t) d.p[t][i] = v;
+  }
+}
+
 }  // namespace
 }  // namespace swa
+
+extern "C" int swa_broadcast_bytes(const void* src, size_t bytes, void* const* dsts, int n_dst, void* stream) {
+  if (n_dst < 0 || n_dst > 8 || (n_dst > 0 && dsts == nullptr)) {
+    swa::set_last_error("broadcast_bytes: 0 to 8 destinations");
+    return SWA_E_INVALID;
+  }
+  if (bytes == 0 || n_dst == 0) return SWA_OK;
+  if (src == nullptr || bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) != 0) {
+    swa::set_last_error("broadcast_bytes: src and bytes must be multiples of 16");
+    return SWA_E_INVALID;
+  }
+  swa::BroadcastDsts d{};
+  d.n = n_dst;
+  for (int i = 0; i < n_dst; ++i) {
+    if (dsts[i] == nullptr || (reinterpret_cast<uintptr_t>(dsts[i]) & 15u) != 0) {
+      swa::set_last_error("broadcast_bytes: destinations must be non-null and 16-byte aligned");
+      return SWA_E_INVALID;
+    }
+    d.p[i] = static_cast<uint4*>(dsts[i]);
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t words = bytes / 16;
+  const size_t want = (words + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>(want < static_cast<size_t>(8 * sms) ? want : static_cast<size_t>(8 * sms));
+  swa::broadcast_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint4*>(src), words,
+                                                                              d);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    swa::set_last_error(cudaGetErrorString(e));
+    return SWA_E_CUDA;
+  }
+  return SWA_OK;
+}
 
 extern "C" int swa_scatter_units(const void* src, const int32_t* unit_of_slot, int n_slots, int S, int hkv,
                                  int chunk_bytes, int row_bytes, void* dst, void* stream) {

@@ -101,6 +101,26 @@ def test_cp_one_rank_nccl_equals_the_plain_forward(cuda_device):
         dist.destroy_process_group()
 
 
+def test_cp_kv_exchange_one_rank(cuda_device):
+    # one rank: the exchange copies the shard (two zigzag chunks) into its own
+    # buffer; the forward through it equals the plain forward bit for bit
+    dev = cuda_device
+    q, k, v, mask, cu = _problem(dev, S=1500, seed=44)
+    S, W = q.shape[1], 200
+    cu_t = torch.from_numpy(np.array([0, 500, S])).int()
+    plan = cp.make_cp_plan(S, 1)
+    kvx = cp.KVExchange(S, k.shape[2], device=dev)
+    k_full, v_full = kvx.exchange(k, v, plan)
+    torch.cuda.synchronize()
+    assert torch.equal(k_full, k) and torch.equal(v_full, v)
+    md = build_switch_attention_metadata(S, S, device=dev, window_size=W, cu_seqlens=cu_t)
+    fl, ll = _lists(mask, dev)
+    o1, l1 = _core.forward(q, k_full, v_full, fl, ll, metadata=md, window_size=W)
+    o0, l0 = _core.forward(q, k, v, fl, ll, metadata=md, window_size=W)
+    torch.cuda.synchronize()
+    assert torch.equal(o0, o1) and torch.equal(l0, l1)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -133,6 +153,21 @@ def _two_gpu_worker(rank, world, port, result_q):
         torch.cuda.synchronize()
         ridx = torch.from_numpy(rows)
         compare(o[0], l[0], ref_o[0].float().cpu()[ridx], ref_l[0].cpu()[ridx], label=f"rank {rank}")
+        # the symmetric-memory exchange: the whole K/V axis on every rank, and the same
+        # rows bit for bit as through the NCCL all-gather (twice: the buffers are reused)
+        plan = cp.make_cp_plan(S, world, costs)
+        kvx = cp.KVExchange(S, k.shape[2], device=dev)
+        kl, vl = k.index_select(1, idx).contiguous(), v.index_select(1, idx).contiguous()
+        for _ in range(2):
+            k_full, v_full = kvx.exchange(kl, vl, plan)
+            torch.cuda.synchronize()
+            assert torch.equal(k_full, k) and torch.equal(v_full, v), "exchanged K/V differ"
+            o2, l2 = cp.context_parallel_switch_gqa_prefill_forward(
+                q.index_select(1, idx).contiguous(), kl, vl, fl, ll, total_len=S, cu_seqlens=cu_t, window_size=W,
+                plan=plan, kv_exchange=kvx)
+            torch.cuda.synchronize()
+            assert torch.equal(o2, o) and torch.equal(l2, l), "symmetric-memory exchange changed the rows"
+        del kvx, k_full, v_full
         result_q.put((rank, "ok"))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         result_q.put((rank, "error:" + type(e).__name__ + ":" + str(e)[:300]))
