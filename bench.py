@@ -28,8 +28,9 @@ slots), as a serving loop would run them.  The copy byte counts are summed over
 the ranks.  ``steady`` repeats the device-timed step back to back for at least
 two seconds with its own clock record.  At N=1 the line also carries the same
 kernel on the row-major [B, S, Hq, 128] layout (``standard_layout``), one
-backward step (dQ, dK, dV) and one decode step.  ``--replicas`` instead gives
-every rank its own 4 sequences (weak scaling).  ``--impl reference`` times the
+backward step (dQ, dK, dV) and one decode step over a BF16 and over an FP8
+cache.  ``--replicas`` instead gives every rank its own 4 sequences (weak
+scaling); ``--cp`` times context-parallel prefill of one packed batch.  ``--impl reference`` times the
 CPU restatement of the reference path (the reference kernels are Hopper-only
 TileLang programs and cannot run on B200 or on a CPU).
 """
@@ -71,7 +72,7 @@ def parse_args():
                     help="sequences per GPU (default: the workload's 4); smaller values give profiling-size cases")
     ap.add_argument("--cp", action="store_true",
                     help="instead of the default line: context-parallel prefill over the N ranks "
-                         "(strong scaling; K/V all-gather + kernel per step)")
+                         "(strong scaling; K/V exchange + kernel per step)")
     ap.add_argument("--replicas", action="store_true",
                     help="instead of the default line: every rank computes its own 4 sequences (weak scaling)")
     ap.add_argument("--steady-seconds", type=float, default=2.0,
@@ -457,10 +458,13 @@ def run_cp(args, world, rank, local_rank):
     Every rank draws the same batch and keeps only its rows of Q, K and V (zigzag
     chunks of equal legal-entry cost, ``context_parallel.make_cp_plan``).  One
     step is the public context-parallel forward (one attention layer): the K/V
-    all-gather (NCCL) and the prefill kernel on the rank's rows.  The rows' key
-    bounds depend only on the batch and are built once, before the steps.
-    ``value`` = effective FLOP of the whole batch / the slowest rank's step time
-    (strong scaling: the batch is fixed as N grows).
+    exchange (``KVExchange``: peer stores into every rank's symmetric-memory
+    buffer) and the prefill kernel on the rank's rows.  The rows' key bounds
+    depend only on the batch and are built once, before the steps.  ``value`` =
+    effective FLOP of the whole batch / the slowest rank's step time (strong
+    scaling: the batch is fixed as N grows); at N > 1 ``kv_exchange_nccl`` is the
+    same step with the NCCL all-gather instead, and ``kv_exchange`` times the two
+    exchanges alone.
     """
     import torch.distributed as dist
     from switchattentionkernels_b200 import context_parallel as cp
