@@ -18,6 +18,10 @@ Reference semantics (YushengZhao/SwitchAttentionKernels):
 * rows are written at their original positions (``:243-249``).
 
 ``prefill_dense`` computes the exact FP32 result (the accuracy reference).
+``prefill_rows`` runs on the device of its inputs: the GPU tests evaluate the
+same FP32 restatement on the GPU to check every row of the full-size workloads
+(cuBLAS FP32 with TF32 off; the tests check it against the CPU evaluation on a
+sample of rows).
 ``prefill_tiled`` replays the kernel loop tile by tile -- union key range of a
 query tile (``swiattn_gqa_prefill.py:95-105``, varlen ``:142-154``), running max
 initialised to ``-2**30`` (``:132``), ``exp2`` rescaling, P rounded to BF16 before
@@ -75,9 +79,10 @@ def prefill_rows(q, k, v, b: int, positions, is_local: bool, *, window: int, sm_
     Skv, Hkv = k.shape[1], k.shape[2]
     r = Hq // Hkv
     sl2 = scale_log2_of(sm_scale, D)
+    dev = q.device
     pos = np.asarray(positions, dtype=np.int64)
-    O = torch.empty((pos.size, Hq, D), dtype=torch.float32)
-    LSE = torch.empty((pos.size, Hq), dtype=torch.float32)
+    O = torch.empty((pos.size, Hq, D), dtype=torch.float32, device=dev)
+    LSE = torch.empty((pos.size, Hq), dtype=torch.float32, device=dev)
     if pos.size == 0:
         return O, LSE
     lo, hi = row_bounds(pos, is_local, window, Skv, metadata)
@@ -94,12 +99,14 @@ def prefill_rows(q, k, v, b: int, positions, is_local: bool, *, window: int, sm_
             O[sl] = float("nan")
             LSE[sl] = float("-inf")
             continue
-        qc = q[b, torch.from_numpy(p)].float().view(n, Hkv, r, D)
+        qc = q[b, torch.from_numpy(p).to(dev)].float().view(n, Hkv, r, D)
         kc = k[b, L0:L1].float()
         vc = v[b, L0:L1].float()
         s = torch.einsum("ngrd,lgd->ngrl", qc, kc) * sl2
-        keys = torch.arange(L0, L1)
-        legal = (keys[None, :] >= torch.from_numpy(l)[:, None]) & (keys[None, :] < torch.from_numpy(h)[:, None])
+        keys = torch.arange(L0, L1, device=dev)
+        lo_t = torch.from_numpy(l).to(dev)[:, None]
+        hi_t = torch.from_numpy(h).to(dev)[:, None]
+        legal = (keys[None, :] >= lo_t) & (keys[None, :] < hi_t)
         s = s.masked_fill(~legal[:, None, None, :], float("-inf"))
         m = s.amax(dim=-1, keepdim=True)
         m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))

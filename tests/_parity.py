@@ -66,6 +66,52 @@ def compare(O, LSE, O_ref, LSE_ref, rows=None, label=""):
     return o_max, o_mean, l_max
 
 
+def compare_every_row_on_device(O, LSE, q, k, v, full, local, window, metadata=None, label="",
+                                rows_per_slice: int = 8192):
+    """Every routed row of a full-size result against the FP32 restatement evaluated
+    on the result's own GPU (``oracle.attention.prefill_rows`` on device tensors),
+    slice by slice, with the tolerances of ``compare``; rows without a legal key
+    must be exactly ``O = NaN``, ``LSE = -inf``.  Returns ``(o_max, o_mean, l_max, rows)``.
+    """
+    assert not torch.backends.cuda.matmul.allow_tf32, "the device oracle needs IEEE FP32 GEMMs"
+    dev = q.device
+    o_max = l_max = 0.0
+    o_sum = 0.0
+    o_cnt = 0
+    rows = 0
+    for b in range(len(full)):
+        for is_local, lst in ((False, full[b]), (True, local[b])):
+            pos_all = np.asarray(lst, dtype=np.int64)
+            for s0 in range(0, pos_all.size, rows_per_slice):
+                pos = pos_all[s0:s0 + rows_per_slice]
+                o_ref, l_ref = oracle_attn.prefill_rows(q, k, v, b, pos, is_local, window=window, metadata=metadata,
+                                                        budget_bytes=1 << 30)
+                pt = torch.from_numpy(pos).to(dev)
+                o = O[b, pt].float()
+                lse = LSE[b, pt].float()
+                empty = torch.isneginf(l_ref)
+                if empty.any():
+                    assert torch.isneginf(lse[empty]).all().item(), f"{label}: rows without a legal key need LSE = -inf"
+                    assert torch.isnan(o[empty]).all().item(), f"{label}: rows without a legal key need O = NaN"
+                fin = ~empty
+                err = (o - o_ref).abs()[fin]
+                assert torch.isfinite(err).all().item(), f"{label}: non-finite output rows (batch {b})"
+                o_max = max(o_max, err.max().item()) if err.numel() else o_max
+                if not fin.any():
+                    rows += pos.size
+                    continue
+                o_sum += err.double().sum().item()
+                o_cnt += err.numel()
+                l_max = max(l_max, (lse - l_ref).abs()[fin].max().item())
+                rows += pos.size
+    assert o_cnt > 0, f"{label}: nothing to compare"
+    o_mean = o_sum / o_cnt
+    assert o_max <= O_MAX_ABS, f"{label}: O max-abs {o_max:.3e} > {O_MAX_ABS}"
+    assert o_mean <= O_MEAN_ABS, f"{label}: O mean-abs {o_mean:.3e} > {O_MEAN_ABS}"
+    assert l_max <= LSE_MAX_ABS, f"{label}: LSE max-abs {l_max:.3e} > {LSE_MAX_ABS}"
+    return o_max, o_mean, l_max, rows
+
+
 def oracle_subset(q, k, v, full, local, window, subset=None, metadata=None, sm_scale=None):
     return oracle_attn.prefill_dense(q.cpu(), k.cpu(), v.cpu(), full, local, window=window, subset=subset,
                                      metadata=metadata, sm_scale=sm_scale)

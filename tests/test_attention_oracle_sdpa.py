@@ -48,3 +48,36 @@ def test_prefill_dense_matches_sdpa(S, Hq, Hkv, W, p_full, sm_scale):
         want_lse = (torch.logsumexp(s, dim=-1) / math.log(2.0)).transpose(0, 1)  # log2 units, [S, Hq]
         assert torch.allclose(O[b], want_o, atol=2e-5, rtol=1e-5), (O[b] - want_o).abs().max()
         assert torch.allclose(L[b], want_lse, atol=2e-5, rtol=1e-5), (L[b] - want_lse).abs().max()
+
+
+def test_every_row_helper_passes_the_oracle_and_catches_a_planted_error():
+    # The helper the GPU tests use to check every row, run here on CPU tensors:
+    # the oracle's own result passes, one row moved by 0.05 fails, and a row
+    # without a legal key (Sq > Skv, local branch) must be NaN / -inf.
+    import sys
+    import os
+    sys.path.insert(0, os.path.dirname(__file__))
+    from _parity import compare_every_row_on_device
+
+    g = torch.Generator().manual_seed(5)
+    B, Sq, Skv, Hq, Hkv, D, W = 2, 90, 60, 4, 2, 128, 8
+    q = torch.randn(B, Sq, Hq, D, generator=g).bfloat16()
+    k = torch.randn(B, Skv, Hkv, D, generator=g).bfloat16()
+    v = torch.randn(B, Skv, Hkv, D, generator=g).bfloat16()
+    mask = torch.rand(B, Sq, generator=g) < 0.4
+    full = [np.nonzero(mask[b].numpy())[0] for b in range(B)]
+    local = [np.nonzero(~mask[b].numpy())[0] for b in range(B)]
+    O, L = oracle_attn.prefill_dense(q, k, v, full, local, window=W)
+    assert torch.isneginf(L).any()  # local rows past Skv + W - 1 have no legal key
+    o_max, o_mean, l_max, rows = compare_every_row_on_device(O, L, q, k, v, full, local, W, label="self")
+    assert rows == B * Sq and o_max == 0.0 and l_max == 0.0
+    bad = O.clone()
+    bad[1, int(full[1][0])] += 0.05
+    with pytest.raises(AssertionError, match="O max-abs"):
+        compare_every_row_on_device(bad, L, q, k, v, full, local, W, label="planted")
+    fin = torch.isfinite(L)
+    empty_row = torch.nonzero(~fin[0, :, 0])[0, 0]
+    bad_l = L.clone()
+    bad_l[0, empty_row] = 0.0
+    with pytest.raises(AssertionError, match="LSE = -inf"):
+        compare_every_row_on_device(O, bad_l, q, k, v, full, local, W, label="planted")
