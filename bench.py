@@ -803,6 +803,10 @@ def run_default(args, world, rank, local_rank):
     v_u = sharded.take_units(v, mine, hkv=Hkv)
     mask_u_cpu = mask_cpu[torch.tensor([u // Hkv for u in mine], dtype=torch.long)].contiguous()
     mask_u = mask_u_cpu.to(dev)
+    # the rank's largest per-unit counts, known on the host: the launch's key-split plan
+    # (long full-causal units over several SMs) needs them and the step reads none back
+    unit_counts = ((int(mask_u_cpu.sum(1).max()), int((~mask_u_cpu).sum(1).max())) if n else (0, 0))
+    split_tiles = _core.split_plan(n, S, r, 1, unit_counts[0], unit_counts[1], W, dev)[0] if n else 0
     o_u = torch.empty((n_max, S, r, D), dtype=torch.bfloat16, device=dev)
     l_u = torch.empty((n_max, S, r), dtype=torch.float32, device=dev)
     if multi:
@@ -821,9 +825,11 @@ def run_default(args, world, rank, local_rank):
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             pf_events.append(ev)
         _core.forward(q_u, k_u, v_u, full, local, window_size=W, validate=False, query_counts=counts,
-                      out=o_u[:n], lse=l_u[:n], prefill_events=ev)
+                      out=o_u[:n], lse=l_u[:n], prefill_events=ev, max_counts=unit_counts)
 
-    launches_per_step = 3  # mask compaction (two launches: rows over 4096 tokens) + the prefill kernel
+    # mask compaction (two launches: rows over 4096 tokens) + the prefill kernel (+ the
+    # merge of key-split pieces)
+    launches_per_step = 3 + (1 if split_tiles else 0)
     for _ in range(WU):
         step()
     torch.cuda.synchronize()
@@ -1088,6 +1094,7 @@ def run_default(args, world, rank, local_rank):
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic", "config": config3_dict(world, args.workload, w["p_full"]),
             "units_per_rank": [len(p) for p in plan],
+            "key_split_tiles_rank0": split_tiles,
             "layout": "each rank holds its units unit-major: q [units, S, Hq/Hkv, 128], k / v [units, S, 1, 128]",
             "effective_tflop_per_step": flops_total / 1e12,
             "pct_of_bf16_peak_per_gpu": 100.0 * value / world / peak_burst,
@@ -1113,7 +1120,7 @@ def run_default(args, world, rank, local_rank):
                        "steps": n_steady, "clocks": steady_clocks,
                        "mcycles_per_step": (st_max * 1e-3 * steady_clocks["sm_mhz"] * 1e6 / 1e6
                                             if steady_clocks else None)},
-            "gpu_launches": launches_per_step * K,  # per rank: compaction (2) + prefill kernel, every step
+            "gpu_launches": launches_per_step * K,  # rank 0: compaction (2) + prefill (+ merge), every step
             "clocks": clock_info,
         }
         if e2e is not None:

@@ -207,6 +207,42 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
                         float scale_log2, const int32_t* gate, int32_t* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Key-split plan for swa_prefill_forward_split (no counterpart in the reference,
+ * whose full-causal branch gives each 64-row query tile one CTA over its whole
+ * key prefix, swiattn_gqa_prefill.py:95-105).  A full-branch work unit whose key
+ * range spans more than *split_tiles 128-key tiles is then run as several pieces
+ * of about equal length on different SMs, and a merge kernel combines their
+ * partial O and LSE.  This lets a launch with few, long full-causal units (a
+ * multi-GPU shard of one or two (batch, KV group) units of a 131K-token
+ * sequence) end with the average work per SM instead of its longest unit.
+ * request_tiles > 0 asks for pieces of about that many tiles; 0 lets the plan
+ * decide from the launch shape (split only when the longest possible
+ * full-causal unit would outlast the estimated work per SM by half; scratch kept
+ * under 1 GiB).  n_bg: units of the launch (0: all B * Hkv).  num_sms: SMs of
+ * the device.  Returns the scratch bytes the launch needs and writes the piece
+ * length to *split_tiles (0 and 0: no split).  Needs no GPU. */
+size_t swa_prefill_split_plan(int B, int Skv, int Hq, int Hkv, int full_cap, int local_cap, int n_bg, int window,
+                              int num_sms, int request_tiles, int* split_tiles);
+
+/* swa_prefill_forward with long full-causal units split over several CTAs
+ * (see swa_prefill_split_plan; split_tiles == 0 is swa_prefill_forward).
+ * scratch: 16-byte aligned device memory, normally the plan's bytes: it holds
+ * slots for the longest full-causal units of every (unit, head block), as many
+ * as fit (at least one each, or the call fails); longer-ranked units run whole.
+ * Every routed row of a split unit gets its partial O (FP32) and LSE there from
+ * each piece, then a second kernel on `stream` writes O and LSE.  Results match the
+ * unsplit launch to rounding (each piece rounds P to BF16 against its own
+ * running max).  Not combinable with replicated outputs.  Launches that overlap
+ * on the GPU need distinct workspaces and scratch buffers. */
+int swa_prefill_forward_split(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                              const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                              const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                              const int32_t* full_starts, const int32_t* local_starts, const int32_t* causal_ends,
+                              const int32_t* bg_list, int n_bg, void* out, float* lse, int B, int Sq, int Skv, int Hq,
+                              int Hkv, int head_dim, int window, float scale_log2, const int32_t* gate,
+                              int32_t* workspace, size_t workspace_bytes, int split_tiles, void* scratch,
+                              size_t scratch_bytes, void* stream);
+
 /* Prefill over a rank's unit-major inputs with its output replicated in
  * row-major form (multi-GPU driver; no counterpart in the reference, which has
  * no distributed code -- its per-(batch, head) grid, swiattn_gqa_prefill.py:69,

@@ -15,6 +15,7 @@ supersets of the reference's accepted inputs:
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 
@@ -274,9 +275,33 @@ def _index_rows(indices: torch.Tensor, B: int, device: torch.device, name: str) 
     return indices.to(dtype=torch.int32).contiguous()
 
 
+_SM_COUNTS: dict = {}
+
+
+def _num_sms(lib, dev) -> int:
+    idx = dev.index if dev.index is not None else (torch.cuda.current_device() if dev.type == "cuda" else 0)
+    if idx not in _SM_COUNTS:
+        _SM_COUNTS[idx] = int(lib.swa_num_sms(idx))
+    return _SM_COUNTS[idx]
+
+
+def split_plan(B: int, kv_len: int, Hq: int, Hkv: int, n_full: int, n_local: int, window_size: int, device, *,
+               n_bg: int = 0, request_tiles: int = 0) -> tuple[int, int]:
+    """``(split_tiles, scratch_bytes)`` of a launch's key split (``swa_prefill_split_plan``):
+    ``(0, 0)`` when long full-causal units are not split.  ``n_full`` / ``n_local``:
+    the largest per-row counts (or the list capacities); ``n_bg``: units of the
+    launch (0: all ``B * Hkv``); ``request_tiles`` > 0 asks for that piece length."""
+    lib = _native.load()
+    dev = torch.device(device)
+    tiles = ctypes.c_int(0)
+    nbytes = int(lib.swa_prefill_split_plan(B, kv_len, Hq, Hkv, n_full, n_local, n_bg, int(window_size),
+                                            _num_sms(lib, dev), int(request_tiles), ctypes.byref(tiles)))
+    return (tiles.value, nbytes) if nbytes else (0, 0)
+
+
 def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, window_size=1024, sm_scale=None,
             validate=True, query_counts=None, bg_list=None, out=None, lse=None, prefill_events=None,
-            status_out=None):
+            status_out=None, key_split="auto", max_counts=None):
     """Both branches of Switch Attention GQA prefill (see ``switch_gqa_prefill_forward``).
 
     ``query_counts``: optional int32 ``[B, 2]`` device tensor of per-row
@@ -293,6 +318,15 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     valid; otherwise the validation bits of an unvalidated call
     (``validate=False``: the kernel then wrote nothing) or ``STATUS_TIMEOUT``
     (a device-side wait gave up; O / LSE are undefined).
+    ``key_split``: ``"auto"`` (default) lets the launch split long full-causal
+    units over several SMs when few such units would otherwise outlast the
+    rest of the work (``swa_prefill_split_plan``; a scratch buffer is then
+    allocated for the partial rows); an int asks for pieces of about that many
+    128-key tiles; ``None`` / ``0`` never splits.  The plan needs the largest
+    per-row counts: the list lengths for the reference's ``B == 1`` form, the
+    counts read back with the validation status otherwise, or ``max_counts``
+    (``(n_full, n_local)`` known on the host, for callers that skip
+    validation); without any of these it sees only the list capacities.
     """
     validate_qkv(q, k, v)
     if window_size <= 0:
@@ -330,6 +364,7 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     counts = ws[4:]
     gate = None
     counts_arg, batch_major = None, 0
+    host_counts = None if max_counts is None else (int(max_counts[0]), int(max_counts[1]))
     with torch.cuda.device(dev):
         if not padded:
             # the reference's form: B == 1, every entry of each list is a routed row
@@ -341,6 +376,7 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
                                                               _native.ptr(counts), _native.ptr(status), rb, ob, 0,
                                                               stream), "index validation")
                 _raise_status(int(status.item()))
+            host_counts = (n_full, n_local)
             if n_full + n_local != q_len:
                 raise ValueError(ERR_COVER)
         elif validate or query_counts is None:
@@ -354,7 +390,9 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
             _native.check(lib.swa_check_cover(_native.ptr(counts), B, q_len, _native.ptr(status), stream),
                           "coverage check")
             if validate:
-                _raise_status(int(status.item()))
+                vals = ws[2:].tolist()  # status and the per-row counts in one read
+                _raise_status(int(vals[0]))
+                host_counts = (max(vals[2:2 + B]), max(vals[2 + B:2 + 2 * B]))
             else:
                 gate = status
             counts_arg = counts
@@ -372,18 +410,31 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
         if bg_list is not None:
             bg_list = bg_list.to(device=dev).contiguous()
             n_bg = int(bg_list.numel())
+        split_tiles, scratch, scratch_bytes = 0, None, 0
+        if key_split:
+            request = 0 if key_split == "auto" else int(key_split)
+            if request < 0:
+                raise ValueError("key_split must be 'auto', None or a non-negative number of key tiles")
+            cf, cl = host_counts if host_counts is not None else (n_full, n_local)
+            split_tiles, scratch_bytes = split_plan(B, kv_len, Hq, Hkv, min(cf, n_full), min(cl, n_local), window_size,
+                                                    dev, n_bg=n_bg, request_tiles=request)
+            if scratch_bytes:
+                scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=dev)
+        args = (_native.ptr(q), _native.ptr(k), _native.ptr(v),
+                _native.ptr(full) if n_full else None, _native.ptr(local) if n_local else None,
+                n_full, n_local, n_full, n_local,
+                _native.ptr(counts_arg), batch_major, n_full, n_local,
+                _native.ptr(fs), _native.ptr(ls), _native.ptr(ce),
+                _native.ptr(bg_list), n_bg,
+                _native.ptr(out), _native.ptr(lse),
+                B, q_len, kv_len, Hq, Hkv, D, int(window_size), float(scale),
+                _native.ptr(gate), _native.ptr(ws), ws.numel() * 4)
         if prefill_events is not None:
             prefill_events[0].record()
-        rc = lib.swa_prefill_forward(
-            _native.ptr(q), _native.ptr(k), _native.ptr(v),
-            _native.ptr(full) if n_full else None, _native.ptr(local) if n_local else None,
-            n_full, n_local, n_full, n_local,
-            _native.ptr(counts_arg), batch_major, n_full, n_local,
-            _native.ptr(fs), _native.ptr(ls), _native.ptr(ce),
-            _native.ptr(bg_list), n_bg,
-            _native.ptr(out), _native.ptr(lse),
-            B, q_len, kv_len, Hq, Hkv, D, int(window_size), float(scale),
-            _native.ptr(gate), _native.ptr(ws), ws.numel() * 4, stream)
+        if split_tiles:
+            rc = lib.swa_prefill_forward_split(*args, split_tiles, _native.ptr(scratch), scratch_bytes, stream)
+        else:
+            rc = lib.swa_prefill_forward(*args, stream)
         _native.check(rc, "switch_gqa_prefill_forward")
         if prefill_events is not None:
             prefill_events[1].record()

@@ -50,6 +50,8 @@ EXPORTED = (
     "swa_gather_units",
     "swa_prefill_forward_replicated",
     "swa_decode_forward_fp8",
+    "swa_prefill_split_plan",
+    "swa_prefill_forward_split",
 )
 
 _lock = threading.Lock()
@@ -96,6 +98,13 @@ def _declare(lib) -> None:
         _i, _i, _i, _i, _i, _i,  # B, Sq, Skv, Hq, Hkv, head_dim
         _i, _f,                # window, scale_log2
         _p, _p, _sz,           # gate, workspace, workspace_bytes
+        _p,                    # stream
+    ]
+    lib.swa_prefill_split_plan.restype = _sz
+    lib.swa_prefill_split_plan.argtypes = [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]
+    lib.swa_prefill_forward_split.restype = _i
+    lib.swa_prefill_forward_split.argtypes = list(lib.swa_prefill_forward.argtypes[:-1]) + [
+        _i, _p, _sz,           # split_tiles, scratch, scratch_bytes
         _p,                    # stream
     ]
     lib.swa_noalloc_max_batch.restype = _i

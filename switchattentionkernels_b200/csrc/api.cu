@@ -406,7 +406,8 @@ int prefill_forward_impl(const void* q, const void* k, const void* v, const int3
                          const int32_t* full_starts, const int32_t* local_starts, const int32_t* causal_ends,
                          const int32_t* bg_list, int n_bg, void* out, float* lse, int B, int Sq, int Skv, int Hq,
                          int Hkv, int head_dim, int window, float scale_log2, const int32_t* gate,
-                         int32_t* workspace, size_t workspace_bytes, void* stream, const Replicas* rep) {
+                         int32_t* workspace, size_t workspace_bytes, void* stream, const Replicas* rep,
+                         int split_tiles = 0, void* scratch = nullptr, size_t scratch_bytes = 0) {
   if (head_dim != 128) return fail(SWA_E_UNSUPPORTED, "head_dim must be 128");
   if (B <= 0 || Sq <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0) return fail(SWA_E_INVALID, "empty or negative shape");
   if (Hq % Hkv != 0) return fail(SWA_E_INVALID, "query heads must be divisible by KV heads");
@@ -524,10 +525,33 @@ int prefill_forward_impl(const void* q, const void* k, const void* v, const int3
     }
   }
 
+  p.pieces = 1;
+  const int64_t n_max_tiles = (static_cast<int64_t>(Skv) + 127) / 128;
+  if (split_tiles > 0 && p.idx_cap[0] > 0 && n_max_tiles > split_tiles) {
+    // pieces per full-branch unit from the piece length; scratch slots for the
+    // longest units of every (unit, head block), as many as the scratch holds (the
+    // plan's bytes give one per position block the counts allow; units ranked
+    // beyond the scratch run whole)
+    if (replicated) return fail(SWA_E_INVALID, "a key split cannot be combined with replicated outputs");
+    const int64_t pieces = (n_max_tiles + split_tiles - 1) / split_tiles;
+    const int64_t pb_cap = (static_cast<int64_t>(p.idx_cap[0]) + p.pc - 1) / p.pc;
+    const int64_t per_rank = static_cast<int64_t>(p.nhb) * p.n_bg * pieces * swa::kSplitSlotBytes;
+    const int64_t k_cap = std::min<int64_t>(pb_cap, static_cast<int64_t>(scratch_bytes) / per_rank);
+    if (scratch == nullptr || !aligned16(scratch) || k_cap < 1)
+      return fail(SWA_E_INVALID, "key-split scratch missing, unaligned or smaller than one slot per unit");
+    const int64_t slots = k_cap * p.nhb * p.n_bg * pieces;
+    p.pieces = static_cast<int>(pieces);
+    p.split_tiles = split_tiles;
+    p.split_pb_cap = static_cast<int>(k_cap);
+    p.part_lse = static_cast<float*>(scratch);
+    p.part_o = static_cast<float*>(scratch) + slots * 256;
+  }
+
   const int64_t per_level = static_cast<int64_t>(p.n_bg) * p.nhb;
-  const int64_t items =
-      (static_cast<int64_t>(p.idx_cap[0] + p.pc - 1) / p.pc + (p.idx_cap[1] + p.pc - 1) / p.pc) * per_level;
+  const int64_t items = (static_cast<int64_t>(p.idx_cap[0] + p.pc - 1) / p.pc * p.pieces +
+                         (p.idx_cap[1] + p.pc - 1) / p.pc) * per_level;
   if (items == 0) return SWA_OK;
+  if (items >= (int64_t(1) << 31)) return fail(SWA_E_UNSUPPORTED, "too many work items");
   const int ctas = static_cast<int>(items < nsm ? items : nsm);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -535,6 +559,8 @@ int prefill_forward_impl(const void* q, const void* k, const void* v, const int3
   if (e != cudaSuccess) return cuda_fail(e, "workspace reset");
   e = swa::launch_prefill(p, ctas, s);
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  e = swa::launch_merge_pieces(p, s);
+  if (e != cudaSuccess) return cuda_fail(e, "key-split merge launch");
   return SWA_OK;
 }
 
@@ -554,6 +580,36 @@ int swa_prefill_forward(const void* q, const void* k, const void* v, const int32
                               counts_batch_major, count_full, count_local, full_starts, local_starts, causal_ends,
                               bg_list, n_bg, out, lse, B, Sq, Skv, Hq, Hkv, head_dim, window, scale_log2, gate,
                               workspace, workspace_bytes, stream, nullptr);
+}
+
+size_t swa_prefill_split_plan(int B, int Skv, int Hq, int Hkv, int full_cap, int local_cap, int n_bg, int window,
+                              int num_sms, int request_tiles, int* split_tiles) {
+  if (split_tiles != nullptr) *split_tiles = 0;
+  if (B <= 0 || Skv <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || full_cap < 0 || local_cap < 0 || window <= 0)
+    return 0;
+  const int r = Hq / Hkv;
+  int rp = r & (-r);
+  if (rp > 256) rp = 256;
+  const int n_units = n_bg > 0 ? n_bg : B * Hkv;
+  const swa::SplitPlan plan =
+      swa::plan_split(n_units, r / rp, 256 / rp, full_cap, local_cap, Skv, window, num_sms, request_tiles);
+  if (split_tiles != nullptr) *split_tiles = plan.tiles;
+  return plan.tiles > 0 ? plan.bytes : 0;
+}
+
+int swa_prefill_forward_split(const void* q, const void* k, const void* v, const int32_t* full_idx,
+                              const int32_t* local_idx, int full_stride, int local_stride, int full_cap, int local_cap,
+                              const int32_t* counts, int counts_batch_major, int count_full, int count_local,
+                              const int32_t* full_starts, const int32_t* local_starts, const int32_t* causal_ends,
+                              const int32_t* bg_list, int n_bg, void* out, float* lse, int B, int Sq, int Skv, int Hq,
+                              int Hkv, int head_dim, int window, float scale_log2, const int32_t* gate,
+                              int32_t* workspace, size_t workspace_bytes, int split_tiles, void* scratch,
+                              size_t scratch_bytes, void* stream) {
+  if (split_tiles < 0) return fail(SWA_E_INVALID, "split_tiles must be non-negative");
+  return prefill_forward_impl(q, k, v, full_idx, local_idx, full_stride, local_stride, full_cap, local_cap, counts,
+                              counts_batch_major, count_full, count_local, full_starts, local_starts, causal_ends,
+                              bg_list, n_bg, out, lse, B, Sq, Skv, Hq, Hkv, head_dim, window, scale_log2, gate,
+                              workspace, workspace_bytes, stream, nullptr, split_tiles, scratch, scratch_bytes);
 }
 
 int swa_prefill_forward_replicated(const void* q, const void* k, const void* v, const int32_t* full_idx,

@@ -46,6 +46,9 @@
 // O and LSE mathematically unchanged while removing most O rescales.  One pair of
 // exponentials in four is evaluated on the FMA pipe (exp2_poly_pair) instead of
 // the MUFU unit, which otherwise bounds the softmax rate.
+#include <algorithm>
+#include <cmath>
+
 #include "sm100.cuh"
 #include "swattn_internal.h"
 
@@ -72,7 +75,8 @@ struct Unit {
   int b, g, hb, pb;
   int count;    // routed rows of this (branch, b)
   int j0, n;    // first key (a multiple of 64) / 64, and number of 128-key tiles from there
-  int pad[7];
+  int part;     // key-split piece: its scratch slot (-1: the unit is not split)
+  int pad[6];
 };
 
 struct SmemLayout {
@@ -188,18 +192,52 @@ __device__ __forceinline__ int64_t replica_row(const PrefillParams& p, int b, in
 // than with 8; each group kept for the tail reads its K/V a second time).
 constexpr int kTailGroups = 8;
 
+// Key tiles of the unit of (branch, b) whose routed slots start at first_slot
+// (< cnt): the union of its rows' key ranges from the first and last routed row,
+// in 128-key tiles from the 64-aligned key at or below the first legal key.
+__device__ __forceinline__ void unit_tiles(const PrefillParams& p, int branch, int b, int first_slot, int cnt,
+                                           int& j0, int& n) {
+  const int last_slot = min(first_slot + p.pc, cnt) - 1;
+  const int fpos = min(max(load_pos(p, branch, b, first_slot), 0), p.Sq - 1);
+  const int lpos = min(max(load_pos(p, branch, b, last_slot), 0), p.Sq - 1);
+  int lo, hi;
+  if (p.ends != nullptr) {
+    lo = max(p.starts[branch][fpos], 0);
+    hi = min(p.ends[lpos], p.Skv);
+  } else {
+    lo = branch ? max(fpos - p.window + 1, 0) : 0;
+    hi = min(lpos + 1, p.Skv);
+  }
+  // key tiles start at the 64-aligned key at or below lo (a 128-key grid would
+  // waste up to 64 more masked keys per row)
+  j0 = lo / 64;
+  n = max((hi - j0 * 64 + kBK - 1) / kBK, 0);
+}
+
+// Pieces of a full-branch unit of n key tiles under a key split: np pieces of
+// len tiles (the last one shorter), of which the first `used` start below n.
+__device__ __forceinline__ void split_pieces(const PrefillParams& p, int n, int& np, int& len, int& used) {
+  np = (p.split_tiles > 0 && n > p.split_tiles) ? (n + p.split_tiles - 1) / p.split_tiles : 1;
+  len = (n + np - 1) / np;
+  used = len > 0 ? (n + len - 1) / len : 1;
+}
+
+template <bool kSplit>
 __device__ bool decode_item(const PrefillParams& p, int it, int maxnpb0, int maxnpb1, Unit& u) {
-  const int per0 = maxnpb0 * p.nhb;  // full-branch items of one group
-  const int per1 = maxnpb1 * p.nhb;  // local-branch items of one group
+  const int P = kSplit ? p.pieces : 1;   // work items per full-branch unit (1: no key split)
+  const int per0 = maxnpb0 * p.nhb * P;  // full-branch items of one group
+  const int per1 = maxnpb1 * p.nhb;      // local-branch items of one group
   const int n_early = max(p.n_bg - kTailGroups, 0);
   const int early_items = n_early * (per0 + per1);
-  int branch, pb, rem;
+  int branch, pb, rem, piece = 0;
   if (it < early_items) {
     const int grp = it / (per0 + per1);
     int w = it - grp * (per0 + per1);
     if (w < per0) {
       branch = 0;
-      pb = maxnpb0 - 1 - w / p.nhb;  // longest full-causal units of the group first
+      pb = maxnpb0 - 1 - w / (p.nhb * P);  // longest full-causal units of the group first
+      piece = w % P;
+      w /= P;
     } else {
       w -= per0;
       branch = 1;
@@ -213,8 +251,9 @@ __device__ bool decode_item(const PrefillParams& p, int it, int maxnpb0, int max
       branch = 0;
       const int grp = n_early + it / per0;
       const int w = it % per0;
-      pb = maxnpb0 - 1 - w / p.nhb;
-      rem = grp * p.nhb + w % p.nhb;
+      pb = maxnpb0 - 1 - w / (p.nhb * P);
+      piece = w % P;
+      rem = grp * p.nhb + (w / P) % p.nhb;
     } else {
       it -= n_late * per0;
       branch = 1;
@@ -230,21 +269,27 @@ __device__ bool decode_item(const PrefillParams& p, int it, int maxnpb0, int max
   const int cnt = min(branch_count(p, branch, b), p.idx_cap[branch]);
   const int first_slot = pb * p.pc;
   if (first_slot >= cnt) return false;
-  const int last_slot = min(first_slot + p.pc, cnt) - 1;
-  const int fpos = min(max(load_pos(p, branch, b, first_slot), 0), p.Sq - 1);
-  const int lpos = min(max(load_pos(p, branch, b, last_slot), 0), p.Sq - 1);
-  int lo, hi;
-  if (p.ends != nullptr) {
-    lo = max(p.starts[branch][fpos], 0);
-    hi = min(p.ends[lpos], p.Skv);
-  } else {
-    lo = branch ? max(fpos - p.window + 1, 0) : 0;
-    hi = min(lpos + 1, p.Skv);
+  int j0, n;
+  unit_tiles(p, branch, b, first_slot, cnt, j0, n);
+  int part = -1;
+  if (kSplit && branch == 0 && P > 1) {
+    int np, len, used;
+    split_pieces(p, n, np, len, used);
+    // the scratch holds the split_pb_cap longest units of each (unit, head block):
+    // rank rr from the end of the branch's position blocks; a longer-ranked unit
+    // runs whole
+    const int rr = (cnt + p.pc - 1) / p.pc - 1 - pb;
+    if (rr >= p.split_pb_cap) {
+      np = 1;
+      used = 1;
+    }
+    if (piece >= used) return false;  // no such piece: an empty item
+    if (np > 1) {
+      j0 += 2 * piece * len;          // j0 counts 64-key steps, a tile is two
+      n = min(len, n - piece * len);
+      part = ((bgi * p.nhb + hb) * p.split_pb_cap + rr) * P + piece;
+    }
   }
-  // key tiles start at the 64-aligned key at or below lo (a 128-key grid would
-  // waste up to 64 more masked keys per row)
-  const int j0 = lo / 64;
-  const int j1 = j0 + (hi - j0 * 64 + kBK - 1) / kBK;
   u.valid = 1;
   u.branch = branch;
   u.b = b;
@@ -253,10 +298,12 @@ __device__ bool decode_item(const PrefillParams& p, int it, int maxnpb0, int max
   u.pb = pb;
   u.count = cnt;
   u.j0 = j0;
-  u.n = max(j1 - j0, 0);
+  u.n = n;
+  u.part = part;
   return true;
 }
 
+template <bool kSplit>
 __device__ __forceinline__ void read_unit(const volatile Unit* src, Unit& u) {
   u.valid = src->valid;
   u.branch = src->branch;
@@ -267,6 +314,7 @@ __device__ __forceinline__ void read_unit(const volatile Unit* src, Unit& u) {
   u.count = src->count;
   u.j0 = src->j0;
   u.n = src->n;
+  u.part = kSplit ? src->part : -1;
 }
 
 // TMA boxes of Q tile i (rows 128 i .. 128 i + 127) of unit u, issued by the
@@ -374,9 +422,11 @@ __device__ __forceinline__ float row_max64(const float* s) {
   return fmax3(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[5]), fmaxf(u[6], u[7]));
 }
 
-// kRep: the launch also writes the replicated row-major outputs (p.n_rep > 0); a
-// separate instantiation, so the plain launch carries none of that code.
-template <bool kRep>
+// kRep: the launch also writes the replicated row-major outputs (p.n_rep > 0);
+// kSplit: long full-causal units run as key-split pieces (p.pieces > 1) whose
+// partial rows go to the scratch.  Separate instantiations, so the plain launch
+// carries none of that code.
+template <bool kRep, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __grid_constant__ PrefillParams p) {
   if (p.gate != nullptr && *p.gate != 0) return;  // index validation failed: write nothing
 #ifdef SWA_CYCLES
@@ -453,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       maxnpb1 = max(maxnpb1, (min(branch_count(p, 1, b), p.idx_cap[1]) + p.pc - 1) / p.pc);
     }
     const int per_level = p.n_bg * p.nhb;
-    const int total = (maxnpb0 + maxnpb1) * per_level;
+    const int total = (maxnpb0 * (kSplit ? p.pieces : 1) + maxnpb1) * per_level;
     auto fetch = [&](Unit& u) {
       u.valid = 0;
       while (true) {
@@ -461,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         if (lane == 0) it = atomicAdd(p.counter, 1);
         it = __shfl_sync(0xffffffffu, it, 0);
         if (it >= total) break;
-        if (decode_item(p, it, maxnpb0, maxnpb1, u)) break;
+        if (decode_item<kSplit>(p, it, maxnpb0, maxnpb1, u)) break;
       }
     };
     uint32_t kv_it = 0;
@@ -488,6 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         dst->count = u.count;
         dst->j0 = u.j0;
         dst->n = u.n;
+        if (kSplit) dst->part = u.part;
         mbar_arrive(&sched_full[slot]);
       }
       __syncwarp();
@@ -566,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       while (true) {
         const int slot = k_sched % kSchedSlots;
         if (!mbar_wait(&sched_full[slot], (k_sched / kSchedSlots) & 1, abort_flag)) { ok = false; return false; }
-        read_unit(&units[slot], u);
+        read_unit<kSplit>(&units[slot], u);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sched_empty[slot]);
         ++k_sched;
@@ -745,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       const int slot = k % kSchedSlots;
       if (!mbar_wait(&sched_full[slot], (k / kSchedSlots) & 1, abort_flag)) break;
       Unit u;
-      read_unit(&units[slot], u);
+      read_unit<kSplit>(&units[slot], u);
       mbar_arrive(&sched_empty[slot]);
       if (!u.valid) break;
       const int slot_abs = u.pb * p.pc + slot_in_unit;
@@ -908,6 +959,37 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
       if (!mbar_wait(&o_full[tile], o_use & 1, abort_flag)) { ok = false; break; }
       ++o_use;
       tr.ev(21, s_use);
+      if constexpr (kSplit) {
+        if (u.part >= 0) {
+          // a key-split piece: the row's partial O / l (FP32) and partial LSE over the
+          // piece's keys [klo, khi) into the scratch; a row without a legal key in
+          // the piece gets O = 0 and LSE = -inf (weight 0 in the merge)
+          const int klo = u.j0 * 64, khi = klo + u.n * kBK;
+          const bool none = max(rb.lo, klo) >= min(rb.hi, khi);
+          const float sc = none ? 0.0f : 1.0f / l;
+          float* po = p.part_o + (static_cast<int64_t>(u.part) * 256 + R) * 128 + 32 * half;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t orr[32];
+            tmem_ld_16x2_x32(tm_o + 64 * c, orr);
+            tmem_ld_wait();
+            reg_fence32(orr);
+            if (valid_row) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                reinterpret_cast<float4*>(po + 64 * c)[e] =
+                    make_float4(__uint_as_float(orr[4 * e]) * sc, __uint_as_float(orr[4 * e + 1]) * sc,
+                                __uint_as_float(orr[4 * e + 2]) * sc, __uint_as_float(orr[4 * e + 3]) * sc);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&o_empty[tile]);
+          if (half == 0 && valid_row)
+            p.part_lse[static_cast<int64_t>(u.part) * 256 + R] = none ? -INFINITY : lg2_approx(l) + m;
+          continue;
+        }
+      }
       // A row whose key range is empty (metadata start >= end, or a local row at
       // t >= Skv + W - 1) has row sum 0 in the reference (swiattn_gqa_prefill.py:201-206,
       // swiattn_gqa_prefill_varlen.py:236-241): O = 0/0 and LSE = log2(0) + m.
@@ -1000,27 +1082,131 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
 #endif
 }
 
+// Combines the key-split pieces of one unit per block (grid: split_pb_cap x nhb x
+// units; blocks of units that are not split return at once): for every routed row
+// of the unit, LSE = log2(sum_s 2^LSE_s) and O = sum_s 2^(LSE_s - LSE) O_s over its
+// pieces s, written as BF16 at the row's position; a row without a legal key in
+// any piece gets O = NaN, LSE = -inf (the reference's 0/0 and log2(0)).  A warp
+// per row, four columns per lane.
+__global__ void __launch_bounds__(256) merge_pieces_kernel(const __grid_constant__ PrefillParams p) {
+  if (p.gate != nullptr && *p.gate != 0) return;
+  const int rr = blockIdx.x, hb = blockIdx.y, bgi = blockIdx.z;  // rr: rank from the last position block
+  const int bg = p.bg_list != nullptr ? p.bg_list[bgi] : bgi;
+  const int b = bg / p.Hkv;
+  const int g = bg % p.Hkv;
+  const int cnt = min(branch_count(p, 0, b), p.idx_cap[0]);
+  const int pb = (cnt + p.pc - 1) / p.pc - 1 - rr;
+  if (pb < 0) return;
+  const int first_slot = pb * p.pc;
+  int j0, n, np, len, used;
+  unit_tiles(p, 0, b, first_slot, cnt, j0, n);
+  split_pieces(p, n, np, len, used);
+  if (np <= 1) return;
+  const int64_t base = ((static_cast<int64_t>(bgi) * p.nhb + hb) * p.split_pb_cap + rr) * p.pieces;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = p.Hq / p.Hkv;
+  for (int R = warp; R < 256; R += 8) {
+    const int slot_abs = first_slot + R / p.rp;
+    if (slot_abs >= cnt) continue;
+    const int qpos = load_pos(p, 0, b, slot_abs);
+    if (qpos < 0 || qpos >= p.Sq) continue;
+    const int head = g * r + hb * p.rp + R % p.rp;
+    const int64_t orow = (static_cast<int64_t>(b) * p.Sq + qpos) * p.Hq + head;
+    float M = -INFINITY;
+    for (int s = 0; s < used; ++s) M = fmaxf(M, p.part_lse[(base + s) * 256 + R]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lse = -INFINITY;
+    if (M == -INFINITY) {
+      acc = make_float4(NAN, NAN, NAN, NAN);
+    } else {
+      float sum = 0.0f;
+      for (int s = 0; s < used; ++s) sum += exp2f(p.part_lse[(base + s) * 256 + R] - M);
+      lse = M + log2f(sum);
+      for (int s = 0; s < used; ++s) {
+        const float w = exp2f(p.part_lse[(base + s) * 256 + R] - lse);
+        if (w == 0.0f) continue;
+        const float4 o = reinterpret_cast<const float4*>(p.part_o + ((base + s) * 256 + R) * 128)[lane];
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+      }
+    }
+    const __nv_bfloat162 lo2 = __floats2bfloat162_rn(acc.x, acc.y);
+    const __nv_bfloat162 hi2 = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<const uint32_t*>(&lo2);
+    packed.y = *reinterpret_cast<const uint32_t*>(&hi2);
+    reinterpret_cast<uint2*>(p.out + orow * 128)[lane] = packed;
+    if (lane == 0) p.lse[orow] = lse;
+  }
+}
+
+template <bool kRep, bool kSplit>
+cudaError_t launch_instance(const PrefillParams& params, int num_sms, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(switch_prefill_kernel<kRep, kSplit>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  switch_prefill_kernel<kRep, kSplit><<<num_sms, kThreads, kSmemBytes, stream>>>(params);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillParams& params, int num_sms, cudaStream_t stream) {
-  static bool attr_set[2][64] = {};
-  const bool rep = params.n_rep > 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[rep][dev]) {
-    cudaError_t e = rep ? cudaFuncSetAttribute(switch_prefill_kernel<true>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
-                        : cudaFuncSetAttribute(switch_prefill_kernel<false>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[rep][dev] = true;
-  }
-  if (rep) {
-    switch_prefill_kernel<true><<<num_sms, kThreads, kSmemBytes, stream>>>(params);
-  } else {
-    switch_prefill_kernel<false><<<num_sms, kThreads, kSmemBytes, stream>>>(params);
-  }
+  if (params.n_rep > 0) return launch_instance<true, false>(params, num_sms, stream);
+  if (params.pieces > 1) return launch_instance<false, true>(params, num_sms, stream);
+  return launch_instance<false, false>(params, num_sms, stream);
+}
+
+cudaError_t launch_merge_pieces(const PrefillParams& params, cudaStream_t stream) {
+  if (params.pieces <= 1) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(params.split_pb_cap), static_cast<unsigned>(params.nhb),
+                  static_cast<unsigned>(params.n_bg));
+  merge_pieces_kernel<<<grid, 256, 0, stream>>>(params);
   return cudaGetLastError();
+}
+
+SplitPlan plan_split(int n_units, int nhb, int pc, int full_cap, int local_cap, int Skv, int window, int num_sms,
+                     int request_tiles) {
+  SplitPlan s{0, 1, 0, 0};
+  const int64_t n_max = (static_cast<int64_t>(Skv) + kBK - 1) / kBK;  // most key tiles a unit can have
+  const int64_t pb_cap = (static_cast<int64_t>(full_cap) + pc - 1) / pc;
+  const int64_t uf = pb_cap * n_units * nhb;                                        // full-branch units
+  const int64_t ul = ((static_cast<int64_t>(local_cap) + pc - 1) / pc) * n_units * nhb;  // local-branch units
+  if (uf == 0 || n_max < 2) return s;
+  int64_t tiles = request_tiles;
+  if (tiles <= 0) {
+    // Split only when the longest full-causal unit would outlast the average work
+    // per SM by half: full units taken as n_max / 2 tiles on average, local units
+    // as the window plus a unit's position span.
+    const int64_t t_local = std::min<int64_t>(n_max, (static_cast<int64_t>(window) + pc + 2 * kBK - 2) / kBK);
+    const double est = (0.5 * static_cast<double>(uf) * static_cast<double>(n_max) +
+                        static_cast<double>(ul) * static_cast<double>(t_local)) /
+                       static_cast<double>(num_sms > 0 ? num_sms : 1);
+    if (n_max < 64 || static_cast<double>(n_max) <= 1.5 * est) return s;
+    tiles = std::max<int64_t>(32, static_cast<int64_t>(std::ceil(est)));
+  }
+  if (n_max <= tiles) return s;
+  const int64_t pieces = (n_max + tiles - 1) / tiles;
+  // scratch slots for the k_cap longest full-branch units of each (unit, head
+  // block): as many as the lists can hold, within kSplitScratchBudget bytes
+  constexpr int64_t kSplitScratchBudget = int64_t(512) << 20;
+  const int64_t per_rank = static_cast<int64_t>(nhb) * n_units * pieces * kSplitSlotBytes;
+  const int64_t k_cap = std::min<int64_t>(pb_cap, kSplitScratchBudget / per_rank);
+  if (k_cap < 1 || pieces > (int64_t(1) << 20)) return s;
+  const int64_t slots = k_cap * nhb * n_units * pieces;
+  s.tiles = static_cast<int>(tiles);
+  s.pieces = static_cast<int>(pieces);
+  s.pb_cap = static_cast<int>(k_cap);
+  s.bytes = static_cast<size_t>(slots * kSplitSlotBytes);
+  return s;
 }
 
 uint32_t prefill_smem_bytes() { return kSmemBytes; }

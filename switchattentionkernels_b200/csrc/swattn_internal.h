@@ -64,9 +64,38 @@ struct __align__(64) PrefillParams {
   const int32_t* unit_gid;
   __nv_bfloat16* rep_out[kMaxReplicas];
   float* rep_lse[kMaxReplicas];
+  // Key-split pieces of long full-causal units (pieces == 1: off).  A full-branch
+  // unit of n > split_tiles key tiles runs as np = ceil(n / split_tiles) pieces of
+  // ceil(n / np) tiles, each a work item of its own (on whichever CTA takes it);
+  // a piece writes every routed row's partial O / l (FP32) and partial LSE into
+  // the scratch slot ((bgi * nhb + hb) * split_pb_cap + rr) * pieces + piece, rr =
+  // the unit's rank from the last position block of its branch (only units with
+  // rr < split_pb_cap are split), and merge_pieces_kernel combines the pieces.
+  int pieces;        // work items per full-branch unit: ceil(max tiles / split_tiles)
+  int split_tiles;
+  int split_pb_cap;  // longest units per (unit, head block) with scratch slots
+  float* part_o;     // [slots, 256, 128]
+  float* part_lse;   // [slots, 256]
 };
 
+// Scratch bytes of one key-split slot: partial LSE and partial O of 256 rows.
+constexpr int64_t kSplitSlotBytes = 256 * 4 + 256 * 128 * 4;
+
+// Plan of a key-split prefill launch (swa_prefill_split_plan): tiles == 0 means
+// no split.
+struct SplitPlan {
+  int tiles;
+  int pieces;
+  int pb_cap;
+  size_t bytes;  // scratch: partial LSE of every slot, then partial O (256-byte aligned)
+};
+SplitPlan plan_split(int n_units, int nhb, int pc, int full_cap, int local_cap, int Skv, int window, int num_sms,
+                     int request_tiles);
+
 cudaError_t launch_prefill(const PrefillParams& params, int num_ctas, cudaStream_t stream);
+// Combines the pieces of every split unit of a launch (after launch_prefill on
+// the same stream).
+cudaError_t launch_merge_pieces(const PrefillParams& params, cudaStream_t stream);
 
 // Decode step: one query token per sequence against its KV cache.
 struct __align__(64) DecodeParams {

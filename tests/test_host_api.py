@@ -203,3 +203,41 @@ def test_backward_workspace_query():
         assert rows * 532 <= got <= rows * 532 + 256 * 6
     assert lib.swa_backward_workspace_bytes(0, 8, 4, 4) == 0
     assert lib.swa_backward_workspace_bytes(2, 8, -1, 4) == 0
+
+
+def _plan(lib, B, Skv, Hq, Hkv, full_cap, local_cap, n_bg, window, request=0, sms=148):
+    tiles = ctypes.c_int(-1)
+    nbytes = lib.swa_prefill_split_plan(B, Skv, Hq, Hkv, full_cap, local_cap, n_bg, window, sms, request,
+                                        ctypes.byref(tiles))
+    return int(nbytes), tiles.value
+
+
+def test_key_split_plan():
+    # host arithmetic only: which launches split long full-causal units, and the scratch they need
+    lib = _native.load()
+    # config 3 at 1 and 8 GPUs (unit-major shards: B = units, Hkv = 1): never split
+    assert _plan(lib, 4, 32768, 32, 8, 4300, 28672, 0, 1024) == (0, 0)
+    assert _plan(lib, 4, 32768, 4, 1, 4300, 28672, 0, 1024) == (0, 0)
+    # config 5 at p_full 1.0 / 0.0 / 0.01 on one GPU (8 units): no split
+    assert _plan(lib, 2, 131072, 32, 4, 131072, 0, 0, 2048) == (0, 0)
+    assert _plan(lib, 2, 131072, 32, 4, 0, 131072, 0, 2048) == (0, 0)
+    assert _plan(lib, 2, 131072, 32, 4, 1400, 130000, 0, 2048) == (0, 0)
+    # config 5 at p_full 0.01, one unit per GPU (8 GPUs): the 1024-tile full units are split
+    nbytes, tiles = _plan(lib, 1, 131072, 8, 1, 1400, 130000, 0, 2048)
+    assert 32 <= tiles < 1024
+    pieces = -(-1024 // tiles)
+    slots = -(-1400 // 32) * pieces
+    assert nbytes == slots * 256 * 4 * (1 + 128)
+    # the same share seen through list capacities only (lists padded to S): no split,
+    # and a requested split keeps its scratch within 512 MiB (the longest units only)
+    assert _plan(lib, 1, 131072, 8, 1, 131072, 131072, 0, 2048) == (0, 0)
+    nbytes, tiles = _plan(lib, 1, 131072, 8, 1, 131072, 131072, 0, 2048, request=512)
+    assert tiles == 512 and 0 < nbytes <= 512 << 20 and nbytes % (2 * 256 * 4 * 129) == 0
+    # a requested piece length is honoured; none when no unit can be that long
+    nbytes, tiles = _plan(lib, 2, 1000, 8, 2, 300, 700, 0, 64, request=2)
+    # 4 (b, g) units x 5 position blocks x 4 pieces of 2 of the 8 tiles
+    assert tiles == 2 and nbytes == 4 * (-(-300 // 64)) * 4 * 256 * 4 * 129
+    assert _plan(lib, 2, 1000, 8, 2, 300, 700, 0, 64, request=8) == (0, 0)
+    assert _plan(lib, 2, 1000, 8, 2, 0, 1000, 0, 64, request=2) == (0, 0)
+    # bad shapes plan nothing
+    assert _plan(lib, 0, 1000, 8, 2, 300, 700, 0, 64, request=2) == (0, 0)
