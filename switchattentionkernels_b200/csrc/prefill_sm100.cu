@@ -60,6 +60,7 @@ constexpr int kThreads = 576;
 constexpr int kBK = 128;            // keys per K/V tile
 constexpr int kStages = 5;          // K/V ring depth (each stage: one K or one V tile)
 constexpr int kSchedSlots = 4;      // work-unit ring depth
+constexpr int kFetchAheadTiles = 2; // the next unit is claimed while the last 3 key tiles load
 constexpr uint32_t kTileBytes = 128 * 128 * 2;   // 32 KB: a 128x128 BF16 tile (2 swizzled halves)
 constexpr uint32_t kHalfBytes = 128 * 64 * 2;    // 16 KB: 128 rows x 64 columns
 constexpr float kRescaleThreshold = 8.0f;
@@ -517,14 +518,26 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
     uint32_t kv_it = 0;
     uint32_t q_use[2] = {0, 0};
     Tracer tr(lane == 0 ? 3 : -1);
+    // The next unit is claimed from the counter only while this unit's last
+    // kFetchAheadTiles + 1 key tiles are being loaded (several tiles before the MMA
+    // warp reaches the unit's end, so the claim and its decode stay hidden).  A
+    // claim at the start of the unit would hold the next item for the whole unit:
+    // with few units per launch (a multi-GPU share) a long full-causal unit claimed
+    // that way waited behind another long one and set the launch's length.
     Unit u;
     fetch(u);
     for (int k = 0;; ++k) {
       tr.ev(60, k);
       Unit un;
       un.valid = 0;
-      if (u.valid) fetch(un);
-      tr.ev(61, k);
+      bool fetched = !u.valid;  // nothing follows the end marker
+      auto fetch_next = [&]() {
+        if (!fetched) {
+          fetch(un);
+          fetched = true;
+          tr.ev(61, k);
+        }
+      };
       const int slot = k % kSchedSlots;
       if (!mbar_wait(&sched_empty[slot], ((k / kSchedSlots) & 1) ^ 1, abort_flag)) break;
       if (lane == 0) {
@@ -577,9 +590,14 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
         // ring order K_0, V_0, K_1, V_1, ...; the Q tiles go between K_0 and V_0 so
         // that K_0 streams in while the previous unit's epilogues still hold Q
         ok = load_kv(0, 0) && load_q(0) && load_q(1) && load_kv(0, 1);
-        for (int j = 1; j < u.n && ok; ++j) ok = load_kv(j, 0) && load_kv(j, 1);
+        if (ok && u.n - 1 <= kFetchAheadTiles) fetch_next();
+        for (int j = 1; j < u.n && ok; ++j) {
+          ok = load_kv(j, 0) && load_kv(j, 1);
+          if (ok && j >= u.n - 1 - kFetchAheadTiles) fetch_next();
+        }
       }
       if (!ok) break;
+      fetch_next();
       u = un;
     }
     if (*abort_flag) {
