@@ -12,8 +12,9 @@
 // span of a tile, so the union key range wastes fewer masked entries.
 //
 // Roles (576 threads, one CTA per SM, persistent over a dynamic work counter):
-//   warp 0      producer : takes work units from the global counter (one unit
-//                          ahead) and publishes them through a shared-memory ring;
+//   warp 0      producer : takes work units from the global counter (the next one
+//                          while the current unit's last key tiles load) and
+//                          publishes them through a shared-memory ring;
 //                          TMA Q gather (boxes of consecutive routed positions, see
 //                          q_tile_boxes) and the K/V tile ring (5 entries of 128
 //                          keys x 128 dims, one TMA box each, K and V alternating);
@@ -495,9 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1) switch_prefill_kernel(const __gri
 
   if (warp == 0) {
     // ------------------------------------------------------------------ scheduler + producer
-    // Lane 0 takes work items from the global counter (one unit ahead), every lane
-    // decodes the same item, the unit is published through the ring for the MMA and
-    // softmax warps, and the warp then issues the unit's TMA loads.
+    // Lane 0 takes work items from the global counter, every lane decodes the same
+    // item, the unit is published through the ring for the MMA and softmax warps,
+    // and the warp then issues the unit's TMA loads.
     int maxnpb0 = 0, maxnpb1 = 0;
     for (int b = 0; b < p.B; ++b) {
       maxnpb0 = max(maxnpb0, (min(branch_count(p, 0, b), p.idx_cap[0]) + p.pc - 1) / p.pc);
