@@ -331,6 +331,13 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     validate_qkv(q, k, v)
     if window_size <= 0:
         raise ValueError("window_size must be positive")
+    host_counts = None
+    if max_counts is not None:
+        if len(max_counts) != 2 or int(max_counts[0]) < 0 or int(max_counts[1]) < 0:
+            raise ValueError("max_counts must be a pair of non-negative counts (n_full, n_local)")
+        host_counts = (int(max_counts[0]), int(max_counts[1]))
+    if key_split not in (None, False, "auto") and (isinstance(key_split, (str, bool)) or int(key_split) < 0):
+        raise ValueError("key_split must be 'auto', None or a non-negative number of key tiles")
     B, q_len, Hq, D = q.shape
     kv_len, Hkv = k.shape[1], k.shape[2]
     dev = q.device
@@ -364,7 +371,6 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
     counts = ws[4:]
     gate = None
     counts_arg, batch_major = None, 0
-    host_counts = None if max_counts is None else (int(max_counts[0]), int(max_counts[1]))
     with torch.cuda.device(dev):
         if not padded:
             # the reference's form: B == 1, every entry of each list is a routed row
@@ -413,8 +419,6 @@ def forward(q, k, v, full_query_indices, local_query_indices, *, metadata=None, 
         split_tiles, scratch, scratch_bytes = 0, None, 0
         if key_split:
             request = 0 if key_split == "auto" else int(key_split)
-            if request < 0:
-                raise ValueError("key_split must be 'auto', None or a non-negative number of key tiles")
             cf, cl = host_counts if host_counts is not None else (n_full, n_local)
             split_tiles, scratch_bytes = split_plan(B, kv_len, Hq, Hkv, min(cf, n_full), min(cl, n_local), window_size,
                                                     dev, n_bg=n_bg, request_tiles=request)

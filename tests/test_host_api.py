@@ -241,3 +241,17 @@ def test_key_split_plan():
     assert _plan(lib, 2, 1000, 8, 2, 0, 1000, 0, 64, request=2) == (0, 0)
     # bad shapes plan nothing
     assert _plan(lib, 0, 1000, 8, 2, 300, 700, 0, 64, request=2) == (0, 0)
+
+
+def test_key_split_arguments_validated():
+    S = 64
+    q = dev(torch.zeros(1, S, 8, 128, dtype=torch.bfloat16))
+    k = dev(torch.zeros(1, S, 2, 128, dtype=torch.bfloat16))
+    pos = torch.arange(S, dtype=torch.int32)
+    with CpuFactories():
+        for bad in ("always", -1, True):
+            got = _err(lambda: _core.forward(q, k, k, dev(pos[:10]), dev(pos[10:]), window_size=16, key_split=bad))
+            assert got["type"] == "ValueError" and "key_split" in got["message"], (bad, got)
+        for bad in ((1,), (-1, 5), (1, 2, 3)):
+            got = _err(lambda: _core.forward(q, k, k, dev(pos[:10]), dev(pos[10:]), window_size=16, max_counts=bad))
+            assert got["type"] == "ValueError" and "max_counts" in got["message"], (bad, got)
